@@ -1,0 +1,477 @@
+"""Benchmark of the B200 INT8 KV-cache decode path.
+
+Default workload: one full decode step over the model's
+8 full-attention layers for 128 sequences at 32768 cached tokens each
+(16 Q / 4 KV heads, head_dim 128).  Per layer a step appends one token per
+sequence (quantize-on-append) and then runs split-K decode attention.  The
+128 sequences are sharded by sequence across ranks with no collective.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 3|1|2|4]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference     # the reference's CPU code on the host
+
+Config 4 (one 1,048,576-token sequence split along context) runs a partial
+(m, l, O) per rank and merges them with an NCCL all-gather plus the
+log-sum-exp combine kernel.
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "echo-core_b200"))
+
+import workloads as W  # noqa: E402
+
+METRIC = "INT8-KV decode attention HBM GB/s (% of peak) and decode tok/s at 32k ctx"
+D = 128
+HKV = 4
+H = 16
+BYTES_PER_TOKEN = W.kv_bytes_per_token(HKV, D)  # 1056: K+V codes + K/V scales, per layer
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """dram bytes per decode launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ CPU legs
+def cpu_decode_units(n_units, ctx, threads, use_ref):
+    """Times n_units single-sequence decode steps at `ctx` on the host.
+    use_ref: the reference's own InferenceEngine::attention (oracle/_ref);
+    else the C restatement (oracle/liboracle.so), single-threaded."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    rng = np.random.default_rng(2)
+    kq, ks = O.quantize_kv(W.kv_rows(rng, ctx, HKV, D), HKV, D)
+    vq, vs = O.quantize_kv(W.kv_rows(rng, ctx, HKV, D), HKV, D)
+    q = W.queries(rng, 1, H, D)[0]
+    if not use_ref:
+        t0 = time.perf_counter()
+        for _ in range(n_units):
+            O.decode_attention(kq, vq, ks, vs, ctx, q, H, HKV, D, W.softmax_scale(D))
+        return time.perf_counter() - t0
+    from concurrent.futures import ThreadPoolExecutor
+    engines = [O.RefAttention(H, HKV, D, ctx + 1) for _ in range(threads)]
+    for e in engines:  # warm: first call copies the cache in and touches the weights
+        e.run(kq, vq, ks, vs, ctx, q)
+
+    def work(i):
+        e = engines[i]
+        for _ in range(n_units // threads + (1 if i < n_units % threads else 0)):
+            e.run(kq, vq, ks, vs, ctx, q)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(work, range(threads)))
+    dt = time.perf_counter() - t0
+    for e in engines:
+        e.close()
+    return dt
+
+
+def cpu_baseline_line(ctx=32768, units=None):
+    units = units or int(os.environ.get("EC_CPU_UNITS", "96"))
+    dt = cpu_decode_units(units, ctx, 1, use_ref=False)
+    gbs = units * ctx * BYTES_PER_TOKEN / dt / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{units} single-sequence decode steps (one layer) at ctx {ctx}, "
+                      f"16 Q / 4 KV heads, d 128; {dt:.1f} s on 1 host core"}
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = os.cpu_count() or 1
+    ctx = 32768
+    use_ref = O.ref_available()
+    kind = "reference" if use_ref else "port"
+    per_step_units = int(os.environ.get("EC_REF_UNITS", str(max(threads, 8))))
+    for _ in range(args.warmup):
+        cpu_decode_units(threads, ctx, threads, use_ref)
+    times = []
+    for _ in range(args.steps):
+        times.append(cpu_decode_units(per_step_units, ctx, threads, use_ref))
+    dt = sum(times)
+    gbs = args.steps * per_step_units * ctx * BYTES_PER_TOKEN / dt / 1e9
+    ms = dt / args.steps * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "cfg3_decode_8layers_128x32k", "sample_units_per_step": per_step_units,
+                   "ctx": ctx, "q_heads": H, "kv_heads": HKV, "head_dim": D},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"{per_step_units} (sequence, layer) decode steps of config 3 "
+                                   f"per step, {threads} host threads, "
+                                   + ("reference InferenceEngine::attention (oracle/_ref)"
+                                      if use_ref else "C restatement (oracle)")},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+def fill_layer(torch, eckv, bc, lens, gen, chunk_tokens=1 << 20):
+    """Fills a BatchCache's slabs with quantized N(0,1)+outlier K/V (setup)."""
+    stream = torch.cuda.current_stream()
+    for s, L in enumerate(lens):
+        off = int(bc.offsets_host[s])
+        done = 0
+        while done < L:
+            n = min(chunk_tokens, L - done)
+            for dst_codes, dst_scales in ((bc.keys, bc.key_scales), (bc.values, bc.val_scales)):
+                x = torch.randn((n, HKV, D), generator=gen, device="cuda", dtype=torch.float32)
+                x[:, :, list(W.OUTLIER_CHANNELS)] *= W.OUTLIER_FACTOR
+                slot = off + done
+                codes = dst_codes[slot:slot + n]
+                scales = dst_scales[slot * HKV:(slot + n) * HKV]
+                eckv.quantize_per_token_symmetric(x, codes, scales, n * HKV, D, stream)
+            done += n
+    bc.length.copy_(torch.tensor(lens, dtype=torch.int32, device="cuda"))
+
+
+def run_gpu_arm(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import eckv
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfgn = args.config
+    cfg = W.config(cfgn)
+    if cfgn == 4:
+        return run_cp_arm(args, rank, world, local_rank)
+    # ---- shard sequences
+    nseq_total = cfg.num_seqs
+    lo = rank * nseq_total // world
+    hi = (rank + 1) * nseq_total // world
+    lens0 = cfg.ctx[lo:hi]
+    nseq = hi - lo
+    layers = cfg.num_layers
+    new_tok = 1
+    cap_extra = (args.warmup + args.steps + 1) * new_tok + 1
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(cfg.seed * 1000 + rank)
+    caches = []
+    for _ in range(layers):
+        bc = eckv.BatchCache([L + cap_extra for L in lens0], num_kv_heads=HKV, device=dev,
+                             max_seq_len=max(lens0) + cap_extra)
+        fill_layer(torch, eckv, bc, lens0, gen)
+        caches.append(bc)
+    q = torch.randn((layers, nseq, H, D), generator=gen, device=dev)
+    kn = torch.randn((layers, nseq, HKV * D), generator=gen, device=dev)
+    vn = torch.randn((layers, nseq, HKV * D), generator=gen, device=dev)
+    out = torch.empty((layers, nseq, H, D), device=dev)
+    for bc in caches:
+        bc.workspace(H)
+    torch.cuda.synchronize()
+    scale = W.softmax_scale(D)
+    stream = torch.cuda.current_stream()
+    plan_chunks = eckv.lib().ec_decode_workspace_size(nseq, H, D, caches[0].max_seq_len)
+    launches_per_layer = 2 + 1 + (1 if plan_chunks > 0 else 0)  # append+bump, decode, combine
+
+    def step(ev=None):
+        for l, bc in enumerate(caches):
+            bc.append(kn[l], vn[l], 1, stream)
+            if ev is not None:
+                ev[l][0].record(stream)
+            bc.decode(q[l], out[l], H, scale, stream)
+            if ev is not None:
+                ev[l][1].record(stream)
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    sync_all()
+    for bc in caches:
+        assert bc.device_error() == 0
+    # bytes of the timed steps: per layer, every cached token after the append
+    lens_t = np.asarray(lens0, dtype=np.int64)
+    bytes_steps = 0
+    for k in range(args.steps):
+        cur = lens_t + (args.warmup + k + 1) * new_tok
+        bytes_steps += layers * int(cur.sum()) * BYTES_PER_TOKEN
+    qo_bytes = 2 * nseq * H * D * 4
+    dec_events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(layers)]
+                  for _ in range(args.steps)]
+    clocks = ClockSampler(local_rank) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    sync_all()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(args.steps):
+        step(dec_events[k])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    ms = t_start.elapsed_time(t_end)
+    clk = clocks.stop() if clocks else None
+    dec_ms = [dec_events[k][l][0].elapsed_time(dec_events[k][l][1])
+              for k in range(args.steps) for l in range(layers)]
+    for bc in caches:
+        assert bc.device_error() == 0
+    # max over ranks
+    t = torch.tensor([ms, float(bytes_steps), float(np.mean(dec_ms))], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = t.clone()
+        dist.all_reduce(tmax[:1], op=dist.ReduceOp.MAX)
+        tsum = t.clone()
+        dist.all_reduce(tsum[1:2], op=dist.ReduceOp.SUM)
+        ms_max, total_bytes = float(tmax[0]), float(tsum[1])
+    else:
+        ms_max, total_bytes = ms, float(bytes_steps)
+
+    # ---- e2e: same step through the C ABI from pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        q_h = torch.empty((layers, nseq, H, D), pin_memory=True)
+        kn_h = torch.empty((layers, nseq, HKV * D), pin_memory=True)
+        vn_h = torch.empty((layers, nseq, HKV * D), pin_memory=True)
+        out_h = torch.empty((layers, nseq, H, D), pin_memory=True)
+        q_h.copy_(q.cpu()); kn_h.copy_(kn.cpu()); vn_h.copy_(vn.cpu())
+        # roll lengths back so the e2e run sees the same contexts
+        for bc in caches:
+            bc.length.sub_(args.steps * new_tok)
+        sync_all()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(args.steps):
+            for l, bc in enumerate(caches):
+                q[l].copy_(q_h[l], non_blocking=True)
+                kn[l].copy_(kn_h[l], non_blocking=True)
+                vn[l].copy_(vn_h[l], non_blocking=True)
+                bc.append(kn[l], vn[l], 1, stream)
+                bc.decode(q[l], out[l], H, scale, stream)
+                out_h[l].copy_(out[l], non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
+        te = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        h2d = (q_h.numel() + kn_h.numel() + vn_h.numel()) * 4
+        d2h = out_h.numel() * 4
+        if world > 1:
+            hb = torch.tensor([float(h2d), float(d2h)], dtype=torch.float64, device=dev)
+            dist.all_reduce(hb, op=dist.ReduceOp.SUM)
+            h2d, d2h = int(hb[0]), int(hb[1])
+        e2e = {"value": round(total_bytes / (float(te[0]) * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(float(te[0]) / args.steps, 4),
+               "tok_s": round(nseq_total * args.steps / (float(te[0]) * 1e-3), 1),
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    if rank != 0:
+        return
+    peak, peak_kind = peaks()
+    gbs = total_bytes / (ms_max * 1e-3) / 1e9
+    # roofline of the dominant kernel (decode, incl. its combine) on this rank
+    dec_avg_ms = float(np.mean(dec_ms))
+    lens_mid = lens_t + (args.warmup + 1) * new_tok
+    alg_bytes = int(lens_mid.sum()) * BYTES_PER_TOKEN + qo_bytes
+    achieved = alg_bytes / (dec_avg_ms * 1e-3) / 1e9
+    tr = committed_traffic()
+    line = {
+        "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: N(0,1) K/V with 4 outlier channels x8 per KV head, N(0,1) Q; "
+                "quantized on device",
+        "config": {"workload": cfg.name, "layers": layers, "seqs": nseq_total, "ctx": lens0[0],
+                   "q_heads": H, "kv_heads": HKV, "head_dim": D,
+                   "parallelism": f"sequence-shard x{world} (no collective)",
+                   "l2": "inputs larger than L2 (KV working set per step >> 126 MB)"},
+        "tok_s": round(nseq_total * args.steps / (ms_max * 1e-3), 1),
+        "pct_of_hbm_peak": round(100 * gbs / (peak * world), 1),
+        "roofline": {"bound": "hbm", "kernel": "decode_kernel+combine_kernel",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "alg_bytes_per_launch": alg_bytes,
+                     "traffic": (tr or {}).get("bytes_per_launch")},
+        "gpu_launches": launches_per_layer * layers * args.steps,
+        "clocks": clk,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_line()
+    print(json.dumps(line), flush=True)
+
+
+def run_cp_arm(args, rank, world, local_rank):
+    """Config 4: 1,048,576-token sequence split contiguously across ranks;
+    per-rank partial state, NCCL all-gather, log-sum-exp combine."""
+    import torch
+    import torch.distributed as dist
+    import eckv
+    dev = torch.device("cuda", local_rank)
+    cfg = W.config(4)
+    total = cfg.ctx[0]
+    lo = rank * total // world
+    hi = (rank + 1) * total // world
+    n = hi - lo
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(cfg.seed * 1000 + rank)
+    bc = eckv.BatchCache([n], num_kv_heads=HKV, device=dev)
+    fill_layer(torch, eckv, bc, [n], gen)
+    q = torch.randn((1, H, D), generator=gen, device=dev)
+    qg = q.clone()
+    if world > 1:
+        dist.broadcast(qg, 0)
+    po = torch.empty((world, 1, H, D), device=dev)
+    pml = torch.empty((world, 1, H, 2), device=dev)
+    out = torch.empty((1, H, D), device=dev)
+    scale = W.softmax_scale(D)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        bc.decode_partial(qg, po[rank], pml[rank], H, scale, stream)
+        if world > 1:
+            dist.all_gather_into_tensor(po, po[rank].contiguous())
+            dist.all_gather_into_tensor(pml, pml[rank].contiguous())
+        eckv.lse_combine(po, pml, world, 1, H, D, out, stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        peak, kind = peaks()
+        gbs = total * BYTES_PER_TOKEN * args.steps / (float(t[0]) * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(float(t[0]) / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": cfg.name, "ctx": total, "parallelism": f"context-split x{world}"},
+            "pct_of_hbm_peak": round(100 * gbs / (peak * world), 1)}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank)
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_gpu_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

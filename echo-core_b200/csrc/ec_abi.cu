@@ -1,0 +1,434 @@
+// ec_abi.cu -- host side of the C ABI declared in include/ec_kv.h.
+//
+// Validates arguments, translates the reference's object model (KVCache,
+// KVCacheLayer, ModelConfig) onto device memory, picks the split plan and
+// launches the kernels.  No exception crosses the ABI; every failure returns
+// an ec_status and records a one-line reason for ec_last_error().
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "ec_common.cuh"
+#include "ec_internal.h"
+#include "ec_kv.h"
+
+namespace {
+
+thread_local char g_last_error[256] = "";
+
+int fail(int status, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(EC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int num_sms_current() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms > 0 ? sms : 148;
+}
+
+bool decode_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim) {
+    if (head_dim != 128) return false;
+    if (num_kv_heads != 4 && num_kv_heads != 8) return false;
+    if (num_heads == 0 || num_heads % num_kv_heads) return false;
+    const uint32_t g = num_heads / num_kv_heads;
+    return g == 1 || g == 2 || g == 4;
+}
+
+cudaStream_t as_stream(ec_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+struct ec_kv_cache {
+    ec_model_config cfg;
+    int scale_mode;
+    int device;
+    void* slab;
+    size_t slab_bytes;
+    std::vector<ec_kv_layer> layers;
+    void* ws;
+    size_t ws_bytes;
+    ec::DecodePlan plan;
+};
+
+extern "C" {
+
+int ec_abi_version(void) { return EC_KV_ABI_VERSION; }
+
+const char* ec_status_string(int status) {
+    switch (status) {
+        case EC_OK: return "ok";
+        case EC_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case EC_ERR_MISALIGNED: return "device pointer not 16-byte aligned";
+        case EC_ERR_CAPACITY: return "cache capacity exceeded";
+        case EC_ERR_UNSUPPORTED: return "shape outside the supported envelope";
+        case EC_ERR_CUDA: return "CUDA error";
+        case EC_ERR_WORKSPACE: return "workspace missing or too small";
+        case EC_ERR_DEVICE_CHECK: return "a kernel flagged bad input";
+        default: return "unknown status";
+    }
+}
+
+const char* ec_last_error(void) { return g_last_error; }
+
+int ec_device_error(int32_t* err_word, ec_stream_t stream, int32_t* code) {
+    if (!code) return fail(EC_ERR_INVALID_ARGUMENT, "ec_device_error: code is NULL");
+    cudaStream_t st = as_stream(stream);
+    int32_t zero = 0, host = 0;
+    cudaError_t e;
+    if (err_word) {
+        e = cudaMemcpyAsync(&host, err_word, sizeof(host), cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(err_word, &zero, sizeof(zero), cudaMemcpyHostToDevice, st);
+    } else {
+        e = cudaMemcpyFromSymbolAsync(&host, ec::g_error_word, sizeof(host), 0, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(ec::g_error_word, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "ec_device_error");
+    *code = host;
+    return EC_OK;
+}
+
+int ec_quantize_per_token_symmetric(const float* input, int8_t* output, float* scales,
+                                    uint32_t num_tokens, uint32_t num_elements,
+                                    ec_stream_t stream) {
+    if (num_tokens == 0) return EC_OK;
+    if (!input || !output || !scales || num_elements == 0)
+        return fail(EC_ERR_INVALID_ARGUMENT, "quantize: null pointer or num_elements == 0");
+    cudaError_t e = ec::launch_quantize_rows(input, output, scales, num_tokens, num_elements,
+                                             as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "quantize launch");
+}
+
+int ec_fused_dequant_dot_int8(const float* query, const int8_t* key_cache, const float* scales,
+                              float* scores, uint32_t dim, uint32_t seq_len, ec_stream_t stream) {
+    if (seq_len == 0) return EC_OK;
+    if (!query || !key_cache || !scales || !scores || dim == 0)
+        return fail(EC_ERR_INVALID_ARGUMENT, "fused_dequant_dot: null pointer or dim == 0");
+    cudaError_t e = ec::launch_fused_dequant_dot(query, key_cache, scales, scores, dim, seq_len,
+                                                 as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "fused_dequant_dot launch");
+}
+
+// ---------------------------------------------------------------- KVCache
+int ec_kv_cache_create(const ec_model_config* config, int scale_mode, ec_kv_cache** out) {
+    if (!config || !out) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_create: null argument");
+    *out = nullptr;
+    if (scale_mode != EC_SCALE_PER_HEAD && scale_mode != EC_SCALE_ROW)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_create: bad scale_mode %d", scale_mode);
+    const ec_model_config& c = *config;
+    if (c.num_kv_heads == 0 || c.head_dim == 0)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_create: num_kv_heads and head_dim must be > 0");
+    if ((uint64_t)c.max_seq_len > 0x7fffffffull)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_create: max_seq_len too large");
+    ec_kv_cache* kc = new (std::nothrow) ec_kv_cache();
+    if (!kc) return fail(EC_ERR_CUDA, "kv_cache_create: host allocation failed");
+    kc->cfg = c;
+    kc->scale_mode = scale_mode;
+    kc->slab = nullptr;
+    kc->ws = nullptr;
+    kc->ws_bytes = 0;
+    kc->plan = ec::DecodePlan{32, 1};
+    cudaGetDevice(&kc->device);
+    kc->layers.assign(c.num_layers, ec_kv_layer{});
+
+    // Same partition as src/kv_cache.cpp:24-71; every sub-buffer is rounded
+    // up to 256 B so the kernels' 16-byte vector and bulk accesses stay aligned.
+    auto r256 = [](size_t b) { return (b + 255) & ~size_t(255); };
+    const size_t row = (size_t)c.num_kv_heads * c.head_dim;
+    const size_t max_seq = c.max_seq_len;
+    size_t per_layer;
+    if (c.use_kv_quantization) {
+        per_layer = 2 * r256(max_seq * row) + 2 * r256(max_seq * c.num_kv_heads * sizeof(float));
+    } else {
+        per_layer = 2 * r256(max_seq * row * sizeof(float));
+    }
+    kc->slab_bytes = per_layer * c.num_layers;
+    if (kc->slab_bytes) {
+        cudaError_t e = cudaMalloc(&kc->slab, kc->slab_bytes);
+        if (e == cudaSuccess) e = cudaMemset(kc->slab, 0, kc->slab_bytes);
+        if (e != cudaSuccess) {
+            cudaFree(kc->slab);
+            delete kc;
+            return cuda_fail(e, "kv_cache_create: device slab");
+        }
+        uint8_t* p = static_cast<uint8_t*>(kc->slab);
+        for (uint32_t l = 0; l < c.num_layers; ++l) {
+            ec_kv_layer& L = kc->layers[l];
+            if (c.use_kv_quantization) {
+                L.keys_int8 = reinterpret_cast<int8_t*>(p); p += r256(max_seq * row);
+                L.values_int8 = reinterpret_cast<int8_t*>(p); p += r256(max_seq * row);
+                L.key_scales = reinterpret_cast<float*>(p); p += r256(max_seq * c.num_kv_heads * 4);
+                L.val_scales = reinterpret_cast<float*>(p); p += r256(max_seq * c.num_kv_heads * 4);
+            } else {
+                L.keys_fp32 = reinterpret_cast<float*>(p); p += r256(max_seq * row * 4);
+                L.values_fp32 = reinterpret_cast<float*>(p); p += r256(max_seq * row * 4);
+            }
+        }
+    }
+    if (c.use_kv_quantization && c.num_layers > 0 &&
+        decode_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim)) {
+        kc->plan = ec::plan_decode(1, (int)c.max_seq_len, num_sms_current());
+        kc->ws_bytes = ec::decode_workspace_bytes(kc->plan, 1, (int)c.num_heads);
+        if (kc->ws_bytes) {
+            cudaError_t e = cudaMalloc(&kc->ws, kc->ws_bytes);
+            if (e != cudaSuccess) {
+                cudaFree(kc->slab);
+                delete kc;
+                return cuda_fail(e, "kv_cache_create: decode workspace");
+            }
+        }
+    }
+    *out = kc;
+    return EC_OK;
+}
+
+void ec_kv_cache_destroy(ec_kv_cache* cache) {
+    if (!cache) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(cache->device);
+    cudaDeviceSynchronize();
+    cudaFree(cache->slab);
+    cudaFree(cache->ws);
+    cudaSetDevice(prev);
+    delete cache;
+}
+
+int ec_kv_cache_layer(const ec_kv_cache* cache, uint32_t layer_idx, ec_kv_layer* out) {
+    if (!cache || !out) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_layer: null argument");
+    if (layer_idx >= cache->cfg.num_layers)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_layer: layer %u >= num_layers %u", layer_idx,
+                    cache->cfg.num_layers);
+    *out = cache->layers[layer_idx];
+    return EC_OK;
+}
+
+int ec_kv_cache_append(ec_kv_cache* cache, uint32_t layer_idx, const float* k_proj,
+                       const float* v_proj, ec_stream_t stream) {
+    if (!cache || !k_proj || !v_proj) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_append: null argument");
+    if (layer_idx >= cache->cfg.num_layers)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_append: layer %u out of range", layer_idx);
+    ec_kv_layer& L = cache->layers[layer_idx];
+    const ec_model_config& c = cache->cfg;
+    if (L.seq_len >= c.max_seq_len)
+        return fail(EC_ERR_CAPACITY, "kv_cache_append: layer %u is full (%u tokens)", layer_idx,
+                    c.max_seq_len);
+    const size_t row = (size_t)c.num_kv_heads * c.head_dim;
+    const size_t pos = L.seq_len;
+    cudaStream_t st = as_stream(stream);
+    cudaError_t e;
+    if (!c.use_kv_quantization) {
+        e = cudaMemcpyAsync(L.keys_fp32 + pos * row, k_proj, row * 4, cudaMemcpyDeviceToDevice, st);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(L.values_fp32 + pos * row, v_proj, row * 4, cudaMemcpyDeviceToDevice, st);
+    } else if (c.head_dim == 128 && aligned16(k_proj) && aligned16(v_proj) &&
+               (c.num_kv_heads == 1 || c.num_kv_heads == 2 || c.num_kv_heads == 4 || c.num_kv_heads == 8)) {
+        ec::AppendArgs a{};
+        a.k = k_proj;
+        a.v = v_proj;
+        a.keys = L.keys_int8;
+        a.values = L.values_int8;
+        a.key_scales = L.key_scales;
+        a.val_scales = L.val_scales;
+        a.host_offset = 0;
+        a.host_capacity = (int32_t)c.max_seq_len;
+        a.host_length = (int32_t)pos;
+        a.err = nullptr;
+        a.total_slots = c.max_seq_len;
+        a.num_seqs = 1;
+        a.n_new = 1;
+        e = ec::launch_append(a, (int)c.num_kv_heads, cache->scale_mode == EC_SCALE_ROW, st);
+    } else if (cache->scale_mode == EC_SCALE_ROW) {
+        e = ec::launch_quantize_rows(k_proj, L.keys_int8 + pos * row, L.key_scales + pos, 1, (uint32_t)row, st);
+        if (e == cudaSuccess)
+            e = ec::launch_quantize_rows(v_proj, L.values_int8 + pos * row, L.val_scales + pos, 1, (uint32_t)row, st);
+    } else {
+        e = ec::launch_quantize_rows(k_proj, L.keys_int8 + pos * row, L.key_scales + pos * c.num_kv_heads,
+                                     c.num_kv_heads, c.head_dim, st);
+        if (e == cudaSuccess)
+            e = ec::launch_quantize_rows(v_proj, L.values_int8 + pos * row, L.val_scales + pos * c.num_kv_heads,
+                                         c.num_kv_heads, c.head_dim, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "kv_cache_append");
+    L.seq_len++;
+    return EC_OK;
+}
+
+uint32_t ec_kv_cache_seq_len(const ec_kv_cache* cache) {
+    if (!cache || cache->cfg.num_layers == 0) return 0;
+    return cache->layers[0].seq_len;
+}
+
+int ec_kv_cache_reset(ec_kv_cache* cache) {
+    if (!cache) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_reset: null cache");
+    for (auto& L : cache->layers) L.seq_len = 0;
+    return EC_OK;
+}
+
+int ec_kv_cache_attention(ec_kv_cache* cache, uint32_t layer_idx, const float* q, float* out,
+                          float softmax_scale, ec_stream_t stream) {
+    if (!cache || !q || !out) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_attention: null argument");
+    const ec_model_config& c = cache->cfg;
+    if (layer_idx >= c.num_layers) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_attention: layer out of range");
+    if (!c.use_kv_quantization)
+        return fail(EC_ERR_UNSUPPORTED, "kv_cache_attention: the fp32 cache mode has no GPU attention kernel yet");
+    if (!decode_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim))
+        return fail(EC_ERR_UNSUPPORTED, "kv_cache_attention: needs head_dim 128, num_kv_heads 4|8, group 1|2|4");
+    if (!aligned16(q) || !aligned16(out)) return fail(EC_ERR_MISALIGNED, "kv_cache_attention: q/out not 16-byte aligned");
+    const ec_kv_layer& L = cache->layers[layer_idx];
+    ec::DecodeArgs a{};
+    a.keys = L.keys_int8;
+    a.values = L.values_int8;
+    a.key_scales = L.key_scales;
+    a.val_scales = L.val_scales;
+    a.host_offset = 0;
+    a.host_capacity = (int32_t)c.max_seq_len;
+    a.host_length = (int32_t)L.seq_len;
+    a.err = nullptr;
+    a.total_slots = c.max_seq_len;
+    a.q = q;
+    a.out = out;
+    a.q_mul = softmax_scale;
+    a.num_seqs = 1;
+    a.num_heads = (int)c.num_heads;
+    a.row_scales = cache->scale_mode == EC_SCALE_ROW;
+    a.mode = ec::kOut;
+    cudaError_t e = ec::launch_decode(a, (int)c.num_kv_heads, cache->plan, cache->ws, as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_cache_attention launch");
+}
+
+// ------------------------------------------------------------ batched cache
+static int check_batch(const ec_kv_batch* b, const char* who) {
+    if (!b) return fail(EC_ERR_INVALID_ARGUMENT, "%s: batch is NULL", who);
+    if (!b->keys || !b->values || !b->key_scales || !b->val_scales || !b->seq_offset ||
+        !b->seq_capacity || !b->seq_len)
+        return fail(EC_ERR_INVALID_ARGUMENT, "%s: null buffer in batch", who);
+    if (b->scale_mode != EC_SCALE_PER_HEAD && b->scale_mode != EC_SCALE_ROW)
+        return fail(EC_ERR_INVALID_ARGUMENT, "%s: bad scale_mode", who);
+    if (!aligned16(b->keys) || !aligned16(b->values) || !aligned16(b->key_scales) ||
+        !aligned16(b->val_scales))
+        return fail(EC_ERR_MISALIGNED, "%s: cache buffers must be 16-byte aligned", who);
+    if (b->num_seqs > 65535u) return fail(EC_ERR_UNSUPPORTED, "%s: more than 65535 sequences", who);
+    if (b->max_seq_len > 0x7fffffffu) return fail(EC_ERR_INVALID_ARGUMENT, "%s: max_seq_len too large", who);
+    return EC_OK;
+}
+
+int ec_kv_batch_append(const ec_kv_batch* b, const float* k, const float* v,
+                       uint32_t tokens_per_seq, ec_stream_t stream) {
+    int rc = check_batch(b, "kv_batch_append");
+    if (rc) return rc;
+    if (tokens_per_seq == 0 || b->num_seqs == 0) return EC_OK;
+    if (!k || !v) return fail(EC_ERR_INVALID_ARGUMENT, "kv_batch_append: k/v NULL");
+    if (b->head_dim != 128 || !(b->num_kv_heads == 1 || b->num_kv_heads == 2 || b->num_kv_heads == 4 ||
+                                b->num_kv_heads == 8))
+        return fail(EC_ERR_UNSUPPORTED, "kv_batch_append: needs head_dim 128 and num_kv_heads 1|2|4|8");
+    if (!aligned16(k) || !aligned16(v)) return fail(EC_ERR_MISALIGNED, "kv_batch_append: k/v not 16-byte aligned");
+    if ((uint64_t)b->num_seqs * tokens_per_seq > 0x7fffffffull)
+        return fail(EC_ERR_UNSUPPORTED, "kv_batch_append: too many tokens in one call");
+    ec::AppendArgs a{};
+    a.k = k;
+    a.v = v;
+    a.keys = b->keys;
+    a.values = b->values;
+    a.key_scales = b->key_scales;
+    a.val_scales = b->val_scales;
+    a.seq_offset = b->seq_offset;
+    a.seq_capacity = b->seq_capacity;
+    a.seq_len = b->seq_len;
+    a.err = b->error_word;
+    a.total_slots = b->total_slots;
+    a.num_seqs = (int)b->num_seqs;
+    a.n_new = (int)tokens_per_seq;
+    cudaError_t e = ec::launch_append(a, (int)b->num_kv_heads, b->scale_mode == EC_SCALE_ROW,
+                                      as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_batch_append launch");
+}
+
+size_t ec_decode_workspace_size(uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim,
+                                uint32_t max_seq_len) {
+    (void)head_dim;
+    ec::DecodePlan p = ec::plan_decode((int)num_seqs, (int)max_seq_len, num_sms_current());
+    return ec::decode_workspace_bytes(p, (int)num_seqs, (int)num_heads);
+}
+
+static int decode_common(const ec_kv_batch* b, const float* q, float* out, float* out_ml,
+                         uint32_t num_heads, float softmax_scale, void* ws, size_t ws_bytes,
+                         int mode, ec_stream_t stream, const char* who) {
+    int rc = check_batch(b, who);
+    if (rc) return rc;
+    if (b->num_seqs == 0) return EC_OK;
+    if (!q || !out || (mode == ec::kPartial && !out_ml))
+        return fail(EC_ERR_INVALID_ARGUMENT, "%s: q/out NULL", who);
+    if (!decode_shape_supported(num_heads, b->num_kv_heads, b->head_dim))
+        return fail(EC_ERR_UNSUPPORTED, "%s: needs head_dim 128, num_kv_heads 4|8, num_heads/num_kv_heads 1|2|4", who);
+    if (!aligned16(q) || !aligned16(out)) return fail(EC_ERR_MISALIGNED, "%s: q/out not 16-byte aligned", who);
+    ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, num_sms_current());
+    const size_t need = ec::decode_workspace_bytes(plan, (int)b->num_seqs, (int)num_heads);
+    if (need > 0 && (!ws || ws_bytes < need))
+        return fail(EC_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", who, need, ws_bytes);
+    if (need > 0 && !aligned16(ws)) return fail(EC_ERR_MISALIGNED, "%s: workspace not 16-byte aligned", who);
+    ec::DecodeArgs a{};
+    a.keys = b->keys;
+    a.values = b->values;
+    a.key_scales = b->key_scales;
+    a.val_scales = b->val_scales;
+    a.seq_offset = b->seq_offset;
+    a.seq_capacity = b->seq_capacity;
+    a.seq_len = b->seq_len;
+    a.err = b->error_word;
+    a.total_slots = b->total_slots;
+    a.q = q;
+    a.out = out;
+    a.out_ml = out_ml;
+    a.q_mul = softmax_scale;
+    a.num_seqs = (int)b->num_seqs;
+    a.num_heads = (int)num_heads;
+    a.row_scales = b->scale_mode == EC_SCALE_ROW;
+    a.mode = mode;
+    cudaError_t e = ec::launch_decode(a, (int)b->num_kv_heads, plan, ws, as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, who);
+}
+
+int ec_decode_attention(const ec_kv_batch* b, const float* q, float* out, uint32_t num_heads,
+                        float softmax_scale, void* workspace, size_t workspace_bytes,
+                        ec_stream_t stream) {
+    return decode_common(b, q, out, nullptr, num_heads, softmax_scale, workspace, workspace_bytes,
+                         ec::kOut, stream, "decode_attention");
+}
+
+int ec_decode_attention_partial(const ec_kv_batch* b, const float* q, float* part_o,
+                                float* part_ml, uint32_t num_heads, float softmax_scale,
+                                void* workspace, size_t workspace_bytes, ec_stream_t stream) {
+    return decode_common(b, q, part_o, part_ml, num_heads, softmax_scale, workspace,
+                         workspace_bytes, ec::kPartial, stream, "decode_attention_partial");
+}
+
+int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t num_parts,
+                   uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim, float* out,
+                   ec_stream_t stream) {
+    if (!part_o || !part_ml || !out) return fail(EC_ERR_INVALID_ARGUMENT, "lse_combine: null argument");
+    if (head_dim != 128) return fail(EC_ERR_UNSUPPORTED, "lse_combine: head_dim must be 128");
+    if (num_parts == 0 || num_seqs == 0 || num_heads == 0) return EC_OK;
+    if (num_seqs > 0x7fffffffu || num_heads > 65535u)
+        return fail(EC_ERR_UNSUPPORTED, "lse_combine: grid too large");
+    cudaError_t e = ec::launch_lse_combine(part_o, part_ml, (int)num_parts, (int)num_seqs,
+                                           (int)num_heads, out, as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "lse_combine launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,73 @@
+// ec_internal.h -- launch arguments and launchers shared by the .cu files.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ec {
+
+struct AppendArgs {
+    const float* k;
+    const float* v;
+    int8_t* keys;
+    int8_t* values;
+    float* key_scales;
+    float* val_scales;
+    const int32_t* seq_offset;    // null: host_offset for every sequence
+    const int32_t* seq_capacity;  // null: host_capacity
+    int32_t* seq_len;             // null: host_length, and no length update
+    int32_t host_offset, host_capacity, host_length;
+    int32_t* err;
+    uint64_t total_slots;
+    int num_seqs;
+    int n_new;
+};
+
+struct DecodeArgs {
+    const int8_t* keys;
+    const int8_t* values;
+    const float* key_scales;
+    const float* val_scales;
+    const int32_t* seq_offset;
+    const int32_t* seq_capacity;
+    const int32_t* seq_len;
+    int32_t host_offset, host_capacity, host_length;
+    int32_t* err;
+    uint64_t total_slots;
+    const float* q;       // [num_seqs][num_heads][128]
+    float* out;           // final output (normalised) when mode == kOut
+    float* out_ml;        // (m, l) per (seq, head) when mode == kPartial
+    float* part_o;        // [num_seqs*max_chunks][num_heads][128]
+    float* part_ml;       // [num_seqs*max_chunks][num_heads][2]
+    float q_mul;          // softmax scale (applied to q first, as the reference does)
+    int num_seqs;
+    int num_heads;
+    int max_chunks;
+    int chunk_tokens;
+    int row_scales;       // 1: EC_SCALE_ROW
+    int mode;             // kOut or kPartial
+};
+
+enum { kOut = 0, kPartial = 1 };
+
+cudaError_t launch_quantize_rows(const float* in, int8_t* out, float* scales, uint32_t rows,
+                                 uint32_t n, cudaStream_t st);
+cudaError_t launch_append(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st);
+cudaError_t launch_fused_dequant_dot(const float* q, const int8_t* k, const float* s, float* out,
+                                     uint32_t dim, uint32_t seq_len, cudaStream_t st);
+
+// Split policy shared by the workspace query and the launch.
+struct DecodePlan {
+    int chunk_tokens;
+    int max_chunks;
+};
+DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms);
+size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads);
+// Returns cudaErrorInvalidValue for a shape outside the envelope.
+cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan, void* ws,
+                          cudaStream_t st);
+cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
+                               int num_seqs, int num_heads, float* out, cudaStream_t st);
+
+}  // namespace ec

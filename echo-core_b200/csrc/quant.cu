@@ -1,0 +1,229 @@
+// quant.cu -- quantize-on-append kernels (sm_100a).
+//
+// Rounding contract, bit-exact with quantize_per_token_symmetric
+// (src/kernels/quant.cpp:18-98) for finite input:
+//   amax  = max |x| over the row                       (:29-60)
+//   scale = amax / 127.0f, or 1.0f when amax == 0       (:63)  -- IEEE division
+//   body  (first n - n%8 elements):  q = sat8(RNE(x * (1.0f/scale)))   (:70-88)
+//   tail  (last n%8 elements):       q = clamp127(round_half_away(x / scale)) (:91-96)
+// Every operation uses an explicitly IEEE-rounded intrinsic; this file must
+// not be compiled with fast-math.
+#include <cstdint>
+
+#include "ec_common.cuh"
+#include "ec_internal.h"
+
+namespace ec {
+
+__device__ int32_t g_error_word = 0;
+
+__device__ __forceinline__ float warp_max(float v, unsigned width = 32) {
+    for (unsigned o = width / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o, width));
+    return v;
+}
+
+__device__ __forceinline__ float scale_of(float amax) {
+    return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+}
+
+__device__ __forceinline__ int32_t q_body(float x, float inv) {
+    int32_t v = __float2int_rn(__fmul_rn(x, inv));
+    return max(-128, min(127, v));
+}
+
+__device__ __forceinline__ int32_t q_tail(float x, float scale) {
+    int32_t v = __float2int_rz(roundf(__fdiv_rn(x, scale)));
+    return max(-127, min(127, v));
+}
+
+// ---------------------------------------------------------------- generic
+// One warp per row, any row length.  Used by ec_quantize_per_token_symmetric
+// and by the single-sequence cache when head_dim is not 128.
+__global__ void quantize_rows_kernel(const float* __restrict__ in, int8_t* __restrict__ out,
+                                     float* __restrict__ scales, uint32_t num_rows,
+                                     uint32_t n) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t warps_per_grid = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t vec_end = n - (n % 8u);
+    for (uint32_t row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < num_rows;
+         row += warps_per_grid) {
+        const float* x = in + (size_t)row * n;
+        int8_t* o = out + (size_t)row * n;
+        float amax = 0.0f;
+        for (uint32_t i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(x[i]));
+        amax = warp_max(amax);
+        const float scale = scale_of(amax);
+        const float inv = __fdiv_rn(1.0f, scale);
+        for (uint32_t i = lane; i < n; i += 32) {
+            const float v = x[i];
+            o[i] = (int8_t)(i < vec_end ? q_body(v, inv) : q_tail(v, scale));
+        }
+        if (lane == 0) scales[row] = scale;
+    }
+}
+
+// ------------------------------------------------------------ batched append
+// One warp per (sequence, new token).  head_dim is 128: lane l holds float4
+// number l of every head's 128-wide slice, so each load and each store of the
+// warp is one contiguous 512 B / 128 B run.  PER_HEAD reduces the absmax per
+// head across the warp; ROW reduces it over the whole token row.
+struct TableView {
+    const int32_t* offset;
+    const int32_t* capacity;
+    const int32_t* length;
+    int32_t host_offset, host_capacity, host_length;  // used when the pointers are null
+    uint64_t total_slots;
+
+    // Loads and checks one entry; false (and a flagged error) for a bad one.
+    __device__ __forceinline__ bool load(int s, int32_t* err, int32_t& off, int32_t& cap,
+                                         int32_t& len) const {
+        off = offset ? offset[s] : host_offset;
+        cap = capacity ? capacity[s] : host_capacity;
+        len = length ? length[s] : host_length;
+        const bool ok = off >= 0 && cap >= 0 && len >= 0 && len <= cap &&
+                        (uint64_t)off + (uint64_t)cap <= total_slots;
+        return ok;
+    }
+};
+
+template <int HKV, bool ROW>
+__global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
+    constexpr int D = 128;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int s = warp / a.n_new;
+    const int i = warp - s * a.n_new;
+    if (s >= a.num_seqs) return;
+    TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, a.host_offset, a.host_capacity,
+                 a.host_length, a.total_slots};
+    int32_t off, cap, len;
+    if (!tv.load(s, a.err, off, cap, len)) {
+        if (i == 0 && lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
+        return;
+    }
+    if ((int64_t)len + a.n_new > cap) {
+        if (i == 0 && lane == 0) flag_error(a.err, EC_DEVERR_OVERFLOW);
+        return;
+    }
+    const int64_t slot = (int64_t)off + len + i;
+    const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
+
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const float* src = (t == 0 ? a.k : a.v) + src_row;
+        int8_t* dst = (t == 0 ? a.keys : a.values) + (size_t)slot * (HKV * D);
+        float* sc = t == 0 ? a.key_scales : a.val_scales;
+        float4 x[HKV];
+#pragma unroll
+        for (int g = 0; g < HKV; ++g) x[g] = __ldcs(reinterpret_cast<const float4*>(src) + g * 32 + lane);
+        float amax[HKV];
+#pragma unroll
+        for (int g = 0; g < HKV; ++g)
+            amax[g] = fmaxf(fmaxf(fabsf(x[g].x), fabsf(x[g].y)), fmaxf(fabsf(x[g].z), fabsf(x[g].w)));
+        if (ROW) {
+            float m = amax[0];
+#pragma unroll
+            for (int g = 1; g < HKV; ++g) m = fmaxf(m, amax[g]);
+            m = warp_max(m);
+#pragma unroll
+            for (int g = 0; g < HKV; ++g) amax[g] = m;
+        } else {
+#pragma unroll
+            for (int g = 0; g < HKV; ++g) amax[g] = warp_max(amax[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < HKV; ++g) {
+            const float scale = scale_of(amax[g]);
+            const float inv = __fdiv_rn(1.0f, scale);
+            const uint32_t b0 = (uint32_t)(q_body(x[g].x, inv) & 0xff);
+            const uint32_t b1 = (uint32_t)(q_body(x[g].y, inv) & 0xff);
+            const uint32_t b2 = (uint32_t)(q_body(x[g].z, inv) & 0xff);
+            const uint32_t b3 = (uint32_t)(q_body(x[g].w, inv) & 0xff);
+            reinterpret_cast<uint32_t*>(dst + g * D)[lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+            if (lane == 0) {
+                if (ROW) {
+                    if (g == 0) sc[slot] = scale;
+                } else {
+                    sc[(size_t)slot * HKV + g] = scale;
+                }
+            }
+        }
+    }
+}
+
+__global__ void bump_lengths_kernel(AppendArgs a) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= a.num_seqs || a.seq_len == nullptr) return;
+    TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, 0, 0, 0, a.total_slots};
+    int32_t off, cap, len;
+    if (!tv.load(s, a.err, off, cap, len)) return;  // already flagged by append_kernel
+    if ((int64_t)len + a.n_new > cap) return;
+    a.seq_len[s] = len + a.n_new;
+}
+
+// ---------------------------------------------------------------- launchers
+cudaError_t launch_quantize_rows(const float* in, int8_t* out, float* scales, uint32_t rows,
+                                 uint32_t n, cudaStream_t st) {
+    if (rows == 0) return cudaSuccess;
+    const uint32_t threads = 256, warps_per_block = threads / 32;
+    uint32_t blocks = (rows + warps_per_block - 1) / warps_per_block;
+    if (blocks > 65535u * 8u) blocks = 65535u * 8u;
+    quantize_rows_kernel<<<blocks, threads, 0, st>>>(in, out, scales, rows, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_append(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st) {
+    const int64_t warps = (int64_t)a.num_seqs * a.n_new;
+    if (warps == 0) return cudaSuccess;
+    const int threads = 256;
+    const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+#define EC_APPEND_CASE(H)                                                                 \
+    case H:                                                                               \
+        if (row_mode) append_kernel<H, true><<<(unsigned)blocks, threads, 0, st>>>(a);   \
+        else append_kernel<H, false><<<(unsigned)blocks, threads, 0, st>>>(a);           \
+        break;
+    switch (num_kv_heads) {
+        EC_APPEND_CASE(1)
+        EC_APPEND_CASE(2)
+        EC_APPEND_CASE(4)
+        EC_APPEND_CASE(8)
+        default: return cudaErrorInvalidValue;
+    }
+#undef EC_APPEND_CASE
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (a.seq_len != nullptr) {
+        bump_lengths_kernel<<<(a.num_seqs + 127) / 128, 128, 0, st>>>(a);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+// ------------------------------------------------------ fused dequant dot
+// scores[pos] = sum_d query[d] * (key[pos][d] * scale[pos]); one warp per pos.
+__global__ void fused_dequant_dot_kernel(const float* __restrict__ q, const int8_t* __restrict__ k,
+                                         const float* __restrict__ s, float* __restrict__ out,
+                                         uint32_t dim, uint32_t seq_len) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t pos = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (pos >= seq_len) return;
+    const int8_t* row = k + (size_t)pos * dim;
+    const float sc = s[pos];
+    float acc = 0.0f;
+    for (uint32_t d = lane; d < dim; d += 32) acc = fmaf((float)row[d] * sc, q[d], acc);
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) out[pos] = acc;
+}
+
+cudaError_t launch_fused_dequant_dot(const float* q, const int8_t* k, const float* s, float* out,
+                                     uint32_t dim, uint32_t seq_len, cudaStream_t st) {
+    if (seq_len == 0) return cudaSuccess;
+    const uint32_t threads = 256;
+    const uint64_t blocks = ((uint64_t)seq_len * 32 + threads - 1) / threads;
+    if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
+    fused_dequant_dot_kernel<<<(unsigned)blocks, threads, 0, st>>>(q, k, s, out, dim, seq_len);
+    return cudaGetLastError();
+}
+
+}  // namespace ec

@@ -1,0 +1,230 @@
+/*
+ * ec_kv.h -- C ABI of the B200 (sm_100a) INT8 KV-cache path of echo-core.
+ *
+ * Three kernels sit behind this boundary:
+ *   1. quantize-on-append: per-token symmetric int8 with an fp32 scale,
+ *      bit-exact with the reference's quantize_per_token_symmetric;
+ *   2. split-K grouped-query decode attention over the int8 cache;
+ *   3. causal chunked-prefill attention over the same cache.
+ *
+ * Conventions
+ *   - Every pointer argument documented "device" must be device memory of the
+ *     current CUDA device.  Host pointers are accepted only where stated.
+ *   - Calls are asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream) unless documented otherwise.
+ *   - Every entry point returns an ec_status.  No exception crosses the ABI.
+ *     ec_last_error() gives a one-line reason for the last failure on the
+ *     calling thread.
+ *   - Kernels never trap.  A bad length/offset table entry, an append past a
+ *     sequence's capacity or a device-side wait that runs out of time writes
+ *     a non-zero code into the batch's error word (or the library's own word
+ *     when none is given) and skips the offending work; ec_device_error()
+ *     reads and clears it.
+ *
+ * Cache layout (identical to the reference's KVCacheLayer, include/kv_cache.h:7-18):
+ *   codes   [slot][num_kv_heads][head_dim]  int8   (keys and values separately)
+ *   scales  [slot][num_kv_heads]            fp32   (EC_SCALE_PER_HEAD)
+ *           [slot]                          fp32   (EC_SCALE_ROW)
+ */
+#ifndef EC_KV_H
+#define EC_KV_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EC_KV_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define EC_API __attribute__((visibility("default")))
+#else
+#define EC_API
+#endif
+
+typedef void* ec_stream_t; /* cudaStream_t */
+
+typedef enum ec_status {
+    EC_OK = 0,
+    EC_ERR_INVALID_ARGUMENT = 1, /* null pointer, zero or inconsistent size     */
+    EC_ERR_MISALIGNED = 2,       /* device pointer not 16-byte aligned          */
+    EC_ERR_CAPACITY = 3,         /* append past max_seq_len / capacity          */
+    EC_ERR_UNSUPPORTED = 4,      /* shape outside the kernels' envelope         */
+    EC_ERR_CUDA = 5,             /* CUDA runtime or launch failure              */
+    EC_ERR_WORKSPACE = 6,        /* workspace missing or too small              */
+    EC_ERR_DEVICE_CHECK = 7      /* a kernel flagged bad input (see above)      */
+} ec_status;
+
+/* Where a token's scales live.  PER_HEAD is what the reference's decode loop
+ * reads (src/inference.cpp:347,387) and what its scale buffer is sized for
+ * (include/kv_cache.h:11-12).  ROW reproduces KVCache::append literally
+ * (src/kv_cache.cpp:101,105): one scale over the whole token row, at [slot]. */
+typedef enum ec_scale_mode { EC_SCALE_PER_HEAD = 0, EC_SCALE_ROW = 1 } ec_scale_mode;
+
+/* Device-side error codes written into an error word. */
+enum {
+    EC_DEVERR_NONE = 0,
+    EC_DEVERR_BAD_TABLE = 1,    /* offset/length/capacity entry out of range */
+    EC_DEVERR_OVERFLOW = 2,     /* append would pass a sequence's capacity   */
+    EC_DEVERR_TIMEOUT = 3       /* a bounded device wait ran out             */
+};
+
+EC_API int ec_abi_version(void);
+EC_API const char* ec_status_string(int status);
+EC_API const char* ec_last_error(void);
+
+/* Reads (and resets to 0) the device error word `err_word` (device int32), or
+ * the library's own word for the current device when err_word is NULL.
+ * Synchronises `stream`.  Returns EC_OK and stores the code in *code. */
+EC_API int ec_device_error(int32_t* err_word, ec_stream_t stream, int32_t* code);
+
+/* ------------------------------------------------------------------------
+ * Kernel-level entry points (device pointers)
+ * ---------------------------------------------------------------------- */
+
+/* Replaces quantize_per_token_symmetric (include/kernels/quant.h:8-14,
+ * src/kernels/quant.cpp:18-98).  input [num_tokens*num_elements] fp32,
+ * output int8 and scales [num_tokens] fp32, all device.  Bit-exact with the
+ * reference for finite input, including the scalar tail for
+ * num_elements % 8 != 0. */
+EC_API int ec_quantize_per_token_symmetric(const float* input, int8_t* output, float* scales,
+                                    uint32_t num_tokens, uint32_t num_elements,
+                                    ec_stream_t stream);
+
+/* Replaces fused_dequant_dot_int8 (include/kernels/quant.h:19-26,
+ * src/kernels/quant.cpp:100-144): scores[pos] = dot(query, key_cache[pos]*scales[pos]). */
+EC_API int ec_fused_dequant_dot_int8(const float* query, const int8_t* key_cache, const float* scales,
+                              float* scores, uint32_t dim, uint32_t seq_len, ec_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Single-sequence cache object: the reference's KVCache (include/kv_cache.h:21-48)
+ * with its storage in HBM.
+ * ---------------------------------------------------------------------- */
+
+/* Field-for-field mirror of ModelConfig (include/config.h:6-24); a C++ caller
+ * may pass its ModelConfig by reinterpret_cast (the C++ wrapper in
+ * ec_kv_cache.hpp static_asserts the layout). */
+typedef struct ec_model_config {
+    uint32_t vocab_size;
+    uint32_t hidden_dim;
+    uint32_t num_heads;
+    uint32_t num_kv_heads;
+    uint32_t head_dim;
+    uint32_t num_layers;
+    uint32_t ffn_hidden_dim;
+    uint32_t max_seq_len;
+    int32_t ffn_type;
+    int32_t norm_type;
+    int32_t pos_encoding;
+    bool use_kv_quantization;
+} ec_model_config;
+
+/* Mirror of KVCacheLayer (include/kv_cache.h:7-18); pointers are device
+ * pointers into the cache's HBM slab. */
+typedef struct ec_kv_layer {
+    int8_t* keys_int8;
+    int8_t* values_int8;
+    float* key_scales;
+    float* val_scales;
+    float* keys_fp32;
+    float* values_fp32;
+    uint32_t seq_len;
+} ec_kv_layer;
+
+typedef struct ec_kv_cache ec_kv_cache;
+
+/* KVCache::KVCache (src/kv_cache.cpp:6-72): one zeroed device slab on the
+ * current device, partitioned per layer exactly as the reference partitions
+ * its host slab.  scale_mode selects PER_HEAD (default) or ROW scales. */
+EC_API int ec_kv_cache_create(const ec_model_config* config, int scale_mode, ec_kv_cache** out);
+/* KVCache::~KVCache (src/kv_cache.cpp:74-77).  Synchronises the device. */
+EC_API void ec_kv_cache_destroy(ec_kv_cache* cache);
+/* KVCache::layer (src/kv_cache.cpp:79-87). */
+EC_API int ec_kv_cache_layer(const ec_kv_cache* cache, uint32_t layer_idx, ec_kv_layer* out);
+/* KVCache::append (src/kv_cache.cpp:89-113): quantizes one token's K and V
+ * ([num_kv_heads*head_dim] fp32 each, device) into the next slot of layer
+ * layer_idx and advances that layer's length.  EC_ERR_CAPACITY instead of the
+ * reference's assert when the layer is full (src/kv_cache.cpp:91). */
+EC_API int ec_kv_cache_append(ec_kv_cache* cache, uint32_t layer_idx, const float* k_proj,
+                       const float* v_proj, ec_stream_t stream);
+/* KVCache::seq_len (src/kv_cache.cpp:115-118): layer 0's length. */
+EC_API uint32_t ec_kv_cache_seq_len(const ec_kv_cache* cache);
+/* KVCache::reset (src/kv_cache.cpp:120-124): zeroes every layer's length. */
+EC_API int ec_kv_cache_reset(ec_kv_cache* cache);
+/* The KV part of InferenceEngine::attention (src/inference.cpp:321-406) for
+ * one decode step of layer layer_idx over that layer's own length:
+ * q [num_heads*head_dim] fp32 (unscaled; softmax_scale is applied to q first,
+ * as src/inference.cpp:322-325 does), out [num_heads*head_dim] fp32, both
+ * device.  Q head h reads KV head h % num_kv_heads (src/inference.cpp:335).
+ * A layer of length 0 gives zeros (src/inference.cpp:331). */
+EC_API int ec_kv_cache_attention(ec_kv_cache* cache, uint32_t layer_idx, const float* q, float* out,
+                          float softmax_scale, ec_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Batched ragged cache: per-sequence contiguous slabs inside caller-owned
+ * device buffers, addressed through an int32 offset / capacity / length
+ * table.  Sequence s owns slots [seq_offset[s], seq_offset[s]+seq_capacity[s])
+ * and holds seq_len[s] tokens.
+ * ---------------------------------------------------------------------- */
+typedef struct ec_kv_batch {
+    int8_t* keys;                /* [total_slots][num_kv_heads][head_dim]          */
+    int8_t* values;              /* same                                           */
+    float* key_scales;           /* [total_slots][num_kv_heads] or [total_slots]   */
+    float* val_scales;           /* same                                           */
+    const int32_t* seq_offset;   /* [num_seqs] first slot of each sequence         */
+    const int32_t* seq_capacity; /* [num_seqs] slots owned by each sequence        */
+    int32_t* seq_len;            /* [num_seqs] cached tokens (append advances it)  */
+    int32_t* error_word;         /* device int32 or NULL (library word)            */
+    uint64_t total_slots;        /* slots in keys/values (bounds every table entry)*/
+    uint32_t num_seqs;
+    uint32_t num_kv_heads;
+    uint32_t head_dim;
+    int32_t scale_mode;          /* ec_scale_mode                                  */
+    uint32_t max_seq_len;        /* host-side bound on every seq_len (sizes grids) */
+} ec_kv_batch;
+
+/* Batched KVCache::append: quantizes tokens_per_seq new tokens of every
+ * sequence, k/v [num_seqs][tokens_per_seq][num_kv_heads*head_dim] fp32 device,
+ * into slots seq_offset[s]+seq_len[s]+i, then advances seq_len[s].  A
+ * sequence that would pass its capacity is skipped whole and flags
+ * EC_DEVERR_OVERFLOW. */
+EC_API int ec_kv_batch_append(const ec_kv_batch* batch, const float* k, const float* v,
+                       uint32_t tokens_per_seq, ec_stream_t stream);
+
+/* Workspace (device bytes) ec_decode_attention needs for this batch shape on
+ * the current device. */
+EC_API size_t ec_decode_workspace_size(uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim,
+                                uint32_t max_seq_len);
+
+/* Decode attention for every sequence of the batch (the loop of
+ * src/inference.cpp:321-392 per sequence):
+ * q [num_seqs][num_heads][head_dim] fp32, out same shape fp32, device.
+ * Supported envelope: head_dim 128, num_kv_heads 4 or 8,
+ * num_heads/num_kv_heads in {1, 2, 4}. */
+EC_API int ec_decode_attention(const ec_kv_batch* batch, const float* q, float* out,
+                        uint32_t num_heads, float softmax_scale, void* workspace,
+                        size_t workspace_bytes, ec_stream_t stream);
+
+/* Context parallelism.  ec_decode_attention_partial computes, for every
+ * (sequence, head), the unnormalised partial state over this batch's tokens:
+ *   part_o  [num_seqs][num_heads][head_dim]  sum_t 2^(s_t*log2e - m) * v_t
+ *   part_ml [num_seqs][num_heads][2]         (m, l): m = max_t s_t*log2e,
+ *                                            l = sum_t 2^(s_t*log2e - m)
+ * (m = -inf, l = 0, o = 0 for an empty shard).  ec_lse_combine merges
+ * num_parts such states, stacked [num_parts][...] in a fixed part order, into
+ * the normalised output [num_seqs][num_heads][head_dim]. */
+EC_API int ec_decode_attention_partial(const ec_kv_batch* batch, const float* q, float* part_o,
+                                float* part_ml, uint32_t num_heads, float softmax_scale,
+                                void* workspace, size_t workspace_bytes, ec_stream_t stream);
+EC_API int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t num_parts,
+                   uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim, float* out,
+                   ec_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* EC_KV_H */

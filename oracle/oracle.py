@@ -1,0 +1,254 @@
+"""ctypes front end of the CPU checkers (TEST INFRASTRUCTURE ONLY).
+
+Loads ``liboracle.so`` (the C restatement in ec_oracle.c) and, when it has
+been built, ``_ref/libecref.so`` (the reference's own compiled sources behind
+ref_shim.cpp).  Only tests, ``__graft_entry__.smoke()`` and the CPU-baseline
+leg of ``bench.py`` import this module.  The shipped library never does.
+
+All arrays are numpy, C-contiguous, float32 / int8.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libecref.so")
+
+SCALE_PER_HEAD = 0
+SCALE_ROW = 1
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i8p = ctypes.POINTER(ctypes.c_int8)
+_u32 = ctypes.c_uint32
+
+
+def _p(a: np.ndarray, ty):
+    return a.ctypes.data_as(ty)
+
+
+def build_oracle() -> None:
+    """Compile liboracle.so if it is missing (gcc only, a second or two)."""
+    if not os.path.exists(ORACLE_SO):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build_oracle()
+        L = ctypes.CDLL(ORACLE_SO)
+        L.oracle_quantize_per_token_symmetric.argtypes = [_f32p, _i8p, _f32p, _u32, _u32]
+        L.oracle_fused_dequant_dot_int8.argtypes = [_f32p, _i8p, _f32p, _f32p, _u32, _u32]
+        L.oracle_kv_append_token.argtypes = [_i8p, _i8p, _f32p, _f32p, _u32, _f32p, _f32p, _u32,
+                                             _u32, ctypes.c_int]
+        L.oracle_decode_attention.argtypes = [_i8p, _i8p, _f32p, _f32p, _u32, _f32p, _f32p, _u32,
+                                              _u32, _u32, ctypes.c_float, ctypes.c_int, _f32p]
+        L.oracle_prefill_attention.argtypes = [_i8p, _i8p, _f32p, _f32p, _u32, _u32, _f32p, _f32p,
+                                               _u32, _u32, _u32, ctypes.c_float, ctypes.c_int, _f32p]
+        _lib = L
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref():
+    """The reference's own code (oracle/_ref).  Raises if it was not built."""
+    global _ref
+    if _ref is None:
+        if not ref_available():
+            raise FileNotFoundError(f"{REF_SO} not built (make -C oracle REF=<reference checkout>)")
+        L = ctypes.CDLL(REF_SO)
+        vp = ctypes.c_void_p
+        L.ref_quantize_per_token_symmetric.argtypes = [_f32p, _i8p, _f32p, _u32, _u32]
+        L.ref_fused_dequant_dot_int8.argtypes = [_f32p, _i8p, _f32p, _f32p, _u32, _u32]
+        L.ref_kvcache_create.argtypes = [_u32, _u32, _u32, _u32, ctypes.c_int]
+        L.ref_kvcache_create.restype = vp
+        L.ref_kvcache_destroy.argtypes = [vp]
+        L.ref_kvcache_append.argtypes = [vp, _u32, _f32p, _f32p]
+        L.ref_kvcache_seq_len.argtypes = [vp]
+        L.ref_kvcache_seq_len.restype = _u32
+        L.ref_kvcache_layer_seq_len.argtypes = [vp, _u32]
+        L.ref_kvcache_layer_seq_len.restype = _u32
+        L.ref_kvcache_reset.argtypes = [vp]
+        L.ref_kvcache_layer_ptrs.argtypes = [vp, _u32, ctypes.POINTER(vp)]
+        L.ref_attn_create.argtypes = [_u32, _u32, _u32, _u32]
+        L.ref_attn_create.restype = vp
+        L.ref_attn_destroy.argtypes = [vp]
+        L.ref_attn_run.argtypes = [vp, _u32, _i8p, _i8p, _f32p, _f32p, _f32p, _f32p]
+        L.ref_attn_run.restype = ctypes.c_int
+        _ref = L
+    return _ref
+
+
+# ---------------------------------------------------------------- restatement
+def quantize_per_token_symmetric(x: np.ndarray, num_tokens: int, num_elements: int):
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    assert x.size == num_tokens * num_elements
+    q = np.zeros(x.size, np.int8)
+    s = np.zeros(num_tokens, np.float32)
+    lib().oracle_quantize_per_token_symmetric(_p(x, _f32p), _p(q, _i8p), _p(s, _f32p),
+                                              num_tokens, num_elements)
+    return q, s
+
+
+def fused_dequant_dot_int8(query, key_cache, scales, dim, seq_len):
+    query = np.ascontiguousarray(query, np.float32)
+    key_cache = np.ascontiguousarray(key_cache, np.int8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    out = np.zeros(seq_len, np.float32)
+    lib().oracle_fused_dequant_dot_int8(_p(query, _f32p), _p(key_cache, _i8p), _p(scales, _f32p),
+                                        _p(out, _f32p), dim, seq_len)
+    return out
+
+
+def quantize_kv(x: np.ndarray, num_kv_heads: int, head_dim: int, mode: int = SCALE_PER_HEAD):
+    """Quantize a [tokens, num_kv_heads*head_dim] block the way KVCache::append
+    does one token at a time.  Returns (codes [tokens, Hkv*d] int8, scales
+    [tokens, Hkv] (PER_HEAD) or [tokens] (ROW))."""
+    x = np.ascontiguousarray(x, np.float32)
+    ntok = x.shape[0]
+    if mode == SCALE_ROW:
+        q, s = quantize_per_token_symmetric(x, ntok, num_kv_heads * head_dim)
+        return q.reshape(ntok, -1), s
+    q, s = quantize_per_token_symmetric(x, ntok * num_kv_heads, head_dim)
+    return q.reshape(ntok, -1), s.reshape(ntok, num_kv_heads)
+
+
+def decode_attention(keys, values, kscales, vscales, kv_len, q, num_heads, num_kv_heads,
+                     head_dim, softmax_scale, mode=SCALE_PER_HEAD):
+    keys = np.ascontiguousarray(keys, np.int8)
+    values = np.ascontiguousarray(values, np.int8)
+    kscales = np.ascontiguousarray(kscales, np.float32)
+    vscales = np.ascontiguousarray(vscales, np.float32)
+    q = np.ascontiguousarray(q, np.float32).reshape(-1)
+    out = np.zeros(num_heads * head_dim, np.float32)
+    scratch = np.zeros(max(kv_len, 1), np.float32)
+    lib().oracle_decode_attention(_p(keys, _i8p), _p(values, _i8p), _p(kscales, _f32p),
+                                  _p(vscales, _f32p), kv_len, _p(q, _f32p), _p(out, _f32p),
+                                  num_heads, num_kv_heads, head_dim, ctypes.c_float(softmax_scale),
+                                  mode, _p(scratch, _f32p))
+    return out.reshape(num_heads, head_dim)
+
+
+def prefill_attention(keys, values, kscales, vscales, past_len, n_new, q, num_heads,
+                      num_kv_heads, head_dim, softmax_scale, mode=SCALE_PER_HEAD):
+    keys = np.ascontiguousarray(keys, np.int8)
+    values = np.ascontiguousarray(values, np.int8)
+    kscales = np.ascontiguousarray(kscales, np.float32)
+    vscales = np.ascontiguousarray(vscales, np.float32)
+    q = np.ascontiguousarray(q, np.float32).reshape(-1)
+    out = np.zeros(n_new * num_heads * head_dim, np.float32)
+    scratch = np.zeros(past_len + n_new, np.float32)
+    lib().oracle_prefill_attention(_p(keys, _i8p), _p(values, _i8p), _p(kscales, _f32p),
+                                   _p(vscales, _f32p), past_len, n_new, _p(q, _f32p),
+                                   _p(out, _f32p), num_heads, num_kv_heads, head_dim,
+                                   ctypes.c_float(softmax_scale), mode, _p(scratch, _f32p))
+    return out.reshape(n_new, num_heads, head_dim)
+
+
+# -------------------------------------------------------- the reference itself
+def ref_quantize_per_token_symmetric(x, num_tokens, num_elements):
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    q = np.zeros(x.size, np.int8)
+    s = np.zeros(num_tokens, np.float32)
+    ref().ref_quantize_per_token_symmetric(_p(x, _f32p), _p(q, _i8p), _p(s, _f32p),
+                                           num_tokens, num_elements)
+    return q, s
+
+
+def ref_fused_dequant_dot_int8(query, key_cache, scales, dim, seq_len):
+    query = np.ascontiguousarray(query, np.float32)
+    key_cache = np.ascontiguousarray(key_cache, np.int8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    out = np.zeros(seq_len, np.float32)
+    ref().ref_fused_dequant_dot_int8(_p(query, _f32p), _p(key_cache, _i8p), _p(scales, _f32p),
+                                     _p(out, _f32p), dim, seq_len)
+    return out
+
+
+class RefKVCache:
+    """The reference's KVCache (src/kv_cache.cpp), host memory."""
+
+    def __init__(self, num_kv_heads, head_dim, num_layers, max_seq_len, quant=True):
+        self.h = ref().ref_kvcache_create(num_kv_heads, head_dim, num_layers, max_seq_len,
+                                          int(quant))
+        self.hkv, self.d, self.max_seq = num_kv_heads, head_dim, max_seq_len
+        self.quant = quant
+
+    def close(self):
+        if self.h:
+            ref().ref_kvcache_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def append(self, layer, k, v):
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        ref().ref_kvcache_append(self.h, layer, _p(k, _f32p), _p(v, _f32p))
+
+    def seq_len(self):
+        return ref().ref_kvcache_seq_len(self.h)
+
+    def layer_seq_len(self, layer):
+        return ref().ref_kvcache_layer_seq_len(self.h, layer)
+
+    def reset(self):
+        ref().ref_kvcache_reset(self.h)
+
+    def layer_arrays(self, layer):
+        """Copies of the layer's int8 codes [max_seq, Hkv*d] and both scale
+        buffers [max_seq*Hkv] (int8 mode), or fp32 K/V (fp32 mode)."""
+        ptrs = (ctypes.c_void_p * 6)()
+        ref().ref_kvcache_layer_ptrs(self.h, layer, ptrs)
+        row = self.hkv * self.d
+        n = self.max_seq
+        if self.quant:
+            k = np.ctypeslib.as_array(ctypes.cast(ptrs[0], _i8p), (n * row,)).copy()
+            v = np.ctypeslib.as_array(ctypes.cast(ptrs[1], _i8p), (n * row,)).copy()
+            ks = np.ctypeslib.as_array(ctypes.cast(ptrs[2], _f32p), (n * self.hkv,)).copy()
+            vs = np.ctypeslib.as_array(ctypes.cast(ptrs[3], _f32p), (n * self.hkv,)).copy()
+            return k.reshape(n, row), v.reshape(n, row), ks, vs
+        k = np.ctypeslib.as_array(ctypes.cast(ptrs[4], _f32p), (n * row,)).copy()
+        v = np.ctypeslib.as_array(ctypes.cast(ptrs[5], _f32p), (n * row,)).copy()
+        return k.reshape(n, row), v.reshape(n, row)
+
+
+class RefAttention:
+    """The reference's InferenceEngine::attention loop (src/inference.cpp:321-406)."""
+
+    def __init__(self, num_heads, num_kv_heads, head_dim, max_seq_len):
+        self.h = ref().ref_attn_create(num_heads, num_kv_heads, head_dim, max_seq_len)
+        self.H, self.hkv, self.d = num_heads, num_kv_heads, head_dim
+
+    def close(self):
+        if self.h:
+            ref().ref_attn_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def run(self, keys, values, kscales, vscales, kv_len, q):
+        keys = np.ascontiguousarray(keys, np.int8)
+        values = np.ascontiguousarray(values, np.int8)
+        kscales = np.ascontiguousarray(kscales, np.float32)
+        vscales = np.ascontiguousarray(vscales, np.float32)
+        q = np.ascontiguousarray(q, np.float32).reshape(-1)
+        out = np.zeros(self.H * self.d, np.float32)
+        rc = ref().ref_attn_run(self.h, kv_len, _p(keys, _i8p), _p(values, _i8p),
+                                _p(kscales, _f32p), _p(vscales, _f32p), _p(q, _f32p),
+                                _p(out, _f32p))
+        if rc != 0:
+            raise ValueError("kv_len must be below the engine's max_seq_len")
+        return out.reshape(self.H, self.d)

@@ -1,0 +1,156 @@
+// ref_shim.cpp -- extern "C" entry points over echo-core's OWN compiled code.
+//
+// TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
+// the unmodified reference sources (src/kernels/quant.cpp, src/kv_cache.cpp,
+// src/inference.cpp, src/kernels/matvec.cpp, src/gguf_reader.cpp) into
+// oracle/_ref/libecref.so.  Parity tests use it to pin the C restatement in
+// ec_oracle.c against the reference itself, and to regenerate the golden
+// fixtures under tests/golden/.  Nothing in the shipped library uses it.
+//
+// The decode-attention loop of the reference is the private method
+// InferenceEngine::attention (src/inference.cpp:301-415).  It is reached here
+// without editing the reference: a one-layer engine whose Q and O projections
+// are fp16 identity matrices (so q == input and output == attn_out exactly),
+// a cache filled directly through KVCache::layer(), and the standard
+// explicit-instantiation rule that lets a template argument name a private
+// member ([temp.spec] "the usual access checking rules do not apply to names
+// used to specify explicit instantiations").
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include "inference.h"
+#include "kv_cache.h"
+#include "kernels/quant.h"
+
+namespace {
+
+template <typename Tag, typename Tag::type M>
+struct Expose {
+    friend typename Tag::type get(Tag) { return M; }
+};
+
+struct AttentionTag {
+    typedef void (InferenceEngine::*type)(uint32_t, const float*, float*);
+    friend type get(AttentionTag);
+};
+template struct Expose<AttentionTag, &InferenceEngine::attention>;
+
+struct CacheTag {
+    typedef std::unique_ptr<KVCache> InferenceEngine::*type;
+    friend type get(CacheTag);
+};
+template struct Expose<CacheTag, &InferenceEngine::kv_cache_>;
+
+ModelConfig make_config(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                        uint32_t num_layers, uint32_t max_seq_len, bool quant) {
+    ModelConfig c{};
+    c.vocab_size = 4;
+    c.hidden_dim = num_heads * head_dim;
+    c.num_heads = num_heads;
+    c.num_kv_heads = num_kv_heads;
+    c.head_dim = head_dim;
+    c.num_layers = num_layers;
+    c.ffn_hidden_dim = 8;
+    c.max_seq_len = max_seq_len;
+    c.ffn_type = ModelConfig::FFNType::Dense;
+    c.norm_type = ModelConfig::NormType::RMSNorm;
+    c.pos_encoding = ModelConfig::PosEncoding::None;
+    c.use_kv_quantization = quant;
+    return c;
+}
+
+}  // namespace
+
+extern "C" {
+
+// include/kernels/quant.h:8-14
+void ref_quantize_per_token_symmetric(const float* input, int8_t* output, float* scales,
+                                      uint32_t num_tokens, uint32_t num_elements) {
+    quantize_per_token_symmetric(input, output, scales, num_tokens, num_elements);
+}
+
+// include/kernels/quant.h:19-26
+void ref_fused_dequant_dot_int8(const float* query, const int8_t* key_cache, const float* scales,
+                                float* scores, uint32_t dim, uint32_t seq_len) {
+    fused_dequant_dot_int8(query, key_cache, scales, scores, dim, seq_len);
+}
+
+// ---- KVCache (include/kv_cache.h:21-48) ----
+void* ref_kvcache_create(uint32_t num_kv_heads, uint32_t head_dim, uint32_t num_layers,
+                         uint32_t max_seq_len, int use_quant) {
+    ModelConfig c = make_config(num_kv_heads, num_kv_heads, head_dim, num_layers, max_seq_len,
+                                use_quant != 0);
+    return new KVCache(c);
+}
+void ref_kvcache_destroy(void* h) { delete static_cast<KVCache*>(h); }
+void ref_kvcache_append(void* h, uint32_t layer, const float* k, const float* v) {
+    static_cast<KVCache*>(h)->append(layer, k, v);
+}
+uint32_t ref_kvcache_seq_len(void* h) { return static_cast<KVCache*>(h)->seq_len(); }
+uint32_t ref_kvcache_layer_seq_len(void* h, uint32_t layer) {
+    return static_cast<KVCache*>(h)->layer(layer).seq_len;
+}
+void ref_kvcache_reset(void* h) { static_cast<KVCache*>(h)->reset(); }
+// Pointers of one layer's host storage: [keys_int8, values_int8, key_scales,
+// val_scales, keys_fp32, values_fp32].
+void ref_kvcache_layer_ptrs(void* h, uint32_t layer, void** out6) {
+    const KVCacheLayer& l = static_cast<KVCache*>(h)->layer(layer);
+    out6[0] = l.keys_int8;
+    out6[1] = l.values_int8;
+    out6[2] = l.key_scales;
+    out6[3] = l.val_scales;
+    out6[4] = l.keys_fp32;
+    out6[5] = l.values_fp32;
+}
+
+// ---- InferenceEngine::attention over a caller-provided int8 cache ----
+struct RefAttn {
+    std::unique_ptr<InferenceEngine> eng;
+    uint32_t num_heads, num_kv_heads, head_dim, max_seq_len;
+};
+
+void* ref_attn_create(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                      uint32_t max_seq_len) {
+    ModelConfig c = make_config(num_heads, num_kv_heads, head_dim, 1, max_seq_len, true);
+    auto* r = new RefAttn{std::make_unique<InferenceEngine>(c), num_heads, num_kv_heads, head_dim,
+                          max_seq_len};
+    WeightLayout L = WeightLayout::compute(c);
+    std::vector<uint16_t> w(L.total_size / sizeof(uint16_t), 0);
+    const size_t hidden = c.hidden_dim;
+    const size_t lb = L.token_embedding_size;  // layer 0 base (bytes)
+    const uint16_t one = 0x3C00;               // fp16 1.0
+    for (size_t i = 0; i < hidden; ++i) {
+        w[(lb + L.q_proj_offset) / 2 + i * hidden + i] = one;
+        w[(lb + L.o_proj_offset) / 2 + i * hidden + i] = one;
+    }
+    r->eng->load_weights(w.data());
+    return r;
+}
+
+void ref_attn_destroy(void* h) { delete static_cast<RefAttn*>(h); }
+
+// Runs the reference's attention loop for one decode step of layer 0 over
+// kv_len cached tokens (layout [pos][num_kv_heads][head_dim], per-head scales
+// [pos][num_kv_heads]).  q: [num_heads*head_dim] unscaled; out: same size.
+// Returns 0 on success, -1 if kv_len does not leave room for the append that
+// attention() performs at its end (src/inference.cpp:414).
+int ref_attn_run(void* h, uint32_t kv_len, const int8_t* keys, const int8_t* values,
+                 const float* key_scales, const float* val_scales, const float* q, float* out) {
+    RefAttn* r = static_cast<RefAttn*>(h);
+    if (kv_len >= r->max_seq_len) return -1;
+    KVCache& cache = *(r->eng.get()->*get(CacheTag()));
+    cache.reset();
+    KVCacheLayer& l = cache.layer(0);
+    const size_t row = static_cast<size_t>(r->num_kv_heads) * r->head_dim;
+    std::memcpy(l.keys_int8, keys, kv_len * row);
+    std::memcpy(l.values_int8, values, kv_len * row);
+    std::memcpy(l.key_scales, key_scales, kv_len * r->num_kv_heads * sizeof(float));
+    std::memcpy(l.val_scales, val_scales, kv_len * r->num_kv_heads * sizeof(float));
+    l.seq_len = kv_len;
+    (r->eng.get()->*get(AttentionTag()))(0, q, out);
+    return 0;
+}
+
+}  // extern "C"

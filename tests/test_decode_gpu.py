@@ -1,0 +1,230 @@
+"""Split-K decode attention on the GPU against the oracle's fp32 output
+(max-abs 2e-3 / rel 1e-3), including the reference's golden outputs, the
+BASELINE shapes, GQA groupings, ROW scales, ragged and empty sequences, and
+context-parallel partials merged by the log-sum-exp combine."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+import workloads as W
+from _util import assert_attn_close, fill_batch
+
+pytestmark = pytest.mark.gpu
+
+D = 128
+
+
+def _dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda")
+
+
+def _make_seq(rng, L, hkv, mode=O.SCALE_PER_HEAD):
+    kq, ks = O.quantize_kv(W.kv_rows(rng, L, hkv, D), hkv, D, mode)
+    vq, vs = O.quantize_kv(W.kv_rows(rng, L, hkv, D), hkv, D, mode)
+    return kq, vq, ks, vs
+
+
+def _run_batch(torch, eckv, seqs, q, H, hkv, mode=0, caps=None, scale=None):
+    caps = caps or [max(s[0].shape[0], 1) for s in seqs]
+    bc = eckv.BatchCache(caps, num_kv_heads=hkv, scale_mode=mode)
+    fill_batch(bc, seqs)
+    out = torch.empty((len(seqs), H, D), dtype=torch.float32, device="cuda")
+    bc.decode(_dev(torch, q), out, H, W.softmax_scale(D) if scale is None else scale)
+    torch.cuda.synchronize()
+    assert bc.device_error() == 0
+    return out.cpu().numpy(), bc
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c"])
+def test_decode_matches_reference_golden(cuda, golden, tag):
+    import torch
+    import eckv
+    g = golden("attention.npz")
+    seq = (g[f"{tag}_keys"], g[f"{tag}_values"], g[f"{tag}_kscales"], g[f"{tag}_vscales"])
+    got, _ = _run_batch(torch, eckv, [seq], g[f"{tag}_q"][None], 16, 4)
+    assert_attn_close(got[0], g[f"{tag}_out"], tag)
+
+
+def test_config1_single_sequence_4096(cuda):
+    """batch 1, ctx 4096, 16 Q / 4 KV heads, seed 0."""
+    import torch
+    import eckv
+    cfg = W.config(1)
+    rng = np.random.default_rng(cfg.seed)
+    seq = _make_seq(rng, 4096, 4)
+    q = W.queries(rng, 1, 16, D)
+    got, _ = _run_batch(torch, eckv, [seq], q, 16, 4)
+    want = O.decode_attention(*seq, 4096, q[0], 16, 4, D, W.softmax_scale(D))
+    assert_attn_close(got[0], want, "cfg1")
+
+
+def test_config2_ragged_batch_append_then_decode(cuda):
+    """64 sequences, ctx U[512, 8192], append one token per
+    sequence (quantize-on-append on the GPU), then decode; seed 1."""
+    import torch
+    import eckv
+    cfg = W.config(2)
+    rng = np.random.default_rng(cfg.seed)
+    seqs = [_make_seq(rng, L, 4) for L in cfg.ctx]
+    k_new = W.kv_rows(rng, 64, 4, D)
+    v_new = W.kv_rows(rng, 64, 4, D)
+    q = W.queries(rng, 64, 16, D)
+    bc = eckv.BatchCache([L + 1 for L in cfg.ctx], num_kv_heads=4)
+    fill_batch(bc, seqs)
+    bc.append(_dev(torch, k_new), _dev(torch, v_new), 1)
+    out = torch.empty((64, 16, D), dtype=torch.float32, device="cuda")
+    bc.decode(_dev(torch, q), out, 16, W.softmax_scale(D))
+    torch.cuda.synchronize()
+    assert bc.device_error() == 0
+    got = out.cpu().numpy()
+    for s in range(64):
+        kq, vq, ks, vs = seqs[s]
+        nk, nks = O.quantize_kv(k_new[s:s + 1], 4, D)
+        nv, nvs = O.quantize_kv(v_new[s:s + 1], 4, D)
+        K = np.concatenate([kq, nk]); V = np.concatenate([vq, nv])
+        KS = np.concatenate([ks, nks]); VS = np.concatenate([vs, nvs])
+        want = O.decode_attention(K, V, KS, VS, cfg.ctx[s] + 1, q[s], 16, 4, D, W.softmax_scale(D))
+        assert_attn_close(got[s], want, f"seq {s}")
+
+
+@pytest.mark.parametrize("H,hkv", [(16, 4), (8, 4), (4, 4), (32, 8), (16, 8), (8, 8)])
+def test_gqa_groupings(cuda, H, hkv):
+    import torch
+    import eckv
+    rng = np.random.default_rng(H * 100 + hkv)
+    lens = [1, 31, 32, 33, 200, 1000]
+    seqs = [_make_seq(rng, L, hkv) for L in lens]
+    q = W.queries(rng, len(lens), H, D)
+    got, _ = _run_batch(torch, eckv, seqs, q, H, hkv)
+    for s, L in enumerate(lens):
+        want = O.decode_attention(*seqs[s], L, q[s], H, hkv, D, W.softmax_scale(D))
+        assert_attn_close(got[s], want, f"H{H} hkv{hkv} L{L}")
+
+
+def test_row_scale_mode(cuda):
+    import torch
+    import eckv
+    rng = np.random.default_rng(42)
+    lens = [7, 130, 515]
+    seqs = [_make_seq(rng, L, 4, O.SCALE_ROW) for L in lens]
+    q = W.queries(rng, len(lens), 16, D)
+    got, _ = _run_batch(torch, eckv, seqs, q, 16, 4, mode=eckv.SCALE_ROW)
+    for s, L in enumerate(lens):
+        want = O.decode_attention(*seqs[s], L, q[s], 16, 4, D, W.softmax_scale(D), O.SCALE_ROW)
+        assert_attn_close(got[s], want, f"row L{L}")
+
+
+def test_empty_and_single_token_sequences(cuda):
+    """A sequence with no cached token yields zeros (src/inference.cpp:328-331)."""
+    import torch
+    import eckv
+    rng = np.random.default_rng(7)
+    e = (np.zeros((0, 512), np.int8), np.zeros((0, 512), np.int8), np.zeros(0, np.float32),
+         np.zeros(0, np.float32))
+    seqs = [e, _make_seq(rng, 1, 4), e, _make_seq(rng, 3000, 4)]
+    q = W.queries(rng, 4, 16, D)
+    got, _ = _run_batch(torch, eckv, seqs, q, 16, 4, caps=[4, 4, 4, 3000])
+    assert not got[0].any() and not got[2].any()
+    for s in (1, 3):
+        L = seqs[s][0].shape[0]
+        want = O.decode_attention(*seqs[s], L, q[s], 16, 4, D, W.softmax_scale(D))
+        assert_attn_close(got[s], want, f"L{L}")
+
+
+def test_all_empty_batch_direct_path(cuda):
+    import torch
+    import eckv
+    bc = eckv.BatchCache([8, 8], num_kv_heads=4)
+    q = torch.randn(2, 16, D, device="cuda")
+    out = torch.full((2, 16, D), 7.0, device="cuda")
+    bc.decode(q, out, 16, 0.1)
+    torch.cuda.synchronize()
+    assert not out.cpu().numpy().any()
+
+
+def test_kvcache_object_append_then_attention(cuda):
+    """The KVCache object path: append through the GPU quantizer one token at a
+    time (the reference's per-token loop), then attention over layer 1's own
+    length, against the oracle fed the same fp32 projections."""
+    import torch
+    import eckv
+    rng = np.random.default_rng(11)
+    L = 300
+    k = W.kv_rows(rng, L, 4, D)
+    v = W.kv_rows(rng, L, 4, D)
+    q = W.queries(rng, 1, 16, D)[0]
+    c = eckv.KVCache(num_heads=16, num_kv_heads=4, head_dim=D, num_layers=2, max_seq_len=512)
+    kd, vd = _dev(torch, k), _dev(torch, v)
+    for t in range(L):
+        c.append(1, kd[t], vd[t])
+    out = torch.empty(16 * D, dtype=torch.float32, device="cuda")
+    c.attention(1, _dev(torch, q), out, W.softmax_scale(D))
+    torch.cuda.synchronize()
+    kq, ks = O.quantize_kv(k, 4, D)
+    vq, vs = O.quantize_kv(v, 4, D)
+    want = O.decode_attention(kq, vq, ks, vs, L, q, 16, 4, D, W.softmax_scale(D))
+    assert_attn_close(out.cpu().numpy().reshape(16, D), want, "kvcache object")
+    out0 = torch.ones(16 * D, dtype=torch.float32, device="cuda")
+    c.attention(0, _dev(torch, q), out0, W.softmax_scale(D))  # layer 0 is empty
+    torch.cuda.synchronize()
+    assert not out0.cpu().numpy().any()
+    c.close()
+
+
+@pytest.mark.parametrize("parts", [2, 3, 4])
+def test_context_parallel_partials_and_lse_combine(cuda, parts):
+    """One long sequence split contiguously across `parts` shards: partial
+    (m, l, O) per shard, merged by ec_lse_combine, equals the whole."""
+    import torch
+    import eckv
+    rng = np.random.default_rng(parts)
+    L = 20000
+    kq, vq, ks, vs = _make_seq(rng, L, 4)
+    q = W.queries(rng, 1, 16, D)
+    bounds = np.linspace(0, L, parts + 1).astype(int)
+    po = torch.empty((parts, 1, 16, D), dtype=torch.float32, device="cuda")
+    pml = torch.empty((parts, 1, 16, 2), dtype=torch.float32, device="cuda")
+    qd = _dev(torch, q)
+    for p in range(parts):
+        a, b = bounds[p], bounds[p + 1]
+        bc = eckv.BatchCache([b - a], num_kv_heads=4)
+        fill_batch(bc, [(kq[a:b], vq[a:b], ks[a * 4:b * 4], vs[a * 4:b * 4])])
+        bc.decode_partial(qd, po[p], pml[p], 16, W.softmax_scale(D))
+    out = torch.empty((1, 16, D), dtype=torch.float32, device="cuda")
+    eckv.lse_combine(po, pml, parts, 1, 16, D, out)
+    torch.cuda.synchronize()
+    want = O.decode_attention(kq, vq, ks, vs, L, q[0], 16, 4, D, W.softmax_scale(D))
+    assert_attn_close(out.cpu().numpy()[0], want, f"cp{parts}")
+
+
+def test_bad_length_table_is_flagged_not_read(cuda):
+    import torch
+    import eckv
+    rng = np.random.default_rng(5)
+    seqs = [_make_seq(rng, 40, 4), _make_seq(rng, 40, 4)]
+    bc = eckv.BatchCache([40, 40], num_kv_heads=4)
+    fill_batch(bc, seqs)
+    bc.length.copy_(torch.tensor([40, 41], dtype=torch.int32))  # 41 > capacity 40
+    out = torch.zeros((2, 16, D), device="cuda")
+    q = W.queries(rng, 2, 16, D)
+    bc.decode(_dev(torch, q), out, 16, W.softmax_scale(D))
+    torch.cuda.synchronize()
+    assert bc.device_error() == eckv.DEVERR_BAD_TABLE
+    want = O.decode_attention(*seqs[0], 40, q[0], 16, 4, D, W.softmax_scale(D))
+    assert_attn_close(out.cpu().numpy()[0], want, "good sequence still decoded")
+
+
+def test_repeated_calls_are_deterministic(cuda):
+    import torch
+    import eckv
+    rng = np.random.default_rng(8)
+    seqs = [_make_seq(rng, L, 4) for L in (5000, 70, 9000)]
+    q = W.queries(rng, 3, 16, D)
+    a, bc = _run_batch(torch, eckv, seqs, q, 16, 4)
+    out = torch.empty((3, 16, D), dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        bc.decode(_dev(torch, q), out, 16, W.softmax_scale(D))
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), a)
