@@ -109,43 +109,60 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU legs
-def cpu_decode_units(n_units, ctx, threads, use_ref):
-    """Times n_units single-sequence decode steps at `ctx` on the host.
-    use_ref: the reference's own InferenceEngine::attention (oracle/_ref);
-    else the C restatement (oracle/liboracle.so), single-threaded."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    rng = np.random.default_rng(2)
-    kq, ks = O.quantize_kv(W.kv_rows(rng, ctx, HKV, D), HKV, D)
-    vq, vs = O.quantize_kv(W.kv_rows(rng, ctx, HKV, D), HKV, D)
-    q = W.queries(rng, 1, H, D)[0]
-    if not use_ref:
+class CpuDecode:
+    """Single-sequence decode steps at `ctx` on the host (setup once, time steps).
+
+    use_ref: the reference's own InferenceEngine::attention (oracle/_ref), one
+    engine per thread, each holding one copy of the cache; else the C
+    restatement (oracle/liboracle.so) on one thread."""
+
+    def __init__(self, ctx, threads, use_ref):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        self.O, self.ctx, self.threads, self.use_ref = O, ctx, threads, use_ref
+        rng = np.random.default_rng(2)
+        self.kq, self.ks = O.quantize_kv(W.kv_rows(rng, ctx, HKV, D), HKV, D)
+        self.vq, self.vs = O.quantize_kv(W.kv_rows(rng, ctx, HKV, D), HKV, D)
+        self.q = W.queries(rng, 1, H, D)[0]
+        self.engines = []
+        if use_ref:
+            for _ in range(threads):
+                e = O.RefAttention(H, HKV, D, ctx + 1)
+                e.load(self.kq, self.vq, self.ks, self.vs, ctx)
+                self.engines.append(e)
+
+    def run(self, n_units):
+        """Seconds for n_units decode steps."""
+        O = self.O
+        if not self.use_ref:
+            t0 = time.perf_counter()
+            for _ in range(n_units):
+                O.decode_attention(self.kq, self.vq, self.ks, self.vs, self.ctx, self.q, H, HKV,
+                                   D, W.softmax_scale(D))
+            return time.perf_counter() - t0
+        from concurrent.futures import ThreadPoolExecutor
+        T = self.threads
+
+        def work(i):
+            e = self.engines[i]
+            out = np.zeros(H * D, np.float32)
+            for _ in range(n_units // T + (1 if i < n_units % T else 0)):
+                e.step(self.q, out)
+
         t0 = time.perf_counter()
-        for _ in range(n_units):
-            O.decode_attention(kq, vq, ks, vs, ctx, q, H, HKV, D, W.softmax_scale(D))
+        with ThreadPoolExecutor(T) as ex:
+            list(ex.map(work, range(T)))
         return time.perf_counter() - t0
-    from concurrent.futures import ThreadPoolExecutor
-    engines = [O.RefAttention(H, HKV, D, ctx + 1) for _ in range(threads)]
-    for e in engines:  # warm: first call copies the cache in and touches the weights
-        e.run(kq, vq, ks, vs, ctx, q)
 
-    def work(i):
-        e = engines[i]
-        for _ in range(n_units // threads + (1 if i < n_units % threads else 0)):
-            e.run(kq, vq, ks, vs, ctx, q)
-
-    t0 = time.perf_counter()
-    with ThreadPoolExecutor(threads) as ex:
-        list(ex.map(work, range(threads)))
-    dt = time.perf_counter() - t0
-    for e in engines:
-        e.close()
-    return dt
+    def close(self):
+        for e in self.engines:
+            e.close()
 
 
 def cpu_baseline_line(ctx=32768, units=None):
     units = units or int(os.environ.get("EC_CPU_UNITS", "96"))
-    dt = cpu_decode_units(units, ctx, 1, use_ref=False)
+    cd = CpuDecode(ctx, 1, use_ref=False)
+    dt = cd.run(units)
     gbs = units * ctx * BYTES_PER_TOKEN / dt / 1e9
     return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
             "sample": f"{units} single-sequence decode steps (one layer) at ctx {ctx}, "
@@ -157,16 +174,19 @@ def run_reference_arm(args, rank):
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    threads = max(1, min(threads, int(os.environ.get("EC_REF_THREADS", "64"))))
     ctx = 32768
     use_ref = O.ref_available()
     kind = "reference" if use_ref else "port"
-    per_step_units = int(os.environ.get("EC_REF_UNITS", str(max(threads, 8))))
+    if not use_ref:
+        threads = 1
+    per_step_units = int(os.environ.get("EC_REF_UNITS", str(threads)))
+    cd = CpuDecode(ctx, threads, use_ref)
     for _ in range(args.warmup):
-        cpu_decode_units(threads, ctx, threads, use_ref)
-    times = []
-    for _ in range(args.steps):
-        times.append(cpu_decode_units(per_step_units, ctx, threads, use_ref))
+        cd.run(threads)
+    times = [cd.run(per_step_units) for _ in range(args.steps)]
+    cd.close()
     dt = sum(times)
     gbs = args.steps * per_step_units * ctx * BYTES_PER_TOKEN / dt / 1e9
     ms = dt / args.steps * 1e3
@@ -179,8 +199,9 @@ def run_reference_arm(args, rank):
                    "ctx": ctx, "q_heads": H, "kv_heads": HKV, "head_dim": D},
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": f"{per_step_units} (sequence, layer) decode steps of config 3 "
-                                   f"per step, {threads} host threads, "
-                                   + ("reference InferenceEngine::attention (oracle/_ref)"
+                                   f"per step on {threads} host threads, "
+                                   + ("the reference's InferenceEngine::attention (oracle/_ref; "
+                                      "includes its identity Q/K/V/O projections)"
                                       if use_ref else "C restatement (oracle)")},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -216,6 +237,16 @@ def run_gpu_arm(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     cfgn = args.config
     cfg = W.config(cfgn)
+    if args.seqs:
+        cfg.ctx = (cfg.ctx * ((args.seqs + len(cfg.ctx) - 1) // len(cfg.ctx)))[:args.seqs]
+        cfg.num_seqs = args.seqs
+        cfg.name += f"_seqs{args.seqs}"
+    if args.layers:
+        cfg.num_layers = args.layers
+        cfg.name += f"_layers{args.layers}"
+    if args.ctx:
+        cfg.ctx = [args.ctx] * len(cfg.ctx)
+        cfg.name += f"_ctx{args.ctx}"
     if cfgn == 4:
         return run_cp_arm(args, rank, world, local_rank)
     # ---- shard sequences
@@ -451,6 +482,10 @@ def main():
     ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--seqs", type=int, default=None,
+                    help="override the sequence count (small profiling cases)")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count")
+    ap.add_argument("--ctx", type=int, default=None, help="override every sequence's context")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

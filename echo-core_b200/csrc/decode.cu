@@ -37,9 +37,16 @@ namespace ec {
 namespace {
 
 constexpr int D = 128;
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 4;
+constexpr int kPairs = 8;                          // QK warp + PV warp pairs
+constexpr int kQkWarps = kPairs;
+constexpr int kConsumerWarps = 2 * kPairs;         // QK warps 0..7, PV warps 8..15
+constexpr int kThreads = kConsumerWarps * 32;      // 16 warps: 4 per SM sub-partition
+constexpr int kStages = 5;
+constexpr int kPBufs = 2;                          // P tiles in flight per pair
+// QK warp 0 also issues the bulk copies.  At its tile i it issues tile
+// i + kPrefetch, whose stage was last used by tile i - kPBufs: every warp has
+// released that stage by the time warp 0 holds the P buffer of tile i.
+constexpr int kPrefetch = kStages - kPBufs;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyRescale = 8.0f;
 constexpr unsigned kFull = 0xffffffffu;
@@ -47,14 +54,17 @@ constexpr unsigned kFull = 0xffffffffu;
 template <int HKV>
 struct Geo {
     static constexpr int T = 128 / HKV;                 // tokens per tile
-    static constexpr int WPH = kConsumerWarps / HKV;    // consumer warps per KV head
+    static constexpr int WPH = kPairs / HKV;            // pairs per KV head
     static constexpr int ROWB = HKV * D;                // code bytes per token row
     static constexpr int KV_TILE = T * ROWB;            // 16 KB
     static constexpr int SC_TILE = T * HKV * 4;         // 512 B
     static constexpr int STAGE = 2 * KV_TILE + 2 * SC_TILE;
-    static constexpr int PBUF = kConsumerWarps * 16 * 4 * 4;
-    static constexpr int SMEM = kStages * STAGE + PBUF + 2 * kStages * 8;
-    static_assert(T == WPH * 16, "each consumer warp owns 16 tokens of a tile");
+    // per pair and P buffer: P'[16 tokens][4 heads] then corr[4]
+    static constexpr int PSLOT = 16 * 4 + 4;
+    static constexpr int PBUF = kPairs * kPBufs * PSLOT * 4;
+    static constexpr int NBARS = 2 * kStages + 2 * kPairs * kPBufs;
+    static constexpr int SMEM = kStages * STAGE + PBUF + NBARS * 8;
+    static_assert(T == WPH * 16, "each pair owns 16 tokens of a tile");
 };
 
 __device__ __forceinline__ void consumer_barrier() {
@@ -75,17 +85,21 @@ __device__ __forceinline__ float pick(const float (&v)[N], int i) {
     return r;
 }
 
-// Lane (within an 8-lane token group) that ends up holding head j's dot.
-template <int GROUP>
-__device__ __forceinline__ int lane_of_head(int j) {
-    if constexpr (GROUP == 4) return (j >> 1) * 4 + (j & 1) * 2;
-    else if constexpr (GROUP == 2) return j * 4;
-    else return 0;
-}
+// Within an 8-lane token group (c = lane & 7), each lane ends the score
+// reduction holding the dot of head head_of_lane(c).  To make the reduction a
+// plain butterfly, the lane keeps its GROUP per-head partial dots in the slot
+// order slot k <-> head k ^ head_of_lane(c); the q registers are loaded in
+// that order once, so no select is needed per token.
 template <int GROUP>
 __device__ __forceinline__ int head_of_lane(int c) {
     if constexpr (GROUP == 4) return ((c >> 2) & 1) * 2 + ((c >> 1) & 1);
     else if constexpr (GROUP == 2) return (c >> 2) & 1;
+    else return 0;
+}
+template <int GROUP>
+__device__ __forceinline__ int lane_of_head(int j) {
+    if constexpr (GROUP == 4) return (j >> 1) * 4 + (j & 1) * 2;
+    else if constexpr (GROUP == 2) return j * 4;
     else return 0;
 }
 template <int GROUP>
@@ -95,37 +109,21 @@ __device__ __forceinline__ bool writer_lane(int c) {
     else return c == 0;
 }
 
-// Sum GROUP per-lane partial dots over the 8 lanes of a token group, leaving
-// head head_of_lane(c)'s total in each lane.
 template <int GROUP>
-__device__ __forceinline__ float transpose_reduce(const float (&v)[GROUP], int c) {
+__device__ __forceinline__ float butterfly(float (&v)[GROUP]) {
     if constexpr (GROUP == 4) {
-        const bool hi = (c & 4) != 0;
-        const float s0 = hi ? v[0] : v[2], s1 = hi ? v[1] : v[3];
-        float k0 = hi ? v[2] : v[0], k1 = hi ? v[3] : v[1];
-        k0 += __shfl_xor_sync(kFull, s0, 4);
-        k1 += __shfl_xor_sync(kFull, s1, 4);
-        const bool mid = (c & 2) != 0;
-        const float s = mid ? k0 : k1;
-        float k = mid ? k1 : k0;
-        k += __shfl_xor_sync(kFull, s, 2);
-        k += __shfl_xor_sync(kFull, k, 1);
-        return k;
+        v[0] += __shfl_xor_sync(kFull, v[2], 4);
+        v[1] += __shfl_xor_sync(kFull, v[3], 4);
+        v[0] += __shfl_xor_sync(kFull, v[1], 2);
     } else if constexpr (GROUP == 2) {
-        const bool hi = (c & 4) != 0;
-        const float s = hi ? v[0] : v[1];
-        float k = hi ? v[1] : v[0];
-        k += __shfl_xor_sync(kFull, s, 4);
-        k += __shfl_xor_sync(kFull, k, 2);
-        k += __shfl_xor_sync(kFull, k, 1);
-        return k;
+        v[0] += __shfl_xor_sync(kFull, v[1], 4);
+        v[0] += __shfl_xor_sync(kFull, v[0], 2);
     } else {
-        float k = v[0];
-        k += __shfl_xor_sync(kFull, k, 4);
-        k += __shfl_xor_sync(kFull, k, 2);
-        k += __shfl_xor_sync(kFull, k, 1);
-        return k;
+        v[0] += __shfl_xor_sync(kFull, v[0], 4);
+        v[0] += __shfl_xor_sync(kFull, v[0], 2);
     }
+    v[0] += __shfl_xor_sync(kFull, v[0], 1);
+    return v[0];
 }
 
 __device__ __forceinline__ void codes16_to_f2(const uint4 w, float2 (&f)[8]) {
@@ -160,6 +158,63 @@ __device__ void write_empty(const DecodeArgs& a, int seq) {
     }
 }
 
+// Bounded wait shared by all 32 lanes of a warp; the outcome is warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+    return __all_sync(kFull, mbar_wait(bar, parity));
+}
+
+// Issues tile j of the chunk into stage j % kStages (warp-collective; lane 0
+// drives the bulk copies).  Waits, bounded, until every consumer warp has
+// released the stage's previous tile.  Returns false on a timeout.
+template <int HKV>
+__device__ __forceinline__ bool issue_tile(const DecodeArgs& a, uint8_t* stages, uint64_t* full,
+                                           uint64_t* empty, int j, int n, size_t slot0,
+                                           uint64_t pol, int lane) {
+    using G = Geo<HKV>;
+    const int s = j % kStages;
+    bool ok = true;
+    if (lane == 0 && j >= kStages) ok = mbar_wait(&empty[s], ((j / kStages) - 1) & 1);
+    ok = __shfl_sync(kFull, ok, 0);
+    if (!ok) return false;
+    const int ntok = min(G::T, n - j * G::T);
+    const size_t slot = slot0 + (size_t)j * G::T;
+    uint8_t* st = stages + s * G::STAGE;
+    const uint32_t kvb = (uint32_t)ntok * G::ROWB;
+    if (!a.row_scales) {
+        if (lane == 0) {
+            const uint32_t scb = (uint32_t)ntok * HKV * 4;
+            mbar_arrive_expect_tx(&full[s], 2 * kvb + 2 * scb);
+            bulk_g2s_hint(st, a.keys + slot * G::ROWB, kvb, &full[s], pol);
+            bulk_g2s_hint(st + G::KV_TILE, a.values + slot * G::ROWB, kvb, &full[s], pol);
+            bulk_g2s_hint(st + 2 * G::KV_TILE, a.key_scales + slot * HKV, scb, &full[s], pol);
+            bulk_g2s_hint(st + 2 * G::KV_TILE + G::SC_TILE, a.val_scales + slot * HKV, scb,
+                          &full[s], pol);
+        }
+    } else {
+        // ROW scales: one fp32 per token, broadcast into the per-head tile
+        // layout with plain loads; the arrive releases them to the consumers.
+        if (lane == 0) {
+            mbar_expect_tx(&full[s], 2 * kvb);
+            bulk_g2s_hint(st, a.keys + slot * G::ROWB, kvb, &full[s], pol);
+            bulk_g2s_hint(st + G::KV_TILE, a.values + slot * G::ROWB, kvb, &full[s], pol);
+        }
+        float* ks = reinterpret_cast<float*>(st + 2 * G::KV_TILE);
+        float* vs = ks + G::T * HKV;
+        for (int t = lane; t < ntok; t += 32) {
+            const float kv = a.key_scales[slot + t];
+            const float vv = a.val_scales[slot + t];
+#pragma unroll
+            for (int g = 0; g < HKV; ++g) {
+                ks[t * HKV + g] = kv;
+                vs[t * HKV + g] = vv;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+    }
+    return true;
+}
+
 template <int HKV, int GROUP>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a) {
     using G = Geo<HKV>;
@@ -167,8 +222,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a)
     __shared__ int fail_flag;
     uint8_t* stages = smem;
     float* pbuf = reinterpret_cast<float*>(smem + kStages * G::STAGE);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * G::STAGE + G::PBUF);
-    uint64_t* empty = full + kStages;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * G::STAGE + G::PBUF);
+    uint64_t* full = bars;                           // [kStages]  TMA -> consumers
+    uint64_t* empty = full + kStages;                // [kStages]  consumers -> producer
+    uint64_t* p_full = empty + kStages;              // [kPairs][kPBufs]  QK -> PV
+    uint64_t* p_empty = p_full + kPairs * kPBufs;    // [kPairs][kPBufs]  PV -> QK
 
     const int seq = blockIdx.y;
     const int chunk = blockIdx.x;
@@ -193,252 +251,272 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        for (int i = 0; i < kPairs * kPBufs; ++i) {
+            mbar_init(&p_full[i], 1);
+            mbar_init(&p_empty[i], 1);
+        }
         fail_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    // ------------------------------------------------------------ producer
-    if (warp == kConsumerWarps) {
+    const int pair = warp % kPairs;
+    const bool is_qk = warp < kQkWarps;
+    const int g = pair / G::WPH;      // KV head
+    const int sw = pair % G::WPH;     // which 16-token slice of each tile
+    const int c = lane & 7;           // 16-byte column of the 128-byte head row
+    const int tq = lane >> 3;         // token within a 4-token pass / PV row group
+    const int hsel = head_of_lane<GROUP>(c);
+    float* pslots = pbuf + pair * kPBufs * G::PSLOT;
+    bool failed = false;
+    float* mo = reinterpret_cast<float*>(stages);                 // merge area, [8][GROUP][128]
+    float* mm = mo + kPairs * GROUP * D;                           // [8][GROUP]
+    float* ml = mm + kPairs * GROUP;                               // [8][GROUP]
+
+    if (is_qk) {
+        // ======================================================== QK warps
+        // Scores of this pair's 16 tokens x GROUP query heads on the tensor
+        // cores: mma.sync m16n8k32 with the int8 K codes as A (rows = tokens,
+        // unconverted) and q as B, split exactly into three digits
+        // q_int = 65536*d0 + 256*d1 + d2 (d0 signed, d1/d2 unsigned bytes) of a
+        // per-head 24-bit fixed-point scale.  Integer accumulation is exact;
+        // the digits are recombined in fp32.  The contraction order over the
+        // 128 dims is permuted (thread t4 holds dims [32*t4, 32*t4+32) of its
+        // rows), identically for A and B.
+        const bool producer = warp == 0;
         const size_t slot0 = (size_t)off + t0;
         const uint64_t pol = l2_policy_evict_first();
+        if (producer) {
+            for (int j = 0; j < kPrefetch && j < ntiles; ++j)
+                issue_tile<HKV>(a, stages, full, empty, j, n, slot0, pol, lane);
+        }
+        const int gid = lane >> 2;    // mma group: token row gid (and gid + 8)
+        const int t4 = lane & 3;      // thread in group: query head t4's column pair
+        // --- q digits as B fragments (n = gid <-> (head gid>>1, digit))
+        uint32_t b_hi[4][2], b_lo[4][2];   // n-tile 0: d0 (s8); n-tile 1: d1 | d2 (u8)
+        float sq_own;                      // dequant scale of head gid>>1
+        {
+            const int hq = gid >> 1;
+            const bool live = hq < GROUP;
+            float qv[32];
+            float amax = 0.0f;
+            const float* qp = a.q + ((size_t)seq * a.num_heads + g + HKV * (live ? hq : 0)) * D + 32 * t4;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float4 v = reinterpret_cast<const float4*>(qp)[e];
+                qv[4 * e + 0] = __fmul_rn(__fmul_rn(v.x, a.q_mul), kLog2e);
+                qv[4 * e + 1] = __fmul_rn(__fmul_rn(v.y, a.q_mul), kLog2e);
+                qv[4 * e + 2] = __fmul_rn(__fmul_rn(v.z, a.q_mul), kLog2e);
+                qv[4 * e + 3] = __fmul_rn(__fmul_rn(v.w, a.q_mul), kLog2e);
+            }
+#pragma unroll
+            for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(qv[e]));
+            amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+            const float kQMax = 8323072.0f;  // 2^23 - 2^16 keeps d0 in [-128, 127]
+            const float inv = amax > 0.0f ? __fdiv_rn(kQMax, amax) : 0.0f;
+            sq_own = amax > 0.0f ? __fdiv_rn(amax, kQMax) : 0.0f;
+            const bool odd = gid & 1;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+                    for (int x = 0; x < 4; ++x) {
+                        const int qi = __float2int_rn(qv[8 * j + 4 * half + x] * inv);
+                        const uint32_t d0 = (uint32_t)(qi >> 16) & 0xffu;
+                        const uint32_t r = (uint32_t)qi & 0xffffu;
+                        const uint32_t dl = odd ? (r & 0xffu) : (r >> 8);
+                        w0 |= (live && !odd ? d0 : 0u) << (8 * x);
+                        w1 |= (live ? dl : 0u) << (8 * x);
+                    }
+                    b_hi[j][half] = w0;
+                    b_lo[j][half] = w1;
+                }
+            }
+        }
+        // scale of the head this thread's accumulator columns belong to (t4)
+        const float sq = __shfl_sync(kFull, sq_own, (2 * t4) << 2);
+        const bool head_live = t4 < GROUP;
+        const float c16 = 65536.0f * sq, c8 = 256.0f * sq;
+        float m_run = -INFINITY;      // running max of head t4 (log2 units)
+        float l_part = 0.0f;          // this thread's share of head t4's sum
+
         for (int i = 0; i < ntiles; ++i) {
             const int s = i % kStages;
-            bool ok = true;
-            if (lane == 0 && i >= kStages) ok = mbar_wait(&empty[s], ((i / kStages) - 1) & 1);
-            ok = __shfl_sync(kFull, ok, 0);
-            if (!ok) {
-                if (lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
+            const int b = i % kPBufs;
+            if (!warp_wait(&full[s], (i / kStages) & 1)) { failed = true; break; }
+            const uint8_t* st = stages + s * G::STAGE;
+            const int8_t* kt = reinterpret_cast<const int8_t*>(st);
+            const float* kst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE);
+            const float* vst = kst + G::T * HKV;
+            const int valid = n - i * G::T;
+
+            const int8_t* r0 = kt + (sw * 16 + gid) * G::ROWB + g * D + 32 * t4;
+            const int8_t* r1 = r0 + 8 * G::ROWB;
+            const uint4 a00 = *reinterpret_cast<const uint4*>(r0);
+            const uint4 a01 = *reinterpret_cast<const uint4*>(r0 + 16);
+            const uint4 a10 = *reinterpret_cast<const uint4*>(r1);
+            const uint4 a11 = *reinterpret_cast<const uint4*>(r1 + 16);
+            const uint32_t w0[8] = {a00.x, a00.y, a00.z, a00.w, a01.x, a01.y, a01.z, a01.w};
+            const uint32_t w1[8] = {a10.x, a10.y, a10.z, a10.w, a11.x, a11.y, a11.z, a11.w};
+            int acc_hi[4] = {0, 0, 0, 0}, acc_lo[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                asm volatile(
+                    "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+                    "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                    : "+r"(acc_hi[0]), "+r"(acc_hi[1]), "+r"(acc_hi[2]), "+r"(acc_hi[3])
+                    : "r"(w0[2 * j]), "r"(w1[2 * j]), "r"(w0[2 * j + 1]), "r"(w1[2 * j + 1]),
+                      "r"(b_hi[j][0]), "r"(b_hi[j][1]));
+                asm volatile(
+                    "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+                    "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                    : "+r"(acc_lo[0]), "+r"(acc_lo[1]), "+r"(acc_lo[2]), "+r"(acc_lo[3])
+                    : "r"(w0[2 * j]), "r"(w1[2 * j]), "r"(w0[2 * j + 1]), "r"(w1[2 * j + 1]),
+                      "r"(b_lo[j][0]), "r"(b_lo[j][1]));
+            }
+            // accumulator (row, col): c0 (gid, 2*t4) c1 (gid, 2*t4+1) c2/c3 rows gid+8
+            const int tA = sw * 16 + gid, tB = tA + 8;
+            float sA = fmaf((float)acc_hi[0], c16, fmaf((float)acc_lo[0], c8, (float)acc_lo[1] * sq));
+            float sB = fmaf((float)acc_hi[2], c16, fmaf((float)acc_lo[2], c8, (float)acc_lo[3] * sq));
+            sA = (head_live && tA < valid) ? sA * kst[tA * HKV + g] : -INFINITY;
+            sB = (head_live && tB < valid) ? sB * kst[tB * HKV + g] : -INFINITY;
+
+            // online softmax of head t4, base 2, lazy rescale
+            float tm = fmaxf(sA, sB);
+            tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 4));
+            tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 8));
+            tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 16));
+            float corr = 1.0f;
+            if (tm > m_run + kLazyRescale) {
+                corr = exp2f(m_run - tm);
+                m_run = tm;
+            }
+            l_part *= corr;
+            const float pA = sA == -INFINITY ? 0.0f : exp2f(sA - m_run);
+            const float pB = sB == -INFINITY ? 0.0f : exp2f(sB - m_run);
+            l_part += pA + pB;
+
+            if (i >= kPBufs && !warp_wait(&p_empty[pair * kPBufs + b], ((i / kPBufs) - 1) & 1)) {
+                failed = true;
                 break;
             }
-            const int ntok = min(G::T, n - i * G::T);
-            const size_t slot = slot0 + (size_t)i * G::T;
-            uint8_t* st = stages + s * G::STAGE;
-            const uint32_t kvb = (uint32_t)ntok * G::ROWB;
-            if (!a.row_scales) {
-                if (lane == 0) {
-                    const uint32_t scb = (uint32_t)ntok * HKV * 4;
-                    mbar_arrive_expect_tx(&full[s], 2 * kvb + 2 * scb);
-                    bulk_g2s_hint(st, a.keys + slot * G::ROWB, kvb, &full[s], pol);
-                    bulk_g2s_hint(st + G::KV_TILE, a.values + slot * G::ROWB, kvb, &full[s], pol);
-                    bulk_g2s_hint(st + 2 * G::KV_TILE, a.key_scales + slot * HKV, scb, &full[s], pol);
-                    bulk_g2s_hint(st + 2 * G::KV_TILE + G::SC_TILE, a.val_scales + slot * HKV, scb,
-                                  &full[s], pol);
-                }
-            } else {
-                // ROW scales: one fp32 per token; broadcast into the per-head
-                // tile layout with plain loads, then arrive.
-                if (lane == 0) {
-                    mbar_expect_tx(&full[s], 2 * kvb);
-                    bulk_g2s_hint(st, a.keys + slot * G::ROWB, kvb, &full[s], pol);
-                    bulk_g2s_hint(st + G::KV_TILE, a.values + slot * G::ROWB, kvb, &full[s], pol);
-                }
-                float* ks = reinterpret_cast<float*>(st + 2 * G::KV_TILE);
-                float* vs = ks + G::T * HKV;
-                for (int t = lane; t < ntok; t += 32) {
-                    const float kv = a.key_scales[slot + t];
-                    const float vv = a.val_scales[slot + t];
-#pragma unroll
-                    for (int g = 0; g < HKV; ++g) {
-                        ks[t * HKV + g] = kv;
-                        vs[t * HKV + g] = vv;
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[s]);
+            if (producer && i + kPrefetch < ntiles &&
+                !issue_tile<HKV>(a, stages, full, empty, i + kPrefetch, n, slot0, pol, lane)) {
+                failed = true;
+                break;
+            }
+            float* pw = pslots + b * G::PSLOT;
+            if (head_live) {
+                pw[gid * 4 + t4] = pA == 0.0f ? 0.0f : pA * vst[tA * HKV + g];
+                pw[(gid + 8) * 4 + t4] = pB == 0.0f ? 0.0f : pB * vst[tB * HKV + g];
+                if (gid == 0) pw[64 + t4] = corr;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&p_full[pair * kPBufs + b]);
+                mbar_arrive(&empty[s]);
             }
         }
-        return;
-    }
-
-    // ------------------------------------------------------------ consumers
-    const int g = warp / G::WPH;      // KV head
-    const int sw = warp % G::WPH;     // which 16-token slice of each tile
-    const int c = lane & 7;           // 16-byte column of the 128-byte head row
-    const int tq = lane >> 3;         // token within a 4-token pass
-    const int hsel = head_of_lane<GROUP>(c);
-
-    float2 q2[GROUP][8];
-#pragma unroll
-    for (int j = 0; j < GROUP; ++j) {
-        const int h = g + HKV * j;
-        const float4* qp = reinterpret_cast<const float4*>(a.q + ((size_t)seq * a.num_heads + h) * D + 16 * c);
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-            const float4 v = qp[k4];
-            q2[j][2 * k4] = make_float2(__fmul_rn(__fmul_rn(v.x, a.q_mul), kLog2e),
-                                        __fmul_rn(__fmul_rn(v.y, a.q_mul), kLog2e));
-            q2[j][2 * k4 + 1] = make_float2(__fmul_rn(__fmul_rn(v.z, a.q_mul), kLog2e),
-                                            __fmul_rn(__fmul_rn(v.w, a.q_mul), kLog2e));
+        l_part += __shfl_xor_sync(kFull, l_part, 4);
+        l_part += __shfl_xor_sync(kFull, l_part, 8);
+        l_part += __shfl_xor_sync(kFull, l_part, 16);
+        consumer_barrier();   // every warp is done with the stage ring
+        if (failed) {
+            if (lane == 0) fail_flag = 1;
+        } else if (gid == 0 && head_live) {
+            mm[pair * GROUP + t4] = m_run;
+            ml[pair * GROUP + t4] = l_part;
         }
-    }
-
-    float2 acc_o[GROUP][8];
-#pragma unroll
-    for (int j = 0; j < GROUP; ++j)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc_o[j][k] = make_float2(0.f, 0.f);
-    float m_run[GROUP];
-#pragma unroll
-    for (int j = 0; j < GROUP; ++j) m_run[j] = -INFINITY;
-    float l_part = 0.0f;
-    bool failed = false;
-    float* pw = pbuf + warp * 64;  // [16 tokens][4 heads]
-
-    for (int i = 0; i < ntiles; ++i) {
-        const int s = i % kStages;
-        const bool ok = __all_sync(kFull, mbar_wait(&full[s], (i / kStages) & 1));
-        if (!ok) {
-            if (lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
-            failed = true;
-            break;
-        }
-        const uint8_t* st = stages + s * G::STAGE;
-        const int8_t* kt = reinterpret_cast<const int8_t*>(st);
-        const int8_t* vt = kt + G::KV_TILE;
-        const float* kst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE);
-        const float* vst = kst + G::T * HKV;
-        const int valid = n - i * G::T;  // tokens of this tile that exist (may exceed T)
-
-        // ---- scores
-        float sc[4];
-#pragma unroll
-        for (int ps = 0; ps < 4; ++ps) {
-            const int tt = sw * 16 + ps * 4 + tq;
-            const uint4 w = *reinterpret_cast<const uint4*>(kt + tt * G::ROWB + g * D + 16 * c);
-            float2 kf[8];
-            codes16_to_f2(w, kf);
-            float v[GROUP];
-#pragma unroll
-            for (int j = 0; j < GROUP; ++j) {
-                float2 a0 = __fmul2_rn(q2[j][0], kf[0]);
-                float2 a1 = __fmul2_rn(q2[j][1], kf[1]);
-#pragma unroll
-                for (int k = 2; k < 8; k += 2) {
-                    a0 = __ffma2_rn(q2[j][k], kf[k], a0);
-                    a1 = __ffma2_rn(q2[j][k + 1], kf[k + 1], a1);
-                }
-                v[j] = (a0.x + a0.y) + (a1.x + a1.y);
-            }
-            const float r = transpose_reduce<GROUP>(v, c) * kst[tt * HKV + g];
-            sc[ps] = tt < valid ? r : -INFINITY;
-        }
-
-        // ---- online softmax (base 2, lazy rescale)
-        float tm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-        tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 8));
-        tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 16));
-        float mt[GROUP];
-        bool resc = false;
-#pragma unroll
-        for (int j = 0; j < GROUP; ++j) {
-            mt[j] = __shfl_sync(kFull, tm, lane_of_head<GROUP>(j));
-            resc |= mt[j] > m_run[j] + kLazyRescale;
-        }
-        if (resc) {
-            float corr[GROUP];
-#pragma unroll
-            for (int j = 0; j < GROUP; ++j) {
-                if (mt[j] > m_run[j] + kLazyRescale) {
-                    corr[j] = exp2f(m_run[j] - mt[j]);
-                    m_run[j] = mt[j];
-                } else {
-                    corr[j] = 1.0f;
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < GROUP; ++j) {
-                const float2 cj = make_float2(corr[j], corr[j]);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) acc_o[j][k] = __fmul2_rn(acc_o[j][k], cj);
-            }
-            l_part *= pick<GROUP>(corr, hsel);
-        }
-        const float m_own = pick<GROUP>(m_run, hsel);
-#pragma unroll
-        for (int ps = 0; ps < 4; ++ps) {
-            const float p = sc[ps] == -INFINITY ? 0.0f : exp2f(sc[ps] - m_own);
-            l_part += p;
-            if (writer_lane<GROUP>(c)) {
-                const int tt = sw * 16 + ps * 4 + tq;
-                pw[(ps * 4 + tq) * 4 + hsel] = sc[ps] == -INFINITY ? 0.0f : p * vst[tt * HKV + g];
-            }
-        }
-        __syncwarp();
-
-        // ---- P . V
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int tw = it * 4 + tq;
-            const int tt = sw * 16 + tw;
-            float pp[4];
-            if constexpr (GROUP == 4) {
-                const float4 p4 = *reinterpret_cast<const float4*>(pw + tw * 4);
-                pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
-            } else if constexpr (GROUP == 2) {
-                const float2 p2 = *reinterpret_cast<const float2*>(pw + tw * 4);
-                pp[0] = p2.x; pp[1] = p2.y;
-            } else {
-                pp[0] = pw[tw * 4];
-            }
-            const uint4 w = *reinterpret_cast<const uint4*>(vt + tt * G::ROWB + g * D + 16 * c);
-            float2 vf[8];
-            codes16_to_f2(w, vf);
-#pragma unroll
-            for (int j = 0; j < GROUP; ++j) {
-                const float2 pj = make_float2(pp[j], pp[j]);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) acc_o[j][k] = __ffma2_rn(pj, vf[k], acc_o[j][k]);
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-    }
-
-    // ---- reduce the four token groups of the warp
-#pragma unroll
-    for (int j = 0; j < GROUP; ++j)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            float2 v = acc_o[j][k];
-            v.x += __shfl_xor_sync(kFull, v.x, 8);
-            v.y += __shfl_xor_sync(kFull, v.y, 8);
-            v.x += __shfl_xor_sync(kFull, v.x, 16);
-            v.y += __shfl_xor_sync(kFull, v.y, 16);
-            acc_o[j][k] = v;
-        }
-    l_part += __shfl_xor_sync(kFull, l_part, 8);
-    l_part += __shfl_xor_sync(kFull, l_part, 16);
-    float l_run[GROUP];
-#pragma unroll
-    for (int j = 0; j < GROUP; ++j) l_run[j] = __shfl_sync(kFull, l_part, lane_of_head<GROUP>(j));
-
-    // ---- merge the WPH warps of each KV head through shared memory
-    consumer_barrier();  // every warp is done with the stage ring
-    float* mo = reinterpret_cast<float*>(stages);                 // [8][GROUP][128]
-    float* mm = mo + kConsumerWarps * GROUP * D;                   // [8][GROUP]
-    float* ml = mm + kConsumerWarps * GROUP;                       // [8][GROUP]
-    if (failed) {
-        if (lane == 0) fail_flag = 1;
     } else {
-        if (tq == 0) {
+        // ======================================================== PV warps
+        float2 acc_o[GROUP][8];
+#pragma unroll
+        for (int j = 0; j < GROUP; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc_o[j][e] = make_float2(0.f, 0.f);
+
+        for (int i = 0; i < ntiles; ++i) {
+            const int s = i % kStages;
+            const int b = i % kPBufs;
+            if (!warp_wait(&p_full[pair * kPBufs + b], (i / kPBufs) & 1)) { failed = true; break; }
+            if (!warp_wait(&full[s], (i / kStages) & 1)) { failed = true; break; }
+            const int8_t* vt = reinterpret_cast<const int8_t*>(stages + s * G::STAGE) + G::KV_TILE;
+            const float* pw = pslots + b * G::PSLOT;
+            float corr[GROUP];
+            bool resc = false;
+#pragma unroll
+            for (int j = 0; j < GROUP; ++j) {
+                corr[j] = pw[64 + j];
+                resc |= corr[j] != 1.0f;
+            }
+            if (resc) {
+#pragma unroll
+                for (int j = 0; j < GROUP; ++j) {
+                    const float2 cj = make_float2(corr[j], corr[j]);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc_o[j][e] = __fmul2_rn(acc_o[j][e], cj);
+                }
+            }
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+                const int tw = it * 4 + tq;
+                const int tt = sw * 16 + tw;
+                float pp[4];
+                if constexpr (GROUP == 4) {
+                    const float4 p4 = *reinterpret_cast<const float4*>(pw + tw * 4);
+                    pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
+                } else if constexpr (GROUP == 2) {
+                    const float2 p2 = *reinterpret_cast<const float2*>(pw + tw * 4);
+                    pp[0] = p2.x; pp[1] = p2.y;
+                } else {
+                    pp[0] = pw[tw * 4];
+                }
+                const uint4 w = *reinterpret_cast<const uint4*>(vt + tt * G::ROWB + g * D + 16 * c);
+                float2 vf[8];
+                codes16_to_f2(w, vf);
+#pragma unroll
+                for (int j = 0; j < GROUP; ++j) {
+                    const float2 pj = make_float2(pp[j], pp[j]);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc_o[j][e] = __ffma2_rn(pj, vf[e], acc_o[j][e]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&p_empty[pair * kPBufs + b]);
+                mbar_arrive(&empty[s]);
+            }
+        }
+        // reduce the four row groups of the warp
+#pragma unroll
+        for (int j = 0; j < GROUP; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                float2 v = acc_o[j][e];
+                v.x += __shfl_xor_sync(kFull, v.x, 8);
+                v.y += __shfl_xor_sync(kFull, v.y, 8);
+                v.x += __shfl_xor_sync(kFull, v.x, 16);
+                v.y += __shfl_xor_sync(kFull, v.y, 16);
+                acc_o[j][e] = v;
+            }
+        consumer_barrier();   // every warp is done with the stage ring
+        if (failed) {
+            if (lane == 0) fail_flag = 1;
+        } else if (tq == 0) {
 #pragma unroll
             for (int j = 0; j < GROUP; ++j)
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    *reinterpret_cast<float2*>(mo + (warp * GROUP + j) * D + 16 * c + 2 * k) = acc_o[j][k];
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int j = 0; j < GROUP; ++j) {
-                mm[warp * GROUP + j] = m_run[j];
-                ml[warp * GROUP + j] = l_run[j];
-            }
+                for (int e = 0; e < 8; ++e)
+                    *reinterpret_cast<float2*>(mo + (pair * GROUP + j) * D + 16 * c + 2 * e) = acc_o[j][e];
         }
     }
     consumer_barrier();
     if (fail_flag) return;
 
+    // ---- merge the WPH pairs of each KV head and write the result
     const int H = a.num_heads;
     for (int o = threadIdx.x; o < HKV * GROUP * D; o += kConsumerWarps * 32) {
         const int d = o % D;

@@ -1,0 +1,69 @@
+// ec_kv_cache.hpp -- C++ face of the C ABI, shaped like echo-core's KVCache.
+//
+// echo-core's engine holds a `std::unique_ptr<KVCache>` and calls
+// KVCache(const ModelConfig&), layer(i), append(i, k, v), seq_len(), reset()
+// (include/kv_cache.h:21-48), then runs its attention loop over the layer's
+// buffers (src/inference.cpp:321-406).  ec::gpu::KVCache keeps those names
+// and argument meanings with the storage in HBM:
+//   - the constructor takes the reference's ModelConfig unchanged (layout is
+//     checked at compile time against ec_model_config);
+//   - layer(i) returns the KVCacheLayer view with device pointers;
+//   - append(i, k, v) takes device pointers to the token's fp32 K/V
+//     projections and quantizes them on the GPU;
+//   - attention(i, q, out) is the KV half of InferenceEngine::attention.
+// Errors throw std::runtime_error carrying ec_last_error(); the reference
+// used assert (compiled out) and std::runtime_error (src/inference.cpp:22).
+#pragma once
+
+#include <cstddef>
+#include <stdexcept>
+#include <string>
+
+#include "ec_kv.h"
+
+namespace ec {
+namespace gpu {
+
+inline void check(int status) {
+    if (status != EC_OK)
+        throw std::runtime_error(std::string("ec: ") + ec_status_string(status) + ": " +
+                                 ec_last_error());
+}
+
+class KVCache {
+public:
+    // Any struct laid out like ModelConfig (include/config.h:6-24) is accepted,
+    // the reference's own type included.
+    template <class ModelConfigT>
+    explicit KVCache(const ModelConfigT& config, ec_scale_mode mode = EC_SCALE_PER_HEAD) {
+        static_assert(sizeof(ModelConfigT) == sizeof(ec_model_config),
+                      "ModelConfig layout differs from ec_model_config");
+        check(ec_kv_cache_create(reinterpret_cast<const ec_model_config*>(&config), mode, &h_));
+    }
+    ~KVCache() { ec_kv_cache_destroy(h_); }
+    KVCache(const KVCache&) = delete;
+    KVCache& operator=(const KVCache&) = delete;
+
+    ec_kv_layer layer(uint32_t layer_idx) const {
+        ec_kv_layer l;
+        check(ec_kv_cache_layer(h_, layer_idx, &l));
+        return l;
+    }
+    void append(uint32_t layer_idx, const float* k_proj, const float* v_proj,
+                ec_stream_t stream = nullptr) {
+        check(ec_kv_cache_append(h_, layer_idx, k_proj, v_proj, stream));
+    }
+    uint32_t seq_len() const { return ec_kv_cache_seq_len(h_); }
+    void reset() { check(ec_kv_cache_reset(h_)); }
+    void attention(uint32_t layer_idx, const float* q, float* out, float softmax_scale,
+                   ec_stream_t stream = nullptr) {
+        check(ec_kv_cache_attention(h_, layer_idx, q, out, softmax_scale, stream));
+    }
+    ec_kv_cache* handle() const { return h_; }
+
+private:
+    ec_kv_cache* h_ = nullptr;
+};
+
+}  // namespace gpu
+}  // namespace ec

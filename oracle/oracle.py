@@ -87,6 +87,10 @@ def ref():
         L.ref_attn_destroy.argtypes = [vp]
         L.ref_attn_run.argtypes = [vp, _u32, _i8p, _i8p, _f32p, _f32p, _f32p, _f32p]
         L.ref_attn_run.restype = ctypes.c_int
+        L.ref_attn_load.argtypes = [vp, _u32, _i8p, _i8p, _f32p, _f32p]
+        L.ref_attn_load.restype = ctypes.c_int
+        L.ref_attn_step.argtypes = [vp, _u32, _f32p, _f32p]
+        L.ref_attn_step.restype = ctypes.c_int
         _ref = L
     return _ref
 
@@ -252,3 +256,21 @@ class RefAttention:
         if rc != 0:
             raise ValueError("kv_len must be below the engine's max_seq_len")
         return out.reshape(self.H, self.d)
+
+    def load(self, keys, values, kscales, vscales, kv_len):
+        """Copies a cache in once; step() then attends to it repeatedly."""
+        self._keep = [np.ascontiguousarray(keys, np.int8), np.ascontiguousarray(values, np.int8),
+                      np.ascontiguousarray(kscales, np.float32),
+                      np.ascontiguousarray(vscales, np.float32)]
+        k, v, ks, vs = self._keep
+        if ref().ref_attn_load(self.h, kv_len, _p(k, _i8p), _p(v, _i8p), _p(ks, _f32p),
+                               _p(vs, _f32p)) != 0:
+            raise ValueError("kv_len must be below the engine's max_seq_len")
+        self.kv_len = kv_len
+
+    def step(self, q, out=None):
+        q = np.ascontiguousarray(q, np.float32).reshape(-1)
+        if out is None:
+            out = np.zeros(self.H * self.d, np.float32)
+        ref().ref_attn_step(self.h, self.kv_len, _p(q, _f32p), _p(out, _f32p))
+        return out

@@ -43,6 +43,22 @@ struct CacheTag {
 };
 template struct Expose<CacheTag, &InferenceEngine::kv_cache_>;
 
+struct QProjTag {
+    typedef float* InferenceEngine::*type;
+    friend type get(QProjTag);
+};
+template struct Expose<QProjTag, &InferenceEngine::q_proj_>;
+struct KProjTag {
+    typedef float* InferenceEngine::*type;
+    friend type get(KProjTag);
+};
+template struct Expose<KProjTag, &InferenceEngine::k_proj_>;
+struct VProjTag {
+    typedef float* InferenceEngine::*type;
+    friend type get(VProjTag);
+};
+template struct Expose<VProjTag, &InferenceEngine::v_proj_>;
+
 ModelConfig make_config(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
                         uint32_t num_layers, uint32_t max_seq_len, bool quant) {
     ModelConfig c{};
@@ -109,6 +125,7 @@ void ref_kvcache_layer_ptrs(void* h, uint32_t layer, void** out6) {
 struct RefAttn {
     std::unique_ptr<InferenceEngine> eng;
     uint32_t num_heads, num_kv_heads, head_dim, max_seq_len;
+    float saved_k_scale = 0.0f, saved_v_scale = 0.0f;  // see ref_attn_step
 };
 
 void* ref_attn_create(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
@@ -131,6 +148,17 @@ void* ref_attn_create(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_d
 
 void ref_attn_destroy(void* h) { delete static_cast<RefAttn*>(h); }
 
+// matvec_fp16_fp32 accumulates into its output (src/kernels/matvec.cpp:43) and
+// attention() does not clear the projection buffers first
+// (src/inference.cpp:313-319), so q would carry the previous call's value.
+// Clear them so every call sees q = input.
+static void clear_projections(RefAttn* r) {
+    InferenceEngine* e = r->eng.get();
+    std::memset(e->*get(QProjTag()), 0, sizeof(float) * r->num_heads * r->head_dim);
+    std::memset(e->*get(KProjTag()), 0, sizeof(float) * r->num_kv_heads * r->head_dim);
+    std::memset(e->*get(VProjTag()), 0, sizeof(float) * r->num_kv_heads * r->head_dim);
+}
+
 // Runs the reference's attention loop for one decode step of layer 0 over
 // kv_len cached tokens (layout [pos][num_kv_heads][head_dim], per-head scales
 // [pos][num_kv_heads]).  q: [num_heads*head_dim] unscaled; out: same size.
@@ -149,6 +177,45 @@ int ref_attn_run(void* h, uint32_t kv_len, const int8_t* keys, const int8_t* val
     std::memcpy(l.key_scales, key_scales, kv_len * r->num_kv_heads * sizeof(float));
     std::memcpy(l.val_scales, val_scales, kv_len * r->num_kv_heads * sizeof(float));
     l.seq_len = kv_len;
+    clear_projections(r);
+    (r->eng.get()->*get(AttentionTag()))(0, q, out);
+    return 0;
+}
+
+// Loads kv_len cached tokens once (see ref_attn_run for the layout) ...
+int ref_attn_load(void* h, uint32_t kv_len, const int8_t* keys, const int8_t* values,
+                  const float* key_scales, const float* val_scales) {
+    RefAttn* r = static_cast<RefAttn*>(h);
+    if (kv_len >= r->max_seq_len) return -1;
+    KVCache& cache = *(r->eng.get()->*get(CacheTag()));
+    cache.reset();
+    KVCacheLayer& l = cache.layer(0);
+    const size_t row = static_cast<size_t>(r->num_kv_heads) * r->head_dim;
+    std::memcpy(l.keys_int8, keys, kv_len * row);
+    std::memcpy(l.values_int8, values, kv_len * row);
+    std::memcpy(l.key_scales, key_scales, kv_len * r->num_kv_heads * sizeof(float));
+    std::memcpy(l.val_scales, val_scales, kv_len * r->num_kv_heads * sizeof(float));
+    l.seq_len = kv_len;
+    r->saved_k_scale = l.key_scales[kv_len];
+    r->saved_v_scale = l.val_scales[kv_len];
+    return 0;
+}
+
+// ... then runs one decode step over it.  attention() appends the step's own
+// token at slot kv_len (src/inference.cpp:414); the length is set back so
+// that every step attends to the same kv_len tokens.
+int ref_attn_step(void* h, uint32_t kv_len, const float* q, float* out) {
+    RefAttn* r = static_cast<RefAttn*>(h);
+    if (kv_len >= r->max_seq_len) return -1;
+    KVCache& cache = *(r->eng.get()->*get(CacheTag()));
+    KVCacheLayer& l = cache.layer(0);
+    // The append at the end of the previous step stored a whole-row scale at
+    // key_scales[kv_len] (src/kv_cache.cpp:101), which in the per-head layout
+    // is the scale of token kv_len / num_kv_heads; put the loaded value back.
+    l.key_scales[kv_len] = r->saved_k_scale;
+    l.val_scales[kv_len] = r->saved_v_scale;
+    l.seq_len = kv_len;
+    clear_projections(r);
     (r->eng.get()->*get(AttentionTag()))(0, q, out);
     return 0;
 }

@@ -183,4 +183,6 @@ def test_fused_dequant_dot(cuda):
         out = torch.empty(L, dtype=torch.float32, device="cuda")
         eckv.fused_dequant_dot_int8(_dev(torch, q), _dev(torch, k), _dev(torch, s), out, dim, L)
         want = O.fused_dequant_dot_int8(q, k, s, dim, L)
-        np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-5, atol=1e-4)
+        # fp32 sums in a different order: bound the error by the terms' magnitude
+        mag = (np.abs(k.astype(np.float32)) * s[:, None] * np.abs(q)[None, :]).sum(1)
+        assert np.all(np.abs(out.cpu().numpy() - want) <= 1e-6 * mag * np.sqrt(dim) + 1e-6)

@@ -190,7 +190,7 @@ def test_context_parallel_partials_and_lse_combine(cuda, parts):
     for p in range(parts):
         a, b = bounds[p], bounds[p + 1]
         bc = eckv.BatchCache([b - a], num_kv_heads=4)
-        fill_batch(bc, [(kq[a:b], vq[a:b], ks[a * 4:b * 4], vs[a * 4:b * 4])])
+        fill_batch(bc, [(kq[a:b], vq[a:b], ks[a:b], vs[a:b])])
         bc.decode_partial(qd, po[p], pml[p], 16, W.softmax_scale(D))
     out = torch.empty((1, 16, D), dtype=torch.float32, device="cuda")
     eckv.lse_combine(po, pml, parts, 1, 16, D, out)
