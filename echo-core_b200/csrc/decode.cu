@@ -9,26 +9,30 @@
 // (log2(e) folded into q), with the maximum carried per split.
 //
 // Work decomposition.  One CTA owns one (sequence, chunk of tokens) and all
-// num_kv_heads heads of it, so each K/V tile it stages is one contiguous run
-// of [tokens][num_kv_heads][128] int8 codes: a single 1-D bulk copy (TMA,
-// no multicast) per tile per tensor, plus one for each scale array.  A
-// producer warp streams tiles through a kStages-deep shared-memory ring
-// guarded by mbarriers; 8 consumer warps each own one KV head (and its
-// GROUP query heads) for a 16-token slice of every tile.  Every K and V
+// KV heads of it.  Tiles of 32 tokens stream through a shared-memory ring:
+// per KV head one 2-D TMA copy of the K codes and one of the V codes (a
+// [32 tokens x 128 B] box of the [slot][head][128] cache, 128-byte swizzled),
+// plus one 1-D bulk copy per scale array.  No multicast.  Each KV head has
+// one QK warp and one PV warp; they hand tiles of p' = p * v_scale to each
+// other through a double-buffered slot guarded by mbarriers.  Every K and V
 // byte is read from HBM exactly once per step.
 //
-// Consumer inner loops, per lane:
-//   QK: 8 lanes share one token row (16 codes each).  Codes become fp32 with
-//       a byte-permute into the mantissa of 2^23 and one packed subtract;
-//       dots use packed fp32 FMA (fma.rn.f32x2); a transposing butterfly
-//       leaves each lane with one head's full dot.
-//   PV: the same lanes own 16 output dims of every head and accumulate
-//       p'(t) * code(t) with packed FMA, p' = p * v_scale (fused scale).
-// Online softmax rescales the accumulators only when a head's running
-// maximum grows by more than 2^8 (exact: numerator and denominator always
-// share the same reference maximum).
+// Both contractions run on the tensor cores as int8 mma.sync m16n8k32 with
+// exact integer accumulation:
+//   scores  S[t][h] = K_codes[t][:] . q_h      A = K codes (unconverted),
+//           B = q_h split exactly into digits q_int = 65536*d0 + 256*d1 + d2
+//           of a 24-bit per-head fixed-point scale (d0 signed, d1/d2 bytes);
+//   output  O[h][d] += sum_t p'[h][t] * V_codes[t][d]
+//                                              A = V codes transposed by
+//           ldmatrix.trans.b8, B = p' per (head, tile) split into two bytes of
+//           a 15-bit power-of-two scale.
+// Integer sums are recombined in fp32.  The online softmax rescales only when
+// a head's running maximum grows by more than 2^8 (exact: numerator and
+// denominator always share the same reference maximum).
 #include <cmath>
 #include <cstdint>
+
+#include <cuda.h>
 
 #include "ec_common.cuh"
 #include "ec_internal.h"
@@ -37,39 +41,29 @@ namespace ec {
 namespace {
 
 constexpr int D = 128;
-constexpr int kPairs = 8;                          // QK warp + PV warp pairs
-constexpr int kQkWarps = kPairs;
-constexpr int kConsumerWarps = 2 * kPairs;         // QK warps 0..7, PV warps 8..15
-constexpr int kThreads = kConsumerWarps * 32;      // 16 warps: 4 per SM sub-partition
-constexpr int kStages = 5;
-constexpr int kPBufs = 2;                          // P tiles in flight per pair
-// QK warp 0 also issues the bulk copies.  At its tile i it issues tile
-// i + kPrefetch, whose stage was last used by tile i - kPBufs: every warp has
-// released that stage by the time warp 0 holds the P buffer of tile i.
-constexpr int kPrefetch = kStages - kPBufs;
+constexpr int T = 32;                              // tokens per tile
+constexpr int kPBufs = 2;                          // p' tiles in flight per head
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyRescale = 8.0f;
 constexpr unsigned kFull = 0xffffffffu;
 
 template <int HKV>
 struct Geo {
-    static constexpr int T = 128 / HKV;                 // tokens per tile
-    static constexpr int WPH = kPairs / HKV;            // pairs per KV head
-    static constexpr int ROWB = HKV * D;                // code bytes per token row
-    static constexpr int KV_TILE = T * ROWB;            // 16 KB
-    static constexpr int SC_TILE = T * HKV * 4;         // 512 B
-    static constexpr int STAGE = 2 * KV_TILE + 2 * SC_TILE;
-    // per pair and P buffer: P'[16 tokens][4 heads] then corr[4]
-    static constexpr int PSLOT = 16 * 4 + 4;
-    static constexpr int PBUF = kPairs * kPBufs * PSLOT * 4;
-    static constexpr int NBARS = 2 * kStages + 2 * kPairs * kPBufs;
-    static constexpr int SMEM = kStages * STAGE + PBUF + NBARS * 8;
-    static_assert(T == WPH * 16, "each pair owns 16 tokens of a tile");
+    static constexpr int kWarps = 2 * HKV;                  // QK warps 0..HKV-1, PV warps HKV..
+    static constexpr int kConsumerThreads = kWarps * 32;
+    static constexpr int kThreads = kConsumerThreads + 32;   // + one producer warp
+    static constexpr int HEAD_TILE = T * D;                 // 4 KB: one head's [32][128] box
+    static constexpr int KV_TILE = HKV * HEAD_TILE;
+    static constexpr int SC_TILE = T * HKV * 4;
+    static constexpr int STAGE = 2 * KV_TILE + 2 * SC_TILE; // multiple of 1024
+    static constexpr int kStages = HKV <= 4 ? 6 : 3;
+    static constexpr int PSLOT = 4 * T + 4;                 // p'[4 heads][32 tokens], corr[4]
+    static constexpr int PBUF = HKV * kPBufs * PSLOT * 4;
+    static constexpr int NBARS = 2 * kStages + 2 * HKV * kPBufs;
+    static constexpr int SMEM = 1024 /*alignment slack*/ + kStages * STAGE + PBUF + NBARS * 8;
+    static_assert(STAGE % 1024 == 0, "swizzled boxes need 1024-byte aligned stages");
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
-
-__device__ __forceinline__ void consumer_barrier() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-}
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
@@ -77,60 +71,43 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                  : "memory");
 }
 
-template <int N>
-__device__ __forceinline__ float pick(const float (&v)[N], int i) {
-    float r = v[0];
-#pragma unroll
-    for (int k = 1; k < N; ++k) r = (i == k) ? v[k] : r;
-    return r;
+// 2-D tiled TMA load (no multicast) with an L2 eviction hint.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
 }
 
-// Within an 8-lane token group (c = lane & 7), each lane ends the score
-// reduction holding the dot of head head_of_lane(c).  To make the reduction a
-// plain butterfly, the lane keeps its GROUP per-head partial dots in the slot
-// order slot k <-> head k ^ head_of_lane(c); the q registers are loaded in
-// that order once, so no select is needed per token.
-template <int GROUP>
-__device__ __forceinline__ int head_of_lane(int c) {
-    if constexpr (GROUP == 4) return ((c >> 2) & 1) * 2 + ((c >> 1) & 1);
-    else if constexpr (GROUP == 2) return (c >> 2) & 1;
-    else return 0;
-}
-template <int GROUP>
-__device__ __forceinline__ int lane_of_head(int j) {
-    if constexpr (GROUP == 4) return (j >> 1) * 4 + (j & 1) * 2;
-    else if constexpr (GROUP == 2) return j * 4;
-    else return 0;
-}
-template <int GROUP>
-__device__ __forceinline__ bool writer_lane(int c) {
-    if constexpr (GROUP == 4) return (c & 1) == 0;
-    else if constexpr (GROUP == 2) return (c & 3) == 0;
-    else return c == 0;
+// Byte offset of 16-byte chunk `c` of row `r` inside a 128-byte-swizzled box.
+__device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <int GROUP>
-__device__ __forceinline__ float butterfly(float (&v)[GROUP]) {
-    if constexpr (GROUP == 4) {
-        v[0] += __shfl_xor_sync(kFull, v[2], 4);
-        v[1] += __shfl_xor_sync(kFull, v[3], 4);
-        v[0] += __shfl_xor_sync(kFull, v[1], 2);
-    } else if constexpr (GROUP == 2) {
-        v[0] += __shfl_xor_sync(kFull, v[1], 4);
-        v[0] += __shfl_xor_sync(kFull, v[0], 2);
-    } else {
-        v[0] += __shfl_xor_sync(kFull, v[0], 4);
-        v[0] += __shfl_xor_sync(kFull, v[0], 2);
-    }
-    v[0] += __shfl_xor_sync(kFull, v[0], 1);
-    return v[0];
+__device__ __forceinline__ void mma_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void codes16_to_f2(const uint4 w, float2 (&f)[8]) {
-    i8x4_to_f2x2(w.x, f[0], f[1]);
-    i8x4_to_f2x2(w.y, f[2], f[3]);
-    i8x4_to_f2x2(w.z, f[4], f[5]);
-    i8x4_to_f2x2(w.w, f[6], f[7]);
+// 16x16 int8 block, rows = tokens, transposed: lane (g, t) gets the bytes of
+// rows 4t..4t+3 at columns g (r0) and g + 8 (r1).
+__device__ __forceinline__ void ldmatrix_t_b8(uint32_t& r0, uint32_t& r1, const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m16n16.x1.trans.shared.b8 {%0, %1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(smem_addr(row_addr)));
 }
 
 __device__ __forceinline__ bool load_entry(const DecodeArgs& a, int s, int32_t& off, int32_t& cap,
@@ -163,43 +140,55 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
     return __all_sync(kFull, mbar_wait(bar, parity));
 }
 
+__device__ __forceinline__ void consumer_barrier(int threads) {
+    asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+
 // Issues tile j of the chunk into stage j % kStages (warp-collective; lane 0
-// drives the bulk copies).  Waits, bounded, until every consumer warp has
-// released the stage's previous tile.  Returns false on a timeout.
+// drives the copies).  Waits, bounded, until every consumer warp has released
+// the stage's previous tile.  Returns false on a timeout.
 template <int HKV>
-__device__ __forceinline__ bool issue_tile(const DecodeArgs& a, uint8_t* stages, uint64_t* full,
-                                           uint64_t* empty, int j, int n, size_t slot0,
+__device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMap* tk,
+                                           const CUtensorMap* tv, uint8_t* stages, uint64_t* full,
+                                           uint64_t* empty, int j, int n, int64_t slot0,
                                            uint64_t pol, int lane) {
     using G = Geo<HKV>;
-    const int s = j % kStages;
+    const int s = j % G::kStages;
     bool ok = true;
-    if (lane == 0 && j >= kStages) ok = mbar_wait(&empty[s], ((j / kStages) - 1) & 1);
+    if (lane == 0 && j >= G::kStages) ok = mbar_wait(&empty[s], ((j / G::kStages) - 1) & 1);
     ok = __shfl_sync(kFull, ok, 0);
     if (!ok) return false;
-    const int ntok = min(G::T, n - j * G::T);
-    const size_t slot = slot0 + (size_t)j * G::T;
+    const int ntok = min(T, n - j * T);
+    const int64_t slot = slot0 + (int64_t)j * T;
     uint8_t* st = stages + s * G::STAGE;
-    const uint32_t kvb = (uint32_t)ntok * G::ROWB;
+    // the boxes always land whole (rows past the tensor are zero-filled)
+    const uint32_t kvb = 2u * G::KV_TILE;
     if (!a.row_scales) {
         if (lane == 0) {
             const uint32_t scb = (uint32_t)ntok * HKV * 4;
-            mbar_arrive_expect_tx(&full[s], 2 * kvb + 2 * scb);
-            bulk_g2s_hint(st, a.keys + slot * G::ROWB, kvb, &full[s], pol);
-            bulk_g2s_hint(st + G::KV_TILE, a.values + slot * G::ROWB, kvb, &full[s], pol);
+            mbar_arrive_expect_tx(&full[s], kvb + 2 * scb);
+#pragma unroll
+            for (int g = 0; g < HKV; ++g) {
+                tma_load_2d(st + g * G::HEAD_TILE, tk, g * D, (int)slot, &full[s], pol);
+                tma_load_2d(st + G::KV_TILE + g * G::HEAD_TILE, tv, g * D, (int)slot, &full[s], pol);
+            }
             bulk_g2s_hint(st + 2 * G::KV_TILE, a.key_scales + slot * HKV, scb, &full[s], pol);
-            bulk_g2s_hint(st + 2 * G::KV_TILE + G::SC_TILE, a.val_scales + slot * HKV, scb,
-                          &full[s], pol);
+            bulk_g2s_hint(st + 2 * G::KV_TILE + G::SC_TILE, a.val_scales + slot * HKV, scb, &full[s],
+                          pol);
         }
     } else {
         // ROW scales: one fp32 per token, broadcast into the per-head tile
         // layout with plain loads; the arrive releases them to the consumers.
         if (lane == 0) {
-            mbar_expect_tx(&full[s], 2 * kvb);
-            bulk_g2s_hint(st, a.keys + slot * G::ROWB, kvb, &full[s], pol);
-            bulk_g2s_hint(st + G::KV_TILE, a.values + slot * G::ROWB, kvb, &full[s], pol);
+            mbar_expect_tx(&full[s], kvb);
+#pragma unroll
+            for (int g = 0; g < HKV; ++g) {
+                tma_load_2d(st + g * G::HEAD_TILE, tk, g * D, (int)slot, &full[s], pol);
+                tma_load_2d(st + G::KV_TILE + g * G::HEAD_TILE, tv, g * D, (int)slot, &full[s], pol);
+            }
         }
         float* ks = reinterpret_cast<float*>(st + 2 * G::KV_TILE);
-        float* vs = ks + G::T * HKV;
+        float* vs = ks + T * HKV;
         for (int t = lane; t < ntok; t += 32) {
             const float kv = a.key_scales[slot + t];
             const float vv = a.val_scales[slot + t];
@@ -216,17 +205,21 @@ __device__ __forceinline__ bool issue_tile(const DecodeArgs& a, uint8_t* stages,
 }
 
 template <int HKV, int GROUP>
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(Geo<HKV>::kThreads, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                  const __grid_constant__ CUtensorMap tmap_v, const DecodeArgs a) {
     using G = Geo<HKV>;
-    extern __shared__ __align__(1024) uint8_t smem[];
+    constexpr int S = G::kStages;
+    extern __shared__ uint8_t smem_raw[];
     __shared__ int fail_flag;
-    uint8_t* stages = smem;
-    float* pbuf = reinterpret_cast<float*>(smem + kStages * G::STAGE);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * G::STAGE + G::PBUF);
-    uint64_t* full = bars;                           // [kStages]  TMA -> consumers
-    uint64_t* empty = full + kStages;                // [kStages]  consumers -> producer
-    uint64_t* p_full = empty + kStages;              // [kPairs][kPBufs]  QK -> PV
-    uint64_t* p_empty = p_full + kPairs * kPBufs;    // [kPairs][kPBufs]  PV -> QK
+    uint8_t* stages = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* pbuf = reinterpret_cast<float*>(stages + S * G::STAGE);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stages + S * G::STAGE + G::PBUF);
+    uint64_t* full = bars;                           // [S]        TMA -> warps
+    uint64_t* empty = full + S;                      // [S]        warps -> producer
+    uint64_t* p_full = empty + S;                    // [HKV][kPBufs]  QK -> PV
+    uint64_t* p_empty = p_full + HKV * kPBufs;       // [HKV][kPBufs]  PV -> QK
 
     const int seq = blockIdx.y;
     const int chunk = blockIdx.x;
@@ -242,16 +235,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a)
         return;
     }
     const int n = min(a.chunk_tokens, len - t0);
-    const int ntiles = (n + G::T - 1) / G::T;
+    const int ntiles = (n + T - 1) / T;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], G::kWarps);
         }
-        for (int i = 0; i < kPairs * kPBufs; ++i) {
+        for (int i = 0; i < HKV * kPBufs; ++i) {
             mbar_init(&p_full[i], 1);
             mbar_init(&p_empty[i], 1);
         }
@@ -260,47 +253,46 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a)
     }
     __syncthreads();
 
-    const int pair = warp % kPairs;
-    const bool is_qk = warp < kQkWarps;
-    const int g = pair / G::WPH;      // KV head
-    const int sw = pair % G::WPH;     // which 16-token slice of each tile
-    const int c = lane & 7;           // 16-byte column of the 128-byte head row
-    const int tq = lane >> 3;         // token within a 4-token pass / PV row group
-    const int hsel = head_of_lane<GROUP>(c);
-    float* pslots = pbuf + pair * kPBufs * G::PSLOT;
+    if (warp == G::kWarps) {
+        // ============================================================ producer
+        // Keeps the ring full: refills a stage as soon as every consumer warp
+        // has released it, independent of the consumers' own progress.
+        const int64_t slot0 = (int64_t)off + t0;
+        const uint64_t pol = l2_policy_evict_first();
+        for (int j = 0; j < ntiles; ++j) {
+            if (!issue_tile<HKV>(a, &tmap_k, &tmap_v, stages, full, empty, j, n, slot0, pol, lane)) {
+                if (lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
+                break;
+            }
+        }
+        return;
+    }
+
+    const bool is_qk = warp < HKV;
+    const int g = is_qk ? warp : warp - HKV;        // KV head of this warp
+    const int gid = lane >> 2;
+    const int t4 = lane & 3;
+    const bool head_live = t4 < GROUP;              // accumulator columns belong to head t4
+    float* pslots = pbuf + g * kPBufs * G::PSLOT;
     bool failed = false;
-    float* mo = reinterpret_cast<float*>(stages);                 // merge area, [8][GROUP][128]
-    float* mm = mo + kPairs * GROUP * D;                           // [8][GROUP]
-    float* ml = mm + kPairs * GROUP;                               // [8][GROUP]
+    // merge area (reused stage memory) for the final (m, l, O) per head
+    float* mo = reinterpret_cast<float*>(stages);    // [HKV][GROUP][128]
+    float* mm = mo + HKV * GROUP * D;                // [HKV][GROUP]
+    float* ml = mm + HKV * GROUP;                    // [HKV][GROUP]
 
     if (is_qk) {
-        // ======================================================== QK warps
-        // Scores of this pair's 16 tokens x GROUP query heads on the tensor
-        // cores: mma.sync m16n8k32 with the int8 K codes as A (rows = tokens,
-        // unconverted) and q as B, split exactly into three digits
-        // q_int = 65536*d0 + 256*d1 + d2 (d0 signed, d1/d2 unsigned bytes) of a
-        // per-head 24-bit fixed-point scale.  Integer accumulation is exact;
-        // the digits are recombined in fp32.  The contraction order over the
-        // 128 dims is permuted (thread t4 holds dims [32*t4, 32*t4+32) of its
-        // rows), identically for A and B.
-        const bool producer = warp == 0;
-        const size_t slot0 = (size_t)off + t0;
-        const uint64_t pol = l2_policy_evict_first();
-        if (producer) {
-            for (int j = 0; j < kPrefetch && j < ntiles; ++j)
-                issue_tile<HKV>(a, stages, full, empty, j, n, slot0, pol, lane);
-        }
-        const int gid = lane >> 2;    // mma group: token row gid (and gid + 8)
-        const int t4 = lane & 3;      // thread in group: query head t4's column pair
-        // --- q digits as B fragments (n = gid <-> (head gid>>1, digit))
-        uint32_t b_hi[4][2], b_lo[4][2];   // n-tile 0: d0 (s8); n-tile 1: d1 | d2 (u8)
-        float sq_own;                      // dequant scale of head gid>>1
+        // ================================================================ QK
+        // q as B fragments: column n = gid <-> (head gid >> 1, digit), thread
+        // t4 holds dims [32*t4, 32*t4 + 32), k-step j covers 8 of them.
+        uint32_t b_hi[4][2], b_lo[4][2];
+        float sq_own;
         {
             const int hq = gid >> 1;
             const bool live = hq < GROUP;
+            const float* qp =
+                a.q + ((size_t)seq * a.num_heads + g + HKV * (live ? hq : 0)) * D + 32 * t4;
             float qv[32];
             float amax = 0.0f;
-            const float* qp = a.q + ((size_t)seq * a.num_heads + g + HKV * (live ? hq : 0)) * D + 32 * t4;
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const float4 v = reinterpret_cast<const float4*>(qp)[e];
@@ -318,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a)
             sq_own = amax > 0.0f ? __fdiv_rn(amax, kQMax) : 0.0f;
             const bool odd = gid & 1;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < 4; ++j)
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     uint32_t w0 = 0, w1 = 0;
@@ -334,58 +326,47 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a)
                     b_hi[j][half] = w0;
                     b_lo[j][half] = w1;
                 }
-            }
         }
-        // scale of the head this thread's accumulator columns belong to (t4)
         const float sq = __shfl_sync(kFull, sq_own, (2 * t4) << 2);
-        const bool head_live = t4 < GROUP;
         const float c16 = 65536.0f * sq, c8 = 256.0f * sq;
         float m_run = -INFINITY;      // running max of head t4 (log2 units)
         float l_part = 0.0f;          // this thread's share of head t4's sum
 
         for (int i = 0; i < ntiles; ++i) {
-            const int s = i % kStages;
+            const int s = i % S;
             const int b = i % kPBufs;
-            if (!warp_wait(&full[s], (i / kStages) & 1)) { failed = true; break; }
+            if (!warp_wait(&full[s], (i / S) & 1)) { failed = true; break; }
             const uint8_t* st = stages + s * G::STAGE;
-            const int8_t* kt = reinterpret_cast<const int8_t*>(st);
+            const uint8_t* kt = st + g * G::HEAD_TILE;
             const float* kst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE);
-            const float* vst = kst + G::T * HKV;
-            const int valid = n - i * G::T;
+            const float* vst = kst + T * HKV;
+            const int valid = n - i * T;
 
-            const int8_t* r0 = kt + (sw * 16 + gid) * G::ROWB + g * D + 32 * t4;
-            const int8_t* r1 = r0 + 8 * G::ROWB;
-            const uint4 a00 = *reinterpret_cast<const uint4*>(r0);
-            const uint4 a01 = *reinterpret_cast<const uint4*>(r0 + 16);
-            const uint4 a10 = *reinterpret_cast<const uint4*>(r1);
-            const uint4 a11 = *reinterpret_cast<const uint4*>(r1 + 16);
-            const uint32_t w0[8] = {a00.x, a00.y, a00.z, a00.w, a01.x, a01.y, a01.z, a01.w};
-            const uint32_t w1[8] = {a10.x, a10.y, a10.z, a10.w, a11.x, a11.y, a11.z, a11.w};
-            int acc_hi[4] = {0, 0, 0, 0}, acc_lo[4] = {0, 0, 0, 0};
+            float sc[4];   // tokens gid, gid+8, 16+gid, 24+gid of head t4
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                asm volatile(
-                    "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
-                    "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                    : "+r"(acc_hi[0]), "+r"(acc_hi[1]), "+r"(acc_hi[2]), "+r"(acc_hi[3])
-                    : "r"(w0[2 * j]), "r"(w1[2 * j]), "r"(w0[2 * j + 1]), "r"(w1[2 * j + 1]),
-                      "r"(b_hi[j][0]), "r"(b_hi[j][1]));
-                asm volatile(
-                    "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 "
-                    "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                    : "+r"(acc_lo[0]), "+r"(acc_lo[1]), "+r"(acc_lo[2]), "+r"(acc_lo[3])
-                    : "r"(w0[2 * j]), "r"(w1[2 * j]), "r"(w0[2 * j + 1]), "r"(w1[2 * j + 1]),
-                      "r"(b_lo[j][0]), "r"(b_lo[j][1]));
+            for (int mt = 0; mt < 2; ++mt) {
+                const int ra = mt * 16 + gid, rb = ra + 8;
+                const uint4 a00 = *reinterpret_cast<const uint4*>(kt + swz(ra, 2 * t4));
+                const uint4 a01 = *reinterpret_cast<const uint4*>(kt + swz(ra, 2 * t4 + 1));
+                const uint4 a10 = *reinterpret_cast<const uint4*>(kt + swz(rb, 2 * t4));
+                const uint4 a11 = *reinterpret_cast<const uint4*>(kt + swz(rb, 2 * t4 + 1));
+                const uint32_t w0[8] = {a00.x, a00.y, a00.z, a00.w, a01.x, a01.y, a01.z, a01.w};
+                const uint32_t w1[8] = {a10.x, a10.y, a10.z, a10.w, a11.x, a11.y, a11.z, a11.w};
+                int hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    mma_s8s8(hi, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1], b_hi[j][0], b_hi[j][1]);
+                    mma_s8u8(lo, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1], b_lo[j][0], b_lo[j][1]);
+                }
+                // accumulator (row, col): [0] (ra, 2*t4) [1] (ra, 2*t4+1) [2]/[3] row rb
+                const float sa = fmaf((float)hi[0], c16, fmaf((float)lo[0], c8, (float)lo[1] * sq));
+                const float sb = fmaf((float)hi[2], c16, fmaf((float)lo[2], c8, (float)lo[3] * sq));
+                sc[2 * mt] = (head_live && ra < valid) ? sa * kst[ra * HKV + g] : -INFINITY;
+                sc[2 * mt + 1] = (head_live && rb < valid) ? sb * kst[rb * HKV + g] : -INFINITY;
             }
-            // accumulator (row, col): c0 (gid, 2*t4) c1 (gid, 2*t4+1) c2/c3 rows gid+8
-            const int tA = sw * 16 + gid, tB = tA + 8;
-            float sA = fmaf((float)acc_hi[0], c16, fmaf((float)acc_lo[0], c8, (float)acc_lo[1] * sq));
-            float sB = fmaf((float)acc_hi[2], c16, fmaf((float)acc_lo[2], c8, (float)acc_lo[3] * sq));
-            sA = (head_live && tA < valid) ? sA * kst[tA * HKV + g] : -INFINITY;
-            sB = (head_live && tB < valid) ? sB * kst[tB * HKV + g] : -INFINITY;
 
             // online softmax of head t4, base 2, lazy rescale
-            float tm = fmaxf(sA, sB);
+            float tm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
             tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 4));
             tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 8));
             tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 16));
@@ -395,145 +376,145 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const DecodeArgs a)
                 m_run = tm;
             }
             l_part *= corr;
-            const float pA = sA == -INFINITY ? 0.0f : exp2f(sA - m_run);
-            const float pB = sB == -INFINITY ? 0.0f : exp2f(sB - m_run);
-            l_part += pA + pB;
+            float p[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                p[e] = sc[e] == -INFINITY ? 0.0f : exp2f(sc[e] - m_run);
+                l_part += p[e];
+            }
 
-            if (i >= kPBufs && !warp_wait(&p_empty[pair * kPBufs + b], ((i / kPBufs) - 1) & 1)) {
+            if (i >= kPBufs && !warp_wait(&p_empty[g * kPBufs + b], ((i / kPBufs) - 1) & 1)) {
                 failed = true;
                 break;
             }
-            if (producer && i + kPrefetch < ntiles &&
-                !issue_tile<HKV>(a, stages, full, empty, i + kPrefetch, n, slot0, pol, lane)) {
-                failed = true;
-                break;
-            }
-            float* pw = pslots + b * G::PSLOT;
+            float* pw = pslots + b * G::PSLOT;   // p'[head][token], then corr[head]
             if (head_live) {
-                pw[gid * 4 + t4] = pA == 0.0f ? 0.0f : pA * vst[tA * HKV + g];
-                pw[(gid + 8) * 4 + t4] = pB == 0.0f ? 0.0f : pB * vst[tB * HKV + g];
-                if (gid == 0) pw[64 + t4] = corr;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int tok = (e >> 1) * 16 + (e & 1) * 8 + gid;
+                    pw[t4 * T + tok] = p[e] == 0.0f ? 0.0f : p[e] * vst[tok * HKV + g];
+                }
+                if (gid == 0) pw[4 * T + t4] = corr;
             }
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&p_full[pair * kPBufs + b]);
+                mbar_arrive(&p_full[g * kPBufs + b]);
                 mbar_arrive(&empty[s]);
             }
         }
         l_part += __shfl_xor_sync(kFull, l_part, 4);
         l_part += __shfl_xor_sync(kFull, l_part, 8);
         l_part += __shfl_xor_sync(kFull, l_part, 16);
-        consumer_barrier();   // every warp is done with the stage ring
+        consumer_barrier(G::kConsumerThreads);   // every warp is done with the stage ring
         if (failed) {
             if (lane == 0) fail_flag = 1;
         } else if (gid == 0 && head_live) {
-            mm[pair * GROUP + t4] = m_run;
-            ml[pair * GROUP + t4] = l_part;
+            mm[g * GROUP + t4] = m_run;
+            ml[g * GROUP + t4] = l_part;
         }
     } else {
-        // ======================================================== PV warps
-        float2 acc_o[GROUP][8];
+        // ================================================================ PV
+        // O^T[dim][col] += V^T[dim][token] . P[token][col], col = (head, digit)
+        float acc[8][2];   // head t4, dims 16*mt + gid (+8)
 #pragma unroll
-        for (int j = 0; j < GROUP; ++j)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc_o[j][e] = make_float2(0.f, 0.f);
+        for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = 0.0f;
+        const int hp = gid >> 1;           // head whose p' digits this thread supplies
+        const bool p_live = hp < GROUP;
+        const bool lo_digit = gid & 1;
 
         for (int i = 0; i < ntiles; ++i) {
-            const int s = i % kStages;
+            const int s = i % S;
             const int b = i % kPBufs;
-            if (!warp_wait(&p_full[pair * kPBufs + b], (i / kPBufs) & 1)) { failed = true; break; }
-            if (!warp_wait(&full[s], (i / kStages) & 1)) { failed = true; break; }
-            const int8_t* vt = reinterpret_cast<const int8_t*>(stages + s * G::STAGE) + G::KV_TILE;
+            if (!warp_wait(&p_full[g * kPBufs + b], (i / kPBufs) & 1)) { failed = true; break; }
+            if (!warp_wait(&full[s], (i / S) & 1)) { failed = true; break; }
+            const uint8_t* vt = stages + s * G::STAGE + G::KV_TILE + g * G::HEAD_TILE;
             const float* pw = pslots + b * G::PSLOT;
-            float corr[GROUP];
-            bool resc = false;
-#pragma unroll
-            for (int j = 0; j < GROUP; ++j) {
-                corr[j] = pw[64 + j];
-                resc |= corr[j] != 1.0f;
+
+            // p' digits as B fragments: tokens 4*t4.. (b0) and 16 + 4*t4.. (b1)
+            float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pb = pa;
+            if (p_live) {
+                pa = *reinterpret_cast<const float4*>(pw + hp * T + 4 * t4);
+                pb = *reinterpret_cast<const float4*>(pw + hp * T + 16 + 4 * t4);
             }
-            if (resc) {
+            float pmax = fmaxf(fmaxf(fmaxf(pa.x, pa.y), fmaxf(pa.z, pa.w)),
+                               fmaxf(fmaxf(pb.x, pb.y), fmaxf(pb.z, pb.w)));
+            pmax = fmaxf(pmax, __shfl_xor_sync(kFull, pmax, 1));
+            pmax = fmaxf(pmax, __shfl_xor_sync(kFull, pmax, 2));
+            // power-of-two scale putting the head's largest p' in [2^14, 2^15);
+            // a tile whose p' all lie below 2^-100 (far under the running max,
+            // with l >= 1) contributes nothing representable and is dropped.
+            if (!(pmax >= 0x1p-100f)) {
+                pa = make_float4(0.f, 0.f, 0.f, 0.f);
+                pb = pa;
+                pmax = 0.0f;
+            }
+            const int e = pmax > 0.0f ? ((__float_as_int(pmax) >> 23) & 0xff) - 127 : 0;
+            const float up = __int_as_float((127 + 14 - e) << 23);
+            const float down = __int_as_float((127 - 14 + e) << 23);
+            uint32_t bw0 = 0, bw1 = 0;
+            {
+                const float va[4] = {pa.x, pa.y, pa.z, pa.w};
+                const float vb[4] = {pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-                for (int j = 0; j < GROUP; ++j) {
-                    const float2 cj = make_float2(corr[j], corr[j]);
+                for (int x = 0; x < 4; ++x) {
+                    const uint32_t qa = (uint32_t)__float2int_rn(va[x] * up);
+                    const uint32_t qb = (uint32_t)__float2int_rn(vb[x] * up);
+                    bw0 |= (lo_digit ? (qa & 0xffu) : (qa >> 8)) << (8 * x);
+                    bw1 |= (lo_digit ? (qb & 0xffu) : (qb >> 8)) << (8 * x);
+                }
+            }
+            const float sp = __shfl_sync(kFull, down, (2 * t4) << 2);
+            float corr = 1.0f;
+            if (head_live) corr = pw[4 * T + t4];
+            if (__any_sync(kFull, corr != 1.0f)) {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) acc_o[j][e] = __fmul2_rn(acc_o[j][e], cj);
+                for (int mt = 0; mt < 8; ++mt) {
+                    acc[mt][0] *= corr;
+                    acc[mt][1] *= corr;
                 }
             }
 #pragma unroll
-            for (int it = 0; it < 4; ++it) {
-                const int tw = it * 4 + tq;
-                const int tt = sw * 16 + tw;
-                float pp[4];
-                if constexpr (GROUP == 4) {
-                    const float4 p4 = *reinterpret_cast<const float4*>(pw + tw * 4);
-                    pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
-                } else if constexpr (GROUP == 2) {
-                    const float2 p2 = *reinterpret_cast<const float2*>(pw + tw * 4);
-                    pp[0] = p2.x; pp[1] = p2.y;
-                } else {
-                    pp[0] = pw[tw * 4];
-                }
-                const uint4 w = *reinterpret_cast<const uint4*>(vt + tt * G::ROWB + g * D + 16 * c);
-                float2 vf[8];
-                codes16_to_f2(w, vf);
-#pragma unroll
-                for (int j = 0; j < GROUP; ++j) {
-                    const float2 pj = make_float2(pp[j], pp[j]);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) acc_o[j][e] = __ffma2_rn(pj, vf[e], acc_o[j][e]);
-                }
+            for (int mt = 0; mt < 8; ++mt) {
+                // 16x16 blocks of V (tokens x dims 16*mt..): rows from lanes 0-15
+                const int r = lane & 15;
+                uint32_t x0, x1, y0, y1;
+                ldmatrix_t_b8(x0, x1, vt + swz(r, mt));
+                ldmatrix_t_b8(y0, y1, vt + swz(16 + r, mt));
+                int d[4] = {0, 0, 0, 0};
+                mma_s8u8(d, x0, x1, y0, y1, bw0, bw1);
+                // d: (dim 16mt+gid, col 2t4 = hi digit of head t4), (.., lo), rows +8
+                acc[mt][0] = fmaf((float)(d[0] * 256 + d[1]), sp, acc[mt][0]);
+                acc[mt][1] = fmaf((float)(d[2] * 256 + d[3]), sp, acc[mt][1]);
             }
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&p_empty[pair * kPBufs + b]);
+                mbar_arrive(&p_empty[g * kPBufs + b]);
                 mbar_arrive(&empty[s]);
             }
         }
-        // reduce the four row groups of the warp
-#pragma unroll
-        for (int j = 0; j < GROUP; ++j)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                float2 v = acc_o[j][e];
-                v.x += __shfl_xor_sync(kFull, v.x, 8);
-                v.y += __shfl_xor_sync(kFull, v.y, 8);
-                v.x += __shfl_xor_sync(kFull, v.x, 16);
-                v.y += __shfl_xor_sync(kFull, v.y, 16);
-                acc_o[j][e] = v;
-            }
-        consumer_barrier();   // every warp is done with the stage ring
+        consumer_barrier(G::kConsumerThreads);   // every warp is done with the stage ring
         if (failed) {
             if (lane == 0) fail_flag = 1;
-        } else if (tq == 0) {
+        } else if (head_live) {
 #pragma unroll
-            for (int j = 0; j < GROUP; ++j)
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    *reinterpret_cast<float2*>(mo + (pair * GROUP + j) * D + 16 * c + 2 * e) = acc_o[j][e];
+            for (int mt = 0; mt < 8; ++mt) {
+                mo[(g * GROUP + t4) * D + 16 * mt + gid] = acc[mt][0];
+                mo[(g * GROUP + t4) * D + 16 * mt + gid + 8] = acc[mt][1];
+            }
         }
     }
-    consumer_barrier();
+    consumer_barrier(G::kConsumerThreads);
     if (fail_flag) return;
 
-    // ---- merge the WPH pairs of each KV head and write the result
+    // ---- write the chunk's state (or the final output when unsplit)
     const int H = a.num_heads;
-    for (int o = threadIdx.x; o < HKV * GROUP * D; o += kConsumerWarps * 32) {
+    for (int o = threadIdx.x; o < HKV * GROUP * D; o += G::kConsumerThreads) {
         const int d = o % D;
-        const int hl = o / D;
+        const int hl = o / D;                 // g2 * GROUP + j
         const int g2 = hl / GROUP, j = hl % GROUP;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w2 = 0; w2 < G::WPH; ++w2) M = fmaxf(M, mm[(g2 * G::WPH + w2) * GROUP + j]);
-        float so = 0.0f, sl = 0.0f;
-#pragma unroll
-        for (int w2 = 0; w2 < G::WPH; ++w2) {
-            const int w = g2 * G::WPH + w2;
-            const float mw = mm[w * GROUP + j];
-            const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
-            so += f * mo[(w * GROUP + j) * D + d];
-            sl += f * ml[w * GROUP + j];
-        }
+        const float M = mm[hl];
+        const float so = mo[hl * D + d];
+        const float sl = ml[hl];
         const int h = g2 + HKV * j;
         if (direct) {
             const size_t oi = ((size_t)seq * H + h) * D + d;
@@ -622,22 +603,58 @@ cudaError_t launch_decode_t(const DecodeArgs& a, const DecodePlan& plan, cudaStr
         if (e != cudaSuccess) return e;
         attr_done |= bit;
     }
+    CUtensorMap mk, mv;
+    if ((e = make_code_map(&mk, a.keys, HKV, a.total_slots)) != cudaSuccess) return e;
+    if ((e = make_code_map(&mv, a.values, HKV, a.total_slots)) != cudaSuccess) return e;
     dim3 grid(plan.max_chunks, a.num_seqs);
-    decode_kernel<HKV, GROUP><<<grid, kThreads, G::SMEM, st>>>(a);
+    decode_kernel<HKV, GROUP><<<grid, G::kThreads, G::SMEM, st>>>(mk, mv, a);
     return cudaGetLastError();
 }
 
 }  // namespace
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Tensor map over [total_slots][hkv * 128] int8 codes; box = one head's 128
+// bytes x 32 tokens, 128-byte swizzle.
+cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t total_slots) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)hkv * D, (cuuint64_t)total_slots};
+    const cuuint64_t strides[1] = {(cuuint64_t)hkv * D};
+    const cuuint32_t box[2] = {D, T};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms) {
-    DecodePlan best{32, 1};
+    DecodePlan best{T, 1};
     if (max_seq_len <= 0 || num_seqs <= 0) return best;
-    const int gran = 32;
-    const int tiles = (max_seq_len + gran - 1) / gran;
+    const int tiles = (max_seq_len + T - 1) / T;
     double best_cost = 1e300;
     const int kmax = tiles < 256 ? tiles : 256;
     for (int k = 1; k <= kmax; ++k) {
-        const int chunk = ((tiles + k - 1) / k) * gran;
+        const int chunk = ((tiles + k - 1) / k) * T;
         const int kk = (max_seq_len + chunk - 1) / chunk;
         const long long ctas = (long long)num_seqs * kk;
         const long long waves = (ctas + num_sms - 1) / num_sms;

@@ -324,6 +324,8 @@ static int check_batch(const ec_kv_batch* b, const char* who) {
         !aligned16(b->val_scales))
         return fail(EC_ERR_MISALIGNED, "%s: cache buffers must be 16-byte aligned", who);
     if (b->num_seqs > 65535u) return fail(EC_ERR_UNSUPPORTED, "%s: more than 65535 sequences", who);
+    if (b->total_slots >= (1ull << 31))
+        return fail(EC_ERR_UNSUPPORTED, "%s: total_slots must be below 2^31", who);
     if (b->max_seq_len > 0x7fffffffu) return fail(EC_ERR_INVALID_ARGUMENT, "%s: max_seq_len too large", who);
     return EC_OK;
 }

@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace ec {
@@ -67,6 +68,9 @@ size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads);
 // Returns cudaErrorInvalidValue for a shape outside the envelope.
 cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan, void* ws,
                           cudaStream_t st);
+// Tensor map over [total_slots][hkv * 128] int8 codes with a 128-byte x
+// 32-token box, 128-byte swizzle.
+cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t total_slots);
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
                                int num_seqs, int num_heads, float* out, cudaStream_t st);
 
