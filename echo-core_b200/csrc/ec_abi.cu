@@ -51,6 +51,8 @@ cudaStream_t as_stream(ec_stream_t s) { return reinterpret_cast<cudaStream_t>(s)
 
 }  // namespace
 
+int ec::set_last_error(int status, const char* msg) { return fail(status, "%s", msg); }
+
 struct ec_kv_cache {
     ec_model_config cfg;
     int scale_mode;

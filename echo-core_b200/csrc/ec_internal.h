@@ -71,6 +71,8 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
 // Tensor map over [total_slots][hkv * 128] int8 codes with a 128-byte x
 // 32-token box, 128-byte swizzle.
 cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t total_slots);
+// Records `msg` as the calling thread's ec_last_error() text; returns status.
+int set_last_error(int status, const char* msg);
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
                                int num_seqs, int num_heads, float* out, cudaStream_t st);
 

@@ -48,7 +48,7 @@ EXPORTS = (
     "ec_kv_cache_create", "ec_kv_cache_destroy", "ec_kv_cache_layer", "ec_kv_cache_append",
     "ec_kv_cache_seq_len", "ec_kv_cache_reset", "ec_kv_cache_attention",
     "ec_kv_batch_append", "ec_decode_workspace_size", "ec_decode_attention",
-    "ec_decode_attention_partial", "ec_lse_combine",
+    "ec_decode_attention_partial", "ec_lse_combine", "ec_decode_attention_noalloc",
 )
 
 
@@ -119,6 +119,7 @@ def lib() -> ctypes.CDLL:
             "ec_decode_attention_partial": ([ctypes.POINTER(KVBatch), vp, vp, vp, u32, f, vp,
                                              ctypes.c_size_t, vp], i32),
             "ec_lse_combine": ([vp, vp, u32, u32, u32, u32, vp, vp], i32),
+            "ec_decode_attention_noalloc": ([ctypes.POINTER(KVBatch), vp, vp, u32, f, vp], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -223,6 +223,25 @@ EC_API int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t nu
                    uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim, float* out,
                    ec_stream_t stream);
 
+/* No counterpart in the reference (which has no device memory at all): this
+ * entry point exists for callers that cannot allocate device memory when they
+ * run decode -- code running where cudaMalloc is not allowed (a host callback
+ * or hook, where a blocking, device-synchronising allocation would stall or
+ * deadlock), or a runtime that carved up its memory once at start-up and may
+ * not grow it.  Same inputs, outputs and results as ec_decode_attention, but
+ * the split-K workspace is a fixed 16 MiB array built into the library, so
+ * the caller passes none and no allocation happens.  Every GPU that loads the
+ * library holds that array until the process exits.  A batch whose workspace
+ * would exceed 16 MiB (ec_decode_workspace_size) is rejected with
+ * EC_ERR_WORKSPACE and a message in ec_last_error(); nothing is launched.
+ * The first call on each device looks up the array's address, so make it
+ * before any stream capture.  All calls share the array: calls whose kernels
+ * can overlap on the GPU (different streams, no ordering between them) race
+ * and corrupt each other's results. */
+EC_API int ec_decode_attention_noalloc(const ec_kv_batch* batch, const float* q, float* out,
+                                       uint32_t num_heads, float softmax_scale,
+                                       ec_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif
