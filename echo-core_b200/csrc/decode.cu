@@ -604,8 +604,8 @@ cudaError_t launch_decode_t(const DecodeArgs& a, const DecodePlan& plan, cudaStr
         attr_done |= bit;
     }
     CUtensorMap mk, mv;
-    if ((e = make_code_map(&mk, a.keys, HKV, a.total_slots)) != cudaSuccess) return e;
-    if ((e = make_code_map(&mv, a.values, HKV, a.total_slots)) != cudaSuccess) return e;
+    if ((e = make_code_map(&mk, a.keys, HKV, a.total_slots, T)) != cudaSuccess) return e;
+    if ((e = make_code_map(&mv, a.values, HKV, a.total_slots, T)) != cudaSuccess) return e;
     dim3 grid(plan.max_chunks, a.num_seqs);
     decode_kernel<HKV, GROUP><<<grid, G::kThreads, G::SMEM, st>>>(mk, mv, a);
     return cudaGetLastError();
@@ -633,13 +633,14 @@ static EncodeTiledFn encode_fn() {
 }
 
 // Tensor map over [total_slots][hkv * 128] int8 codes; box = one head's 128
-// bytes x 32 tokens, 128-byte swizzle.
-cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t total_slots) {
+// bytes x box_rows tokens, 128-byte swizzle.
+cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t total_slots,
+                          int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
     const cuuint64_t dims[2] = {(cuuint64_t)hkv * D, (cuuint64_t)total_slots};
     const cuuint64_t strides[1] = {(cuuint64_t)hkv * D};
-    const cuuint32_t box[2] = {D, T};
+    const cuuint32_t box[2] = {D, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides,
                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -422,6 +422,38 @@ int ec_decode_attention_partial(const ec_kv_batch* b, const float* q, float* par
                          workspace_bytes, ec::kPartial, stream, "decode_attention_partial");
 }
 
+int ec_prefill_attention(const ec_kv_batch* b, const float* q, float* out, uint32_t n_new,
+                         uint32_t num_heads, float softmax_scale, ec_stream_t stream) {
+    int rc = check_batch(b, "prefill_attention");
+    if (rc) return rc;
+    if (b->num_seqs == 0 || n_new == 0) return EC_OK;
+    if (!q || !out) return fail(EC_ERR_INVALID_ARGUMENT, "prefill_attention: q/out NULL");
+    if (b->head_dim != 128 || b->num_kv_heads == 0 || num_heads == 0 || num_heads % b->num_kv_heads)
+        return fail(EC_ERR_UNSUPPORTED, "prefill_attention: needs head_dim 128 and num_heads a multiple of num_kv_heads");
+    if (!aligned16(q) || !aligned16(out)) return fail(EC_ERR_MISALIGNED, "prefill_attention: q/out not 16-byte aligned");
+    if (n_new > 0x7fffffffu / 128u) return fail(EC_ERR_UNSUPPORTED, "prefill_attention: n_new too large");
+    ec::PrefillArgs a{};
+    a.keys = b->keys;
+    a.values = b->values;
+    a.key_scales = b->key_scales;
+    a.val_scales = b->val_scales;
+    a.seq_offset = b->seq_offset;
+    a.seq_capacity = b->seq_capacity;
+    a.seq_len = b->seq_len;
+    a.err = b->error_word;
+    a.total_slots = b->total_slots;
+    a.q = q;
+    a.out = out;
+    a.num_seqs = (int)b->num_seqs;
+    a.num_heads = (int)num_heads;
+    a.num_kv_heads = (int)b->num_kv_heads;
+    a.n_new = (int)n_new;
+    a.row_scales = b->scale_mode == EC_SCALE_ROW;
+    a.qk_mul = softmax_scale * 1.4426950408889634f;
+    cudaError_t e = ec::launch_prefill(a, as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "prefill_attention launch");
+}
+
 int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t num_parts,
                    uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim, float* out,
                    ec_stream_t stream) {

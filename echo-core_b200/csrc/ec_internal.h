@@ -69,8 +69,26 @@ size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads);
 cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan, void* ws,
                           cudaStream_t st);
 // Tensor map over [total_slots][hkv * 128] int8 codes with a 128-byte x
-// 32-token box, 128-byte swizzle.
-cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t total_slots);
+// box_rows-token box, 128-byte swizzle.
+cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t total_slots,
+                          int box_rows);
+
+struct PrefillArgs {
+    const int8_t* keys;
+    const int8_t* values;
+    const float* key_scales;
+    const float* val_scales;
+    const int32_t* seq_offset;
+    const int32_t* seq_capacity;
+    const int32_t* seq_len;   // lengths after the chunk's append
+    int32_t* err;
+    uint64_t total_slots;
+    const float* q;           // [num_seqs][n_new][num_heads][128] fp32 (cast to bf16 on load)
+    float* out;               // same shape, fp32
+    int num_seqs, num_heads, num_kv_heads, n_new, row_scales;
+    float qk_mul;             // softmax scale * log2(e)
+};
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st);
 // Records `msg` as the calling thread's ec_last_error() text; returns status.
 int set_last_error(int status, const char* msg);
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,

@@ -1,0 +1,587 @@
+// prefill.cu -- causal chunked-prefill attention over the int8 KV cache on the
+// 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// The reference has no chunked prefill: a prompt is fed one token at a time
+// (src/main.cpp:404-405), each token running the decode loop of
+// InferenceEngine::attention (src/inference.cpp:321-392) over the cache as it
+// stands after that token's append.  So query row i of an n_new-token chunk
+// appended after `past` cached tokens attends to slots [0, past + i]; this
+// kernel computes exactly that for all rows at once.
+//
+// One CTA owns 128 query rows of one query head of one sequence (query head h
+// reads KV head h % num_kv_heads, src/inference.cpp:335).  Warp roles:
+//   producer  (warp 8)    2-D TMA of the int8 K and V codes of 128-token
+//                         tiles (128-byte swizzle, no multicast), 2 stages;
+//   converter (warps 4-7) int8 -> bf16 K (K-major) and int8 -> f16 V
+//                         (MN-major), both exact, into 128B-swizzled UMMA
+//                         operand layouts;
+//   MMA       (warp 9)    one thread issues tcgen05.mma: S = Q K^T (bf16 x
+//                         bf16 -> fp32, double-buffered in TMEM) one tile
+//                         ahead of the softmax, then O += P'hi V + P'lo V
+//                         (f16 x f16 -> fp32, accumulated in TMEM);
+//   softmax   (warps 0-3) thread r owns query row r (TMEM lane r): scales S
+//                         by the per-token k-scale, masks causally, runs the
+//                         online softmax in base 2 with lazy rescaling of O in
+//                         TMEM, and writes p' = p * v_scale (the fused
+//                         v-scale) as an f16 hi/lo pair into the P operands.
+// Q is cast to bf16 on load (the queries are bf16-cast); the softmax scale and
+// log2(e) multiply the fp32 scores.  K and V codes are exact in bf16 / f16; p'
+// enters the PV product as an f16 pair hi + lo (two MMAs), about 22 bits, so
+// the only rounding of consequence is Q's bf16 cast (part of the contract).  Every wait is bounded; a timeout raises a CTA-wide abort
+// flag so that every role stops, waits for its own in-flight work and the
+// CTA frees its tensor memory before returning.
+#include <cmath>
+#include <cstdint>
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ec_common.cuh"
+#include "ec_internal.h"
+
+namespace ec {
+namespace {
+
+constexpr int D = 128;
+constexpr int BM = 128;                    // query rows per CTA (TMEM lanes)
+constexpr int BN = 128;                    // kv tokens per tile
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 10 * 32;
+constexpr int ATOM = 128 * 128;            // one [128 rows][128 B] swizzled block
+constexpr int OFF_Q = 0;                   // bf16 Q   : 2 K-blocks (dims 0-63, 64-127)
+constexpr int OFF_K = OFF_Q + 2 * ATOM;    // bf16 K   : 2 K-blocks
+constexpr int OFF_V = OFF_K + 2 * ATOM;    // f16  V   : 2 dim halves, MN-major
+constexpr int OFF_P = OFF_V + 2 * ATOM;    // f16  P'hi: 2 K-blocks (tokens 0-63, 64-127)
+constexpr int OFF_PL = OFF_P + 2 * ATOM;   // f16  P'lo = f16(p' - P'hi), same layout
+constexpr int I8_TILE = BN * 128;          // 16 KB of int8 codes
+constexpr int OFF_I8 = OFF_PL + 2 * ATOM;  // [2 stages][K, V]
+constexpr int OFF_SC = OFF_I8 + 2 * 2 * I8_TILE;   // k-scale * qk_mul [BN], v-scale [BN]
+constexpr int OFF_BAR = OFF_SC + 2 * BN * 4;
+enum {
+    B_KV_FULL = 0, B_KV_EMPTY = 2, B_KC_FULL = 4, B_KC_FREE, B_VC_FULL, B_VC_FREE,
+    B_S_FULL = 8, B_S_FREE = 10, B_P_FULL = 12, B_PV_DONE, B_Q_FULL, B_DRAIN, NBARS
+};
+constexpr int OFF_MISC = OFF_BAR + NBARS * 8;      // [0] tmem base, [1] abort flag
+constexpr int SMEM = 1024 + OFF_MISC + 16;
+static_assert(SMEM <= 227 * 1024, "shared memory budget");
+
+constexpr int TMEM_COLS = 512;             // S0 [0,128), S1 [128,256), O [256,384)
+constexpr int TM_O = 256;
+constexpr float kLazyRescale = 8.0f;
+constexpr unsigned kFull = 0xffffffffu;
+
+// Instruction descriptors (kind::f16, fp32 accumulate, M = 128, N = 128).
+constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | (16u << 17) | (8u << 24);
+constexpr uint32_t kIdescPV = (1u << 4) | (0u << 7) | (0u << 10) | (1u << 16) | (16u << 17) | (8u << 24);
+
+struct Smem {
+    uint8_t* base;
+    __device__ uint64_t* bar(int i) const { return reinterpret_cast<uint64_t*>(base + OFF_BAR) + i; }
+    __device__ volatile int* abort_flag() const {
+        return reinterpret_cast<volatile int*>(base + OFF_MISC) + 1;
+    }
+    __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(base + OFF_MISC); }
+};
+
+// Bounded wait that also gives up as soon as another role has aborted.
+__device__ __forceinline__ bool wait_abortable(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitBudgetCycles) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool warp_wait_abortable(uint64_t* bar, uint32_t parity,
+                                                    volatile int* abort_flag) {
+    return __all_sync(kFull, wait_abortable(bar, parity, abort_flag));
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 128B-swizzled shared-memory matrix descriptor (sm_100 UMMA format).
+__device__ __forceinline__ uint64_t umma_desc(const void* p, uint32_t lbo, uint32_t sbo) {
+    const uint32_t a = smem_addr(p);
+    return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                     bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)accumulate), "r"(0u), "r"(0u),
+        "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+        "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
+        "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])),
+        "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
+        "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
+        "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
+        "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
+        "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of 16-byte chunk c of row r in a [rows][128 B] 128B-swizzled block.
+__device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// int8 code row (a 128-byte swizzled TMA row) -> bf16 K-major row t of Ks.
+__device__ __forceinline__ void convert_k_row(const uint8_t* src, uint8_t* ks, int t) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {   // source chunk c: dims 16c .. 16c+15
+        const uint4 w = *reinterpret_cast<const uint4*>(src + swz(t, c));
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        uint32_t o[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float2 lo, hi;
+            i8x4_to_f2x2(ww[q], lo, hi);
+            o[2 * q] = pack_bf16(lo.x, lo.y);
+            o[2 * q + 1] = pack_bf16(hi.x, hi.y);
+        }
+        uint8_t* blk = ks + (c >> 2) * ATOM;
+        const int cb = 2 * (c & 3);
+        *reinterpret_cast<uint4*>(blk + swz(t, cb)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(blk + swz(t, cb + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+// int8 code row -> f16 MN-major token row t of Vs (two 64-dim halves).
+__device__ __forceinline__ void convert_v_row(const uint8_t* src, uint8_t* vs, int t) {
+    const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);  // 1024 + 128
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 w = *reinterpret_cast<const uint4*>(src + swz(t, c));
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        uint32_t o[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            // biased bytes under the f16 exponent of 1024: 0x64uu = 1024 + u
+            const uint32_t b = ww[q] ^ 0x80808080u;
+            uint32_t h0 = __byte_perm(b, 0x64646464u, 0x5140);   // bytes 0,1
+            uint32_t h1 = __byte_perm(b, 0x64646464u, 0x7362);   // bytes 2,3
+            __half2 x0 = __hsub2(*reinterpret_cast<__half2*>(&h0), bias);
+            __half2 x1 = __hsub2(*reinterpret_cast<__half2*>(&h1), bias);
+            o[2 * q] = *reinterpret_cast<uint32_t*>(&x0);
+            o[2 * q + 1] = *reinterpret_cast<uint32_t*>(&x1);
+        }
+        uint8_t* blk = vs + (c >> 2) * ATOM;
+        const int cb = 2 * (c & 3);
+        *reinterpret_cast<uint4*>(blk + swz(t, cb)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(blk + swz(t, cb + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+__device__ __forceinline__ void named_bar(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                   const __grid_constant__ CUtensorMap tmap_v, const PrefillArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem S{reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                      ~uintptr_t(1023))};
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    // ---- work item: heaviest (latest) query blocks first; the GROUP heads of a
+    // KV head and neighbouring blocks are adjacent for L2 reuse of K/V.
+    const int H = a.num_heads, HKV = a.num_kv_heads, GROUP = H / HKV;
+    const int nqb = (a.n_new + BM - 1) / BM;
+    int idx = blockIdx.x;
+    const int jh = idx % GROUP;  idx /= GROUP;
+    const int qb = nqb - 1 - (idx % nqb);  idx /= nqb;
+    const int g = idx % HKV;
+    const int seq = idx / HKV;
+    const int h = g + HKV * jh;
+
+    const int32_t off = a.seq_offset[seq], cap = a.seq_capacity[seq], len = a.seq_len[seq];
+    const int past = len - a.n_new;
+    if (!(off >= 0 && cap >= 0 && len <= cap && past >= 0 &&
+          (uint64_t)off + (uint64_t)cap <= a.total_slots)) {
+        if (threadIdx.x == 0 && qb == nqb - 1 && jh == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
+        return;
+    }
+    const int q0 = qb * BM;
+    const int rows = min(BM, a.n_new - q0);
+    const int kv_end = past + q0 + rows;              // exclusive
+    const int ntiles = (kv_end + BN - 1) / BN;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(S.bar(B_KV_FULL + i), 1);
+            mbar_init(S.bar(B_KV_EMPTY + i), 4);
+            mbar_init(S.bar(B_S_FULL + i), 1);
+            mbar_init(S.bar(B_S_FREE + i), 4);
+        }
+        mbar_init(S.bar(B_KC_FULL), 4);
+        mbar_init(S.bar(B_KC_FREE), 1);
+        mbar_init(S.bar(B_VC_FULL), 4);
+        mbar_init(S.bar(B_VC_FREE), 1);
+        mbar_init(S.bar(B_P_FULL), 4);
+        mbar_init(S.bar(B_PV_DONE), 1);
+        mbar_init(S.bar(B_Q_FULL), 4);
+        mbar_init(S.bar(B_DRAIN), 1);
+        *S.abort_flag() = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_addr(S.tmem_slot())), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *S.tmem_slot();
+    volatile int* abort_flag = S.abort_flag();
+    uint8_t* Qs = S.base + OFF_Q;
+    uint8_t* Ks = S.base + OFF_K;
+    uint8_t* Vs = S.base + OFF_V;
+    uint8_t* Ps = S.base + OFF_P;
+    uint8_t* Pl = S.base + OFF_PL;
+    uint8_t* I8 = S.base + OFF_I8;
+    float* sc_k = reinterpret_cast<float*>(S.base + OFF_SC);
+    float* sc_v = sc_k + BN;
+
+    if (warp == kProducerWarp) {
+        // ================================================================ TMA
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int issued = 0;
+            for (int j = 0; j < ntiles; ++j) {
+                const int st = j & 1;
+                if (j >= 2 && !wait_abortable(S.bar(B_KV_EMPTY + st), ((j >> 1) - 1) & 1, abort_flag))
+                    break;
+                mbar_arrive_expect_tx(S.bar(B_KV_FULL + st), 2 * I8_TILE);
+                const int y = off + j * BN;
+                tma_load_2d(I8 + (2 * st) * I8_TILE, &tmap_k, g * D, y, S.bar(B_KV_FULL + st), pol);
+                tma_load_2d(I8 + (2 * st + 1) * I8_TILE, &tmap_v, g * D, y, S.bar(B_KV_FULL + st), pol);
+                issued = j + 1;
+            }
+            // never leave with copies in flight into this CTA's shared memory
+            for (int j = max(0, issued - 2); j < issued; ++j) {
+                const long long t0 = clock64();
+                while (!mbar_try_wait(S.bar(B_KV_FULL + (j & 1)), (j >> 1) & 1) &&
+                       clock64() - t0 < kWaitBudgetCycles) {
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ================================================================ MMA
+        if (lane == 0) {
+            bool ok = wait_abortable(S.bar(B_Q_FULL), 0, abort_flag);
+            auto qk = [&](int j) {
+                const uint32_t d = tmem + (j & 1) * BN;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const int o = (kk >> 2) * ATOM + (kk & 3) * 32;
+                    umma(d, umma_desc(Qs + o, 16, 1024), umma_desc(Ks + o, 16, 1024), kIdescQK, kk > 0);
+                }
+                umma_commit(S.bar(B_S_FULL + (j & 1)));
+                umma_commit(S.bar(B_KC_FREE));
+            };
+            if (ok && (ok = wait_abortable(S.bar(B_KC_FULL), 0, abort_flag))) {
+                tc_fence_after();
+                qk(0);
+            }
+            for (int j = 0; ok && j < ntiles; ++j) {
+                if (j + 1 < ntiles) {
+                    ok = wait_abortable(S.bar(B_KC_FULL), (j + 1) & 1, abort_flag);
+                    if (ok && j + 1 >= 2)
+                        ok = wait_abortable(S.bar(B_S_FREE + ((j + 1) & 1)), ((j - 1) >> 1) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    qk(j + 1);
+                }
+                ok = wait_abortable(S.bar(B_P_FULL), j & 1, abort_flag) &&
+                     wait_abortable(S.bar(B_VC_FULL), j & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const int o = (kk >> 2) * ATOM + (kk & 3) * 32;
+                    const uint64_t vb = umma_desc(Vs + kk * 16 * 128, ATOM, 1024);
+                    umma(tmem + TM_O, umma_desc(Ps + o, 16, 1024), vb, kIdescPV, j > 0 || kk > 0);
+                    umma(tmem + TM_O, umma_desc(Pl + o, 16, 1024), vb, kIdescPV, true);
+                }
+                umma_commit(S.bar(B_PV_DONE));
+                umma_commit(S.bar(B_VC_FREE));
+            }
+            // before the tensor memory is freed, every issued MMA must be done:
+            // one more commit tracks all of them
+            umma_commit(S.bar(B_DRAIN));
+            const long long t0 = clock64();
+            while (!mbar_try_wait(S.bar(B_DRAIN), 0) && clock64() - t0 < kWaitBudgetCycles) {
+            }
+        }
+    } else if (warp >= 4) {
+        // ================================================================ convert
+        const int t = threadIdx.x - 128;     // token row of the tile
+        for (int j = 0; j < ntiles; ++j) {
+            const int st = j & 1;
+            if (!warp_wait_abortable(S.bar(B_KV_FULL + st), (j >> 1) & 1, abort_flag)) break;
+            if (j >= 1 && !warp_wait_abortable(S.bar(B_KC_FREE), (j - 1) & 1, abort_flag)) break;
+            convert_k_row(I8 + (2 * st) * I8_TILE, Ks, t);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(S.bar(B_KC_FULL));
+            if (j >= 1 && !warp_wait_abortable(S.bar(B_VC_FREE), (j - 1) & 1, abort_flag)) break;
+            convert_v_row(I8 + (2 * st + 1) * I8_TILE, Vs, t);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(S.bar(B_VC_FULL));
+                mbar_arrive(S.bar(B_KV_EMPTY + st));
+            }
+        }
+    } else {
+        // ================================================================ softmax
+        const int r = threadIdx.x;             // query row of the block == TMEM lane
+        const bool live = r < rows;
+        const int qpos = q0 + r;               // row within the appended chunk
+        const int limit = live ? past + qpos : -1;   // last kv slot this row may see
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+
+        // Q row -> bf16, K-major swizzled
+        {
+            const float* qp = a.q + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {   // 16 chunks of 8 dims
+                float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+                if (live) {
+                    x0 = reinterpret_cast<const float4*>(qp)[2 * c];
+                    x1 = reinterpret_cast<const float4*>(qp)[2 * c + 1];
+                }
+                uint8_t* blk = Qs + (c >> 3) * ATOM;
+                *reinterpret_cast<uint4*>(blk + swz(r, c & 7)) =
+                    make_uint4(pack_bf16(x0.x, x0.y), pack_bf16(x0.z, x0.w), pack_bf16(x1.x, x1.y),
+                               pack_bf16(x1.z, x1.w));
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(S.bar(B_Q_FULL));
+        }
+
+        auto scale_at = [&](const float* arr, int slot) -> float {
+            return a.row_scales ? arr[slot] : arr[(size_t)slot * HKV + g];
+        };
+        // per-token scales of tile j for column r (prefetched one tile ahead)
+        auto load_scales = [&](int j, float& ks, float& vs) {
+            const int slot = off + j * BN + r;
+            const bool in = j * BN + r < len;
+            ks = in ? scale_at(a.key_scales, slot) * a.qk_mul : 0.0f;
+            vs = in ? scale_at(a.val_scales, slot) : 0.0f;
+        };
+        float ks_next, vs_next;
+        load_scales(0, ks_next, vs_next);
+        float m_run = -INFINITY, l_run = 0.0f;
+        bool ok = true;
+
+        for (int j = 0; j < ntiles && ok; ++j) {
+            named_bar(2, 128);        // previous tile's scales are no longer read
+            sc_k[r] = ks_next;
+            sc_v[r] = vs_next;
+            named_bar(2, 128);
+            if (j + 1 < ntiles) load_scales(j + 1, ks_next, vs_next);
+
+            if (!warp_wait_abortable(S.bar(B_S_FULL + (j & 1)), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t s_addr = lane_base + (j & 1) * BN;
+            const int kv0 = j * BN;
+            const bool diag = kv0 + BN - 1 > past + q0;   // some column may be masked
+            // pass 1: row max
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float v[32];
+                tmem_ld32(s_addr + 32 * k, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int c = 32 * k + i;
+                    float s = v[i] * sc_k[c];
+                    if (diag && kv0 + c > limit) s = -INFINITY;
+                    tmax = fmaxf(tmax, s);
+                }
+            }
+            if (!live) tmax = -INFINITY;
+            float corr = 1.0f;
+            if (tmax > m_run + kLazyRescale) {
+                corr = exp2f(m_run - tmax);
+                m_run = tmax;
+            }
+            l_run *= corr;
+
+            // P buffer and O are free once PV of the previous tile is done
+            if (j >= 1 && !warp_wait_abortable(S.bar(B_PV_DONE), (j - 1) & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            if (j >= 1 && __any_sync(kFull, corr != 1.0f)) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float o[32];
+                    tmem_ld32(lane_base + TM_O + 32 * k, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= corr;
+                    tmem_st32(lane_base + TM_O + 32 * k, o);
+                }
+            }
+            // pass 2: p' = exp2(s - m) * v_scale as an f16 pair hi + lo (hi =
+            // f16(p'), lo = f16(p' - hi)), K-major swizzled, 8 tokens at a time
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float v[32];
+                tmem_ld32(s_addr + 32 * k, v);
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {   // chunk of 8 tokens
+                    uint32_t hi[4], lo[4];
+#pragma unroll
+                    for (int u = 0; u < 8; u += 2) {
+                        float pv[2];
+#pragma unroll
+                        for (int w = 0; w < 2; ++w) {
+                            const int c = 32 * k + 8 * cc + u + w;
+                            float s = v[8 * cc + u + w] * sc_k[c];
+                            if ((diag && kv0 + c > limit) || !live) s = -INFINITY;
+                            const float p = s == -INFINITY ? 0.0f : exp2f(s - m_run);
+                            l_run += p;
+                            pv[w] = p * sc_v[c];
+                        }
+                        const __half2 h2 = __floats2half2_rn(pv[0], pv[1]);
+                        const float2 hf = __half22float2(h2);
+                        const __half2 l2 = __floats2half2_rn(pv[0] - hf.x, pv[1] - hf.y);
+                        hi[u / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+                        lo[u / 2] = *reinterpret_cast<const uint32_t*>(&l2);
+                    }
+                    const int chunk = 4 * k + cc;    // 0..15 over the 128 tokens
+                    const int boff = (chunk >> 3) * ATOM + swz(r, chunk & 7);
+                    *reinterpret_cast<uint4*>(Ps + boff) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<uint4*>(Pl + boff) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(S.bar(B_S_FREE + (j & 1)));
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(S.bar(B_P_FULL));
+        }
+        // ---- epilogue: O / l for live rows
+        if (ok && warp_wait_abortable(S.bar(B_PV_DONE), (ntiles - 1) & 1, abort_flag)) {
+            tc_fence_after();
+            float* op = a.out + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D;
+            const float inv = (live && l_run > 0.0f) ? __fdiv_rn(1.0f, l_run) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float o[32];
+                tmem_ld32(lane_base + TM_O + 32 * k, o);
+                if (live) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        reinterpret_cast<float4*>(op + 32 * k)[i / 4] =
+                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                }
+            }
+        }
+        if (!ok && lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(TMEM_COLS) : "memory");
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st) {
+    static unsigned long long attr_done = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (!bit || !(attr_done & bit)) {
+        e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        if (e != cudaSuccess) return e;
+        attr_done |= bit;
+    }
+    CUtensorMap mk, mv;
+    if ((e = make_code_map(&mk, a.keys, a.num_kv_heads, a.total_slots, BN)) != cudaSuccess) return e;
+    if ((e = make_code_map(&mv, a.values, a.num_kv_heads, a.total_slots, BN)) != cudaSuccess) return e;
+    const int nqb = (a.n_new + BM - 1) / BM;
+    const long long blocks = (long long)a.num_seqs * a.num_heads * nqb;
+    if (blocks == 0) return cudaSuccess;
+    if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    prefill_kernel<<<(unsigned)blocks, kThreads, SMEM, st>>>(mk, mv, a);
+    return cudaGetLastError();
+}
+
+}  // namespace ec

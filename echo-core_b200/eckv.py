@@ -48,7 +48,8 @@ EXPORTS = (
     "ec_kv_cache_create", "ec_kv_cache_destroy", "ec_kv_cache_layer", "ec_kv_cache_append",
     "ec_kv_cache_seq_len", "ec_kv_cache_reset", "ec_kv_cache_attention",
     "ec_kv_batch_append", "ec_decode_workspace_size", "ec_decode_attention",
-    "ec_decode_attention_partial", "ec_lse_combine", "ec_decode_attention_noalloc",
+    "ec_decode_attention_partial", "ec_lse_combine", "ec_prefill_attention",
+    "ec_decode_attention_noalloc",
 )
 
 
@@ -119,6 +120,7 @@ def lib() -> ctypes.CDLL:
             "ec_decode_attention_partial": ([ctypes.POINTER(KVBatch), vp, vp, vp, u32, f, vp,
                                              ctypes.c_size_t, vp], i32),
             "ec_lse_combine": ([vp, vp, u32, u32, u32, u32, vp, vp], i32),
+            "ec_prefill_attention": ([ctypes.POINTER(KVBatch), vp, vp, u32, u32, f, vp], i32),
             "ec_decode_attention_noalloc": ([ctypes.POINTER(KVBatch), vp, vp, u32, f, vp], i32),
         }
         for name, (args, res) in sig.items():
@@ -290,6 +292,14 @@ class BatchCache:
                                                 _ptr(part_ml), num_heads,
                                                 ctypes.c_float(softmax_scale), _ptr(ws),
                                                 ws.numel(), _stream(stream)))
+
+    def prefill(self, q, out, n_new: int, num_heads: int, softmax_scale: float,
+                stream=None) -> None:
+        """Causal attention of the last n_new cached tokens of every sequence
+        (q [num_seqs][n_new][num_heads][128] fp32, bf16-cast on load)."""
+        d = self.desc()
+        check(lib().ec_prefill_attention(ctypes.byref(d), _ptr(q), _ptr(out), n_new, num_heads,
+                                         ctypes.c_float(softmax_scale), _stream(stream)))
 
     def device_error(self, stream=None) -> int:
         return device_error(self.err, stream)

@@ -223,6 +223,21 @@ EC_API int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t nu
                    uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim, float* out,
                    ec_stream_t stream);
 
+/* Chunked-prefill attention.  The reference has no chunked prefill: it feeds
+ * a prompt one token at a time (src/main.cpp:404-405), each token running the
+ * decode loop of src/inference.cpp:321-392 over the cache as it stands after
+ * that token's append.  This computes the same attention for a whole chunk at
+ * once.  For every sequence the chunk is the last n_new cached tokens (slots
+ * [len - n_new, len) after ec_kv_batch_append), and query row i attends to
+ * slots [0, len - n_new + i].  q [num_seqs][n_new][num_heads][128] fp32 is cast
+ * to bf16 on load (bf16-cast queries); out has the same shape, fp32.  Runs on
+ * the tcgen05 tensor cores; head_dim 128, any num_kv_heads dividing num_heads.
+ * p' = p * v_scale is carried in f16, so v_scale must stay below 255
+ * (|v| below about 32,000). */
+EC_API int ec_prefill_attention(const ec_kv_batch* batch, const float* q, float* out,
+                                uint32_t n_new, uint32_t num_heads, float softmax_scale,
+                                ec_stream_t stream);
+
 /* No counterpart in the reference (which has no device memory at all): this
  * entry point exists for callers that cannot allocate device memory when they
  * run decode -- code running where cudaMalloc is not allowed (a host callback

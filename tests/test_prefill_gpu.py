@@ -1,0 +1,113 @@
+"""Chunked-prefill attention on the tcgen05 tensor cores against the oracle.
+
+The oracle for a chunk is the reference's decode loop run per query row with
+a causal length (the reference feeds prompts one token at a time,
+src/main.cpp:404-405).  Queries are bf16-cast on load, so the oracle is fed
+the same bf16-rounded queries; the tolerance is the attention bar of the other
+tests (max-abs 2e-3, |err| <= 2e-3 + 1e-3*|ref|).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+import workloads as W
+from _util import assert_attn_close, fill_batch
+
+pytestmark = pytest.mark.gpu
+
+D = 128
+
+
+def _bf16_round(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).bfloat16().float().numpy()
+
+
+def _case(torch, eckv, pasts, n_new, H, hkv, seed, mode=0, rows=None):
+    """Builds caches of `pasts` tokens, appends n_new tokens per sequence on
+    the GPU, runs prefill; returns GPU output and the oracle check rows."""
+    rng = np.random.default_rng(seed)
+    seqs, k_new, v_new = [], [], []
+    for p in pasts:
+        kf = W.kv_rows(rng, p + n_new, hkv, D)
+        vf = W.kv_rows(rng, p + n_new, hkv, D)
+        seqs.append((kf, vf))
+    bc = eckv.BatchCache([p + n_new for p in pasts], num_kv_heads=hkv, scale_mode=mode)
+    filled = []
+    for (kf, vf), p in zip(seqs, pasts):
+        if p:
+            kq, ks = O.quantize_kv(kf[:p], hkv, D, mode)
+            vq, vs = O.quantize_kv(vf[:p], hkv, D, mode)
+        else:
+            ns = hkv if mode == 0 else 1
+            kq = vq = np.zeros((0, hkv * D), np.int8)
+            ks = vs = np.zeros((0, ns) if mode == 0 else (0,), np.float32)
+        filled.append((kq, vq, ks, vs))
+    fill_batch(bc, filled)
+    kn = np.stack([kf[p:] for (kf, vf), p in zip(seqs, pasts)])
+    vn = np.stack([vf[p:] for (kf, vf), p in zip(seqs, pasts)])
+    bc.append(torch.from_numpy(kn).cuda(), torch.from_numpy(vn).cuda(), n_new)
+    q = W.queries(rng, len(pasts) * n_new, H, D).reshape(len(pasts), n_new, H, D)
+    out = torch.full((len(pasts), n_new, H, D), float("nan"), device="cuda")
+    bc.prefill(torch.from_numpy(q).cuda(), out, n_new, H, W.softmax_scale(D))
+    torch.cuda.synchronize()
+    assert bc.device_error() == 0
+    got = out.cpu().numpy()
+    qb = _bf16_round(q)
+    checks = []
+    for s, ((kf, vf), p) in enumerate(zip(seqs, pasts)):
+        kq, ks = O.quantize_kv(kf, hkv, D, mode)
+        vq, vs = O.quantize_kv(vf, hkv, D, mode)
+        for i in (rows if rows is not None else range(n_new)):
+            want = O.decode_attention(kq, vq, ks, vs, p + i + 1, qb[s, i], H, hkv, D,
+                                      W.softmax_scale(D), mode)
+            checks.append((got[s, i], want, f"seq {s} row {i}"))
+    return checks
+
+
+def test_prefill_small_ragged_unaligned(cuda):
+    """Pasts not multiples of the 128-token tile, a chunk that ends mid block."""
+    import torch
+    import eckv
+    for got, want, what in _case(torch, eckv, [300, 1000, 0], 200, 16, 4, 1):
+        assert_attn_close(got, want, what)
+
+
+def test_prefill_config5_shape_rows(cuda):
+    """Config 5's shapes (8192 cached + 4096 appended, 16 Q / 4 KV heads) on
+    two sequences; rows checked at both ends of the chunk and at block edges."""
+    import torch
+    import eckv
+    rows = [0, 1, 2, 127, 128, 129, 1000, 2047, 2048, 4000, 4094, 4095]
+    for got, want, what in _case(torch, eckv, [8192, 8192], 4096, 16, 4, 4, rows=rows):
+        assert_attn_close(got, want, what)
+
+
+@pytest.mark.parametrize("H,hkv", [(8, 8), (32, 8), (4, 1), (16, 2)])
+def test_prefill_gqa_groupings(cuda, H, hkv):
+    import torch
+    import eckv
+    for got, want, what in _case(torch, eckv, [129, 40], 130, H, hkv, H + hkv):
+        assert_attn_close(got, want, what)
+
+
+def test_prefill_row_scales(cuda):
+    import torch
+    import eckv
+    for got, want, what in _case(torch, eckv, [77, 256], 64, 16, 4, 9, mode=1):
+        assert_attn_close(got, want, what)
+
+
+def test_prefill_bad_table_flagged(cuda):
+    import torch
+    import eckv
+    bc = eckv.BatchCache([64, 64], num_kv_heads=4)
+    bc.length.copy_(torch.tensor([64, 10], dtype=torch.int32))   # 10 < n_new: past < 0
+    q = torch.randn(2, 32, 16, D, device="cuda")
+    out = torch.zeros(2, 32, 16, D, device="cuda")
+    bc.prefill(q, out, 32, 16, 0.1)
+    torch.cuda.synchronize()
+    assert bc.device_error() == eckv.DEVERR_BAD_TABLE
+    assert not out[1].cpu().numpy().any()
