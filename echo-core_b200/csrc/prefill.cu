@@ -162,6 +162,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// tcgen05.ld without the wait; call tmem_wait_ld() before using v.
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float (&v)[32]) {
+    uint32_t* r = reinterpret_cast<uint32_t*>(v);
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
@@ -234,6 +252,13 @@ __device__ __forceinline__ void convert_v_row(const uint8_t* src, uint8_t* vs, i
         *reinterpret_cast<uint4*>(blk + swz(t, cb)) = make_uint4(o[0], o[1], o[2], o[3]);
         *reinterpret_cast<uint4*>(blk + swz(t, cb + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
     }
+}
+
+// 2^x on the SFU (ex2.approx: relative error about 2^-22, -inf -> +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 __device__ __forceinline__ void named_bar(int id, int threads) {
@@ -454,28 +479,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const uint32_t s_addr = lane_base + (j & 1) * BN;
             const int kv0 = j * BN;
-            const bool diag = kv0 + BN - 1 > past + q0;   // some column may be masked
-            // pass 1: row max
+            // columns past a row's causal limit exist only near the diagonal or
+            // in a partial block (rows >= `rows` have limit -1)
+            const bool masked_tile = kv0 + BN - 1 > past + q0 || rows < BM;
+            const float4* sk4 = reinterpret_cast<const float4*>(sc_k);
+            const float4* sv4 = reinterpret_cast<const float4*>(sc_v);
+            // pass 1: row max of s = S * k_scale * qk_mul
             float tmax = -INFINITY;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float v[32];
-                tmem_ld32(s_addr + 32 * k, v);
+            for (int k = 0; k < 4; k += 2) {
+                float v0[32], v1[32];
+                tmem_ld32_nowait(s_addr + 32 * k, v0);
+                tmem_ld32_nowait(s_addr + 32 * k + 32, v1);
+                tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int c = 32 * k + i;
-                    float s = v[i] * sc_k[c];
-                    if (diag && kv0 + c > limit) s = -INFINITY;
-                    tmax = fmaxf(tmax, s);
+                for (int i = 0; i < 32; i += 4) {
+                    const float4 ka = sk4[(32 * k + i) / 4], kb = sk4[(32 * k + 32 + i) / 4];
+                    float a4[4] = {v0[i] * ka.x, v0[i + 1] * ka.y, v0[i + 2] * ka.z, v0[i + 3] * ka.w};
+                    float b4[4] = {v1[i] * kb.x, v1[i + 1] * kb.y, v1[i + 2] * kb.z, v1[i + 3] * kb.w};
+                    if (masked_tile) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (kv0 + 32 * k + i + u > limit) a4[u] = -INFINITY;
+                            if (kv0 + 32 * k + 32 + i + u > limit) b4[u] = -INFINITY;
+                        }
+                    }
+                    tmax = fmaxf(tmax, fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3])));
+                    tmax = fmaxf(tmax, fmaxf(fmaxf(b4[0], b4[1]), fmaxf(b4[2], b4[3])));
                 }
             }
-            if (!live) tmax = -INFINITY;
             float corr = 1.0f;
             if (tmax > m_run + kLazyRescale) {
-                corr = exp2f(m_run - tmax);
+                corr = fast_exp2(m_run - tmax);
                 m_run = tmax;
             }
             l_run *= corr;
+            const float neg_m = m_run == -INFINITY ? 0.0f : -m_run;
 
             // P buffer and O are free once PV of the previous tile is done
             if (j >= 1 && !warp_wait_abortable(S.bar(B_PV_DONE), (j - 1) & 1, abort_flag)) { ok = false; break; }
@@ -490,37 +529,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(lane_base + TM_O + 32 * k, o);
                 }
             }
-            // pass 2: p' = exp2(s - m) * v_scale as an f16 pair hi + lo (hi =
+            // pass 2: p' = 2^(s - m) * v_scale as an f16 pair hi + lo (hi =
             // f16(p'), lo = f16(p' - hi)), K-major swizzled, 8 tokens at a time
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float v[32];
-                tmem_ld32(s_addr + 32 * k, v);
+            for (int k = 0; k < 4; k += 2) {
+                float v0[32], v1[32];
+                tmem_ld32_nowait(s_addr + 32 * k, v0);
+                tmem_ld32_nowait(s_addr + 32 * k + 32, v1);
+                tmem_wait_ld();
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {   // chunk of 8 tokens
-                    uint32_t hi[4], lo[4];
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    const float* v = h2 ? v1 : v0;
+                    const int cbase = 32 * (k + h2);
 #pragma unroll
-                    for (int u = 0; u < 8; u += 2) {
-                        float pv[2];
+                    for (int cc = 0; cc < 4; ++cc) {   // chunk of 8 tokens
+                        uint32_t hi[4], lo[4];
 #pragma unroll
-                        for (int w = 0; w < 2; ++w) {
-                            const int c = 32 * k + 8 * cc + u + w;
-                            float s = v[8 * cc + u + w] * sc_k[c];
-                            if ((diag && kv0 + c > limit) || !live) s = -INFINITY;
-                            const float p = s == -INFINITY ? 0.0f : exp2f(s - m_run);
-                            l_run += p;
-                            pv[w] = p * sc_v[c];
+                        for (int u = 0; u < 8; u += 4) {
+                            const int c = cbase + 8 * cc + u;
+                            const float4 kf = sk4[c / 4], vf = sv4[c / 4];
+                            float e[4] = {fmaf(v[8 * cc + u], kf.x, neg_m), fmaf(v[8 * cc + u + 1], kf.y, neg_m),
+                                          fmaf(v[8 * cc + u + 2], kf.z, neg_m), fmaf(v[8 * cc + u + 3], kf.w, neg_m)};
+                            if (masked_tile) {
+#pragma unroll
+                                for (int w = 0; w < 4; ++w)
+                                    if (kv0 + c + w > limit) e[w] = -INFINITY;
+                            }
+                            float p[4];
+#pragma unroll
+                            for (int w = 0; w < 4; ++w) p[w] = fast_exp2(e[w]);
+                            l_run += (p[0] + p[1]) + (p[2] + p[3]);
+                            const float pv[4] = {p[0] * vf.x, p[1] * vf.y, p[2] * vf.z, p[3] * vf.w};
+#pragma unroll
+                            for (int w = 0; w < 4; w += 2) {
+                                const __half2 h = __floats2half2_rn(pv[w], pv[w + 1]);
+                                const float2 hf = __half22float2(h);
+                                const __half2 l2 = __floats2half2_rn(pv[w] - hf.x, pv[w + 1] - hf.y);
+                                hi[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&h);
+                                lo[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&l2);
+                            }
                         }
-                        const __half2 h2 = __floats2half2_rn(pv[0], pv[1]);
-                        const float2 hf = __half22float2(h2);
-                        const __half2 l2 = __floats2half2_rn(pv[0] - hf.x, pv[1] - hf.y);
-                        hi[u / 2] = *reinterpret_cast<const uint32_t*>(&h2);
-                        lo[u / 2] = *reinterpret_cast<const uint32_t*>(&l2);
+                        const int chunk = (cbase >> 3) + cc;    // 0..15 over the 128 tokens
+                        const int boff = (chunk >> 3) * ATOM + swz(r, chunk & 7);
+                        *reinterpret_cast<uint4*>(Ps + boff) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(Pl + boff) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     }
-                    const int chunk = 4 * k + cc;    // 0..15 over the 128 tokens
-                    const int boff = (chunk >> 3) * ATOM + swz(r, chunk & 7);
-                    *reinterpret_cast<uint4*>(Ps + boff) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    *reinterpret_cast<uint4*>(Pl + boff) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                 }
             }
             tc_fence_before();
