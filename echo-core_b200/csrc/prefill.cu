@@ -51,24 +51,25 @@ constexpr int kMmaWarp = 9;
 constexpr int kThreads = 10 * 32;
 constexpr int ATOM = 128 * 128;            // one [128 rows][128 B] swizzled block
 constexpr int OFF_Q = 0;                   // bf16 Q   : 2 K-blocks (dims 0-63, 64-127)
-constexpr int OFF_K = OFF_Q + 2 * ATOM;    // bf16 K   : 2 K-blocks
-constexpr int OFF_V = OFF_K + 2 * ATOM;    // f16  V   : 2 dim halves, MN-major
-constexpr int OFF_P = OFF_V + 2 * ATOM;    // f16  P'hi: 2 K-blocks (tokens 0-63, 64-127)
-constexpr int OFF_PL = OFF_P + 2 * ATOM;   // f16  P'lo = f16(p' - P'hi), same layout
+constexpr int OFF_K = OFF_Q + 2 * ATOM;    // bf16 K   : [2 buffers][2 K-blocks]
+constexpr int OFF_V = OFF_K + 4 * ATOM;    // f16  V   : [2 buffers][2 dim halves], MN-major
 constexpr int I8_TILE = BN * 128;          // 16 KB of int8 codes
-constexpr int OFF_I8 = OFF_PL + 2 * ATOM;  // [2 stages][K, V]
+constexpr int OFF_I8 = OFF_V + 4 * ATOM;   // [2 stages][K, V]
 constexpr int OFF_SC = OFF_I8 + 2 * 2 * I8_TILE;   // k-scale * qk_mul [BN], v-scale [BN]
 constexpr int OFF_BAR = OFF_SC + 2 * BN * 4;
 enum {
-    B_KV_FULL = 0, B_KV_EMPTY = 2, B_KC_FULL = 4, B_KC_FREE, B_VC_FULL, B_VC_FREE,
-    B_S_FULL = 8, B_S_FREE = 10, B_P_FULL = 12, B_PV_DONE, B_Q_FULL, B_DRAIN, NBARS
+    B_KV_FULL = 0, B_KV_EMPTY = 2, B_KC_FULL = 4, B_KC_FREE = 6, B_VC_FULL = 8, B_VC_FREE = 10,
+    B_S_FULL = 12, B_P_FULL = 15, B_PV_BUF = 18, B_Q_FULL = 21, B_DRAIN, NBARS
 };
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;      // [0] tmem base, [1] abort flag
 constexpr int SMEM = 1024 + OFF_MISC + 16;
 static_assert(SMEM <= 227 * 1024, "shared memory budget");
 
-constexpr int TMEM_COLS = 512;             // S0 [0,128), S1 [128,256), O [256,384)
-constexpr int TM_O = 256;
+// Tensor memory: three S/P buffers of 128 columns (QK^T scores, overwritten in
+// place by p' as f16 hi/lo pairs), then the O accumulator.
+constexpr int TMEM_COLS = 512;
+constexpr int NSP = 3;
+constexpr int TM_O = 384;
 constexpr float kLazyRescale = 8.0f;
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -138,6 +139,27 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, ui
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
         ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)accumulate), "r"(0u), "r"(0u),
         "r"(0u), "r"(0u));
+}
+
+// A operand from tensor memory (rows = lanes, 2 f16 per 32-bit column).
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                        uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"((uint32_t)accumulate), "r"(0u),
+        "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+        "%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+        "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]),
+        "r"(v[14]), "r"(v[15])
+        : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -301,15 +323,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(S.bar(B_KV_FULL + i), 1);
             mbar_init(S.bar(B_KV_EMPTY + i), 4);
-            mbar_init(S.bar(B_S_FULL + i), 1);
-            mbar_init(S.bar(B_S_FREE + i), 4);
+            mbar_init(S.bar(B_KC_FULL + i), 4);
+            mbar_init(S.bar(B_KC_FREE + i), 1);
+            mbar_init(S.bar(B_VC_FULL + i), 4);
+            mbar_init(S.bar(B_VC_FREE + i), 1);
         }
-        mbar_init(S.bar(B_KC_FULL), 4);
-        mbar_init(S.bar(B_KC_FREE), 1);
-        mbar_init(S.bar(B_VC_FULL), 4);
-        mbar_init(S.bar(B_VC_FREE), 1);
-        mbar_init(S.bar(B_P_FULL), 4);
-        mbar_init(S.bar(B_PV_DONE), 1);
+        for (int i = 0; i < NSP; ++i) {
+            mbar_init(S.bar(B_S_FULL + i), 1);
+            mbar_init(S.bar(B_P_FULL + i), 4);
+            mbar_init(S.bar(B_PV_BUF + i), 1);
+        }
         mbar_init(S.bar(B_Q_FULL), 4);
         mbar_init(S.bar(B_DRAIN), 1);
         *S.abort_flag() = 0;
@@ -326,13 +349,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *S.tmem_slot();
     volatile int* abort_flag = S.abort_flag();
     uint8_t* Qs = S.base + OFF_Q;
-    uint8_t* Ks = S.base + OFF_K;
-    uint8_t* Vs = S.base + OFF_V;
-    uint8_t* Ps = S.base + OFF_P;
-    uint8_t* Pl = S.base + OFF_PL;
     uint8_t* I8 = S.base + OFF_I8;
     float* sc_k = reinterpret_cast<float*>(S.base + OFF_SC);
     float* sc_v = sc_k + BN;
+    auto Kc = [&](int b) { return S.base + OFF_K + b * 2 * ATOM; };
+    auto Vc = [&](int b) { return S.base + OFF_V + b * 2 * ATOM; };
 
     if (warp == kProducerWarp) {
         // ================================================================ TMA
@@ -361,42 +382,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ================================================================ MMA
         if (lane == 0) {
             bool ok = wait_abortable(S.bar(B_Q_FULL), 0, abort_flag);
-            auto qk = [&](int j) {
-                const uint32_t d = tmem + (j & 1) * BN;
+            // QK^T of tile j into S/P buffer j % 3
+            auto qk = [&](int j) -> bool {
+                const int kb = j & 1, sb = j % NSP;
+                if (!wait_abortable(S.bar(B_KC_FULL + kb), (j >> 1) & 1, abort_flag)) return false;
+                if (j >= NSP && !wait_abortable(S.bar(B_PV_BUF + sb), ((j / NSP) - 1) & 1, abort_flag))
+                    return false;   // PV of tile j - 3 has read its p' out of this buffer
+                tc_fence_after();
+                const uint8_t* kc = Kc(kb);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const int o = (kk >> 2) * ATOM + (kk & 3) * 32;
-                    umma(d, umma_desc(Qs + o, 16, 1024), umma_desc(Ks + o, 16, 1024), kIdescQK, kk > 0);
+                    umma(tmem + sb * BN, umma_desc(Qs + o, 16, 1024), umma_desc(kc + o, 16, 1024),
+                         kIdescQK, kk > 0);
                 }
-                umma_commit(S.bar(B_S_FULL + (j & 1)));
-                umma_commit(S.bar(B_KC_FREE));
+                umma_commit(S.bar(B_S_FULL + sb));
+                umma_commit(S.bar(B_KC_FREE + kb));
+                return true;
             };
-            if (ok && (ok = wait_abortable(S.bar(B_KC_FULL), 0, abort_flag))) {
-                tc_fence_after();
-                qk(0);
-            }
+            if (ok) ok = qk(0);
             for (int j = 0; ok && j < ntiles; ++j) {
-                if (j + 1 < ntiles) {
-                    ok = wait_abortable(S.bar(B_KC_FULL), (j + 1) & 1, abort_flag);
-                    if (ok && j + 1 >= 2)
-                        ok = wait_abortable(S.bar(B_S_FREE + ((j + 1) & 1)), ((j - 1) >> 1) & 1, abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-                    qk(j + 1);
-                }
-                ok = wait_abortable(S.bar(B_P_FULL), j & 1, abort_flag) &&
-                     wait_abortable(S.bar(B_VC_FULL), j & 1, abort_flag);
+                if (j + 1 < ntiles && !(ok = qk(j + 1))) break;
+                const int vb = j & 1, sb = j % NSP;
+                ok = wait_abortable(S.bar(B_P_FULL + sb), (j / NSP) & 1, abort_flag) &&
+                     wait_abortable(S.bar(B_VC_FULL + vb), (j >> 1) & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
+                const uint8_t* vc = Vc(vb);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    const int o = (kk >> 2) * ATOM + (kk & 3) * 32;
-                    const uint64_t vb = umma_desc(Vs + kk * 16 * 128, ATOM, 1024);
-                    umma(tmem + TM_O, umma_desc(Ps + o, 16, 1024), vb, kIdescPV, j > 0 || kk > 0);
-                    umma(tmem + TM_O, umma_desc(Pl + o, 16, 1024), vb, kIdescPV, true);
+                    // tokens 16kk..16kk+15: chunk kk/2 of 32 tokens holds hi in its
+                    // first 16 columns and lo in the next 16
+                    const uint32_t a = tmem + sb * BN + 32 * (kk >> 1) + 8 * (kk & 1);
+                    const uint64_t vbd = umma_desc(vc + kk * 16 * 128, ATOM, 1024);
+                    umma_ts(tmem + TM_O, a, vbd, kIdescPV, j > 0 || kk > 0);
+                    umma_ts(tmem + TM_O, a + 16, vbd, kIdescPV, true);
                 }
-                umma_commit(S.bar(B_PV_DONE));
-                umma_commit(S.bar(B_VC_FREE));
+                umma_commit(S.bar(B_PV_BUF + sb));
+                umma_commit(S.bar(B_VC_FREE + vb));
             }
             // before the tensor memory is freed, every issued MMA must be done:
             // one more commit tracks all of them
@@ -409,19 +432,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ================================================================ convert
         const int t = threadIdx.x - 128;     // token row of the tile
         for (int j = 0; j < ntiles; ++j) {
-            const int st = j & 1;
+            const int st = j & 1, b = j & 1;
             if (!warp_wait_abortable(S.bar(B_KV_FULL + st), (j >> 1) & 1, abort_flag)) break;
-            if (j >= 1 && !warp_wait_abortable(S.bar(B_KC_FREE), (j - 1) & 1, abort_flag)) break;
-            convert_k_row(I8 + (2 * st) * I8_TILE, Ks, t);
+            if (j >= 2 && !warp_wait_abortable(S.bar(B_KC_FREE + b), ((j >> 1) - 1) & 1, abort_flag)) break;
+            convert_k_row(I8 + (2 * st) * I8_TILE, Kc(b), t);
             fence_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(S.bar(B_KC_FULL));
-            if (j >= 1 && !warp_wait_abortable(S.bar(B_VC_FREE), (j - 1) & 1, abort_flag)) break;
-            convert_v_row(I8 + (2 * st + 1) * I8_TILE, Vs, t);
+            if (lane == 0) mbar_arrive(S.bar(B_KC_FULL + b));
+            if (j >= 2 && !warp_wait_abortable(S.bar(B_VC_FREE + b), ((j >> 1) - 1) & 1, abort_flag)) break;
+            convert_v_row(I8 + (2 * st + 1) * I8_TILE, Vc(b), t);
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(S.bar(B_VC_FULL));
+                mbar_arrive(S.bar(B_VC_FULL + b));
                 mbar_arrive(S.bar(B_KV_EMPTY + st));
             }
         }
@@ -436,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Q row -> bf16, K-major swizzled
         {
             const float* qp = a.q + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D;
-#pragma unroll
+#pragma unroll 4
             for (int c = 0; c < 16; ++c) {   // 16 chunks of 8 dims
                 float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
                 if (live) {
@@ -469,15 +492,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
 
         for (int j = 0; j < ntiles && ok; ++j) {
+            const int sb = j % NSP;
             named_bar(2, 128);        // previous tile's scales are no longer read
             sc_k[r] = ks_next;
             sc_v[r] = vs_next;
             named_bar(2, 128);
             if (j + 1 < ntiles) load_scales(j + 1, ks_next, vs_next);
 
-            if (!warp_wait_abortable(S.bar(B_S_FULL + (j & 1)), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+            if (!warp_wait_abortable(S.bar(B_S_FULL + sb), (j / NSP) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t s_addr = lane_base + (j & 1) * BN;
+            const uint32_t s_addr = lane_base + sb * BN;
             const int kv0 = j * BN;
             // columns past a row's causal limit exist only near the diagonal or
             // in a partial block (rows >= `rows` have limit -1)
@@ -516,10 +540,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             l_run *= corr;
             const float neg_m = m_run == -INFINITY ? 0.0f : -m_run;
 
-            // P buffer and O are free once PV of the previous tile is done
-            if (j >= 1 && !warp_wait_abortable(S.bar(B_PV_DONE), (j - 1) & 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
+            // rescale O only when some row's maximum jumped (rare): O must
+            // first hold every earlier tile's contribution
             if (j >= 1 && __any_sync(kFull, corr != 1.0f)) {
+                const int pj = j - 1;
+                if (!warp_wait_abortable(S.bar(B_PV_BUF + pj % NSP), (pj / NSP) & 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     float o[32];
@@ -530,62 +556,50 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             // pass 2: p' = 2^(s - m) * v_scale as an f16 pair hi + lo (hi =
-            // f16(p'), lo = f16(p' - hi)), K-major swizzled, 8 tokens at a time
+            // f16(p'), lo = f16(p' - hi)), written over the chunk's own S
+            // columns once they have been read: chunk k (tokens 32k..32k+31)
+            // keeps hi in its first 16 columns and lo in the next 16
 #pragma unroll
-            for (int k = 0; k < 4; k += 2) {
-                float v0[32], v1[32];
-                tmem_ld32_nowait(s_addr + 32 * k, v0);
-                tmem_ld32_nowait(s_addr + 32 * k + 32, v1);
-                tmem_wait_ld();
+            for (int k = 0; k < 4; ++k) {
+                float v[32];
+                tmem_ld32(s_addr + 32 * k, v);
+                uint32_t hi[16], lo[16];
 #pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2) {
-                    const float* v = h2 ? v1 : v0;
-                    const int cbase = 32 * (k + h2);
+                for (int u = 0; u < 32; u += 4) {
+                    const int c = 32 * k + u;
+                    const float4 kf = sk4[c / 4], vf = sv4[c / 4];
+                    float e[4] = {fmaf(v[u], kf.x, neg_m), fmaf(v[u + 1], kf.y, neg_m),
+                                  fmaf(v[u + 2], kf.z, neg_m), fmaf(v[u + 3], kf.w, neg_m)};
+                    if (masked_tile) {
 #pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {   // chunk of 8 tokens
-                        uint32_t hi[4], lo[4];
+                        for (int w = 0; w < 4; ++w)
+                            if (kv0 + c + w > limit) e[w] = -INFINITY;
+                    }
+                    float pr[4];
 #pragma unroll
-                        for (int u = 0; u < 8; u += 4) {
-                            const int c = cbase + 8 * cc + u;
-                            const float4 kf = sk4[c / 4], vf = sv4[c / 4];
-                            float e[4] = {fmaf(v[8 * cc + u], kf.x, neg_m), fmaf(v[8 * cc + u + 1], kf.y, neg_m),
-                                          fmaf(v[8 * cc + u + 2], kf.z, neg_m), fmaf(v[8 * cc + u + 3], kf.w, neg_m)};
-                            if (masked_tile) {
+                    for (int w = 0; w < 4; ++w) pr[w] = fast_exp2(e[w]);
+                    l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
+                    const float pv[4] = {pr[0] * vf.x, pr[1] * vf.y, pr[2] * vf.z, pr[3] * vf.w};
 #pragma unroll
-                                for (int w = 0; w < 4; ++w)
-                                    if (kv0 + c + w > limit) e[w] = -INFINITY;
-                            }
-                            float p[4];
-#pragma unroll
-                            for (int w = 0; w < 4; ++w) p[w] = fast_exp2(e[w]);
-                            l_run += (p[0] + p[1]) + (p[2] + p[3]);
-                            const float pv[4] = {p[0] * vf.x, p[1] * vf.y, p[2] * vf.z, p[3] * vf.w};
-#pragma unroll
-                            for (int w = 0; w < 4; w += 2) {
-                                const __half2 h = __floats2half2_rn(pv[w], pv[w + 1]);
-                                const float2 hf = __half22float2(h);
-                                const __half2 l2 = __floats2half2_rn(pv[w] - hf.x, pv[w + 1] - hf.y);
-                                hi[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&h);
-                                lo[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&l2);
-                            }
-                        }
-                        const int chunk = (cbase >> 3) + cc;    // 0..15 over the 128 tokens
-                        const int boff = (chunk >> 3) * ATOM + swz(r, chunk & 7);
-                        *reinterpret_cast<uint4*>(Ps + boff) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4*>(Pl + boff) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    for (int w = 0; w < 4; w += 2) {
+                        const __half2 hh = __floats2half2_rn(pv[w], pv[w + 1]);
+                        const float2 hf = __half22float2(hh);
+                        const __half2 ll = __floats2half2_rn(pv[w] - hf.x, pv[w + 1] - hf.y);
+                        hi[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+                        lo[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&ll);
                     }
                 }
+                tmem_st16(s_addr + 32 * k, hi);
+                tmem_st16(s_addr + 32 * k + 16, lo);
             }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(S.bar(B_S_FREE + (j & 1)));
-            fence_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(S.bar(B_P_FULL));
+            if (lane == 0) mbar_arrive(S.bar(B_P_FULL + sb));
         }
         // ---- epilogue: O / l for live rows
-        if (ok && warp_wait_abortable(S.bar(B_PV_DONE), (ntiles - 1) & 1, abort_flag)) {
+        const int lj = ntiles - 1;
+        if (ok && warp_wait_abortable(S.bar(B_PV_BUF + lj % NSP), (lj / NSP) & 1, abort_flag)) {
             tc_fence_after();
             float* op = a.out + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D;
             const float inv = (live && l_run > 0.0f) ? __fdiv_rn(1.0f, l_run) : 0.0f;
