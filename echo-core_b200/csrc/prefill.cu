@@ -10,26 +10,32 @@
 //
 // One CTA owns 128 query rows of one query head of one sequence (query head h
 // reads KV head h % num_kv_heads, src/inference.cpp:335).  Warp roles:
-//   producer  (warp 8)    2-D TMA of the int8 K and V codes of 128-token
+//   producer  (warp 12)   2-D TMA of the int8 K and V codes of 128-token
 //                         tiles (128-byte swizzle, no multicast), 2 stages;
-//   converter (warps 4-7) int8 -> bf16 K (K-major) and int8 -> f16 V
+//   converter (warps 8-11) int8 -> bf16 K (K-major) and int8 -> f16 V
 //                         (MN-major), both exact, into 128B-swizzled UMMA
-//                         operand layouts;
-//   MMA       (warp 9)    one thread issues tcgen05.mma: S = Q K^T (bf16 x
-//                         bf16 -> fp32, double-buffered in TMEM) one tile
-//                         ahead of the softmax, then O += P'hi V + P'lo V
-//                         (f16 x f16 -> fp32, accumulated in TMEM);
-//   softmax   (warps 0-3) thread r owns query row r (TMEM lane r): scales S
-//                         by the per-token k-scale, masks causally, runs the
-//                         online softmax in base 2 with lazy rescaling of O in
-//                         TMEM, and writes p' = p * v_scale (the fused
-//                         v-scale) as an f16 hi/lo pair into the P operands.
+//                         operand layouts (K one tile, V two tiles);
+//   MMA       (warp 13)   one thread issues tcgen05.mma: S = Q K^T (bf16 x
+//                         bf16 -> fp32) into one of three S/P buffers in TMEM,
+//                         one tile ahead of the softmax, then O += P'hi V +
+//                         P'lo V with P' read from TMEM (f16 x f16 -> fp32,
+//                         accumulated in TMEM);
+//   softmax   (warps 0-7) query row r is TMEM lane r; warps w and w+4 share
+//                         the lanes of quadrant w and split each tile's 128
+//                         columns in halves, exchanging the row maximum
+//                         through shared memory.  They scale S by the
+//                         per-token k-scale, mask causally, run the online
+//                         softmax in base 2 with lazy rescaling of O, and write
+//                         p' = p * v_scale (the fused v-scale) as an f16 hi/lo
+//                         pair over the S columns they have read.
 // Q is cast to bf16 on load (the queries are bf16-cast); the softmax scale and
 // log2(e) multiply the fp32 scores.  K and V codes are exact in bf16 / f16; p'
 // enters the PV product as an f16 pair hi + lo (two MMAs), about 22 bits, so
-// the only rounding of consequence is Q's bf16 cast (part of the contract).  Every wait is bounded; a timeout raises a CTA-wide abort
-// flag so that every role stops, waits for its own in-flight work and the
-// CTA frees its tensor memory before returning.
+// the only rounding of consequence is Q's bf16 cast (part of the contract).
+// Every wait is bounded; a timeout raises a CTA-wide abort flag so that every
+// role stops, waits for its own in-flight work and the CTA frees its tensor
+// memory before returning.  The softmax warps decide together (a barrier
+// that ORs their failure flags) so that none is left at a named barrier.
 #include <cmath>
 #include <cstdint>
 
@@ -46,20 +52,29 @@ namespace {
 constexpr int D = 128;
 constexpr int BM = 128;                    // query rows per CTA (TMEM lanes)
 constexpr int BN = 128;                    // kv tokens per tile
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 10 * 32;
+// Warp roles:
+//   warps 0-7   softmax: warp w owns TMEM lanes 32*(w%4).. (query rows) and
+//               columns 64*(w/4).. of every S/P buffer and of O;
+//   warps 8-11  converter;
+//   warp 12     TMA producer, warp 13 MMA issuer.
+// Four warps share an SMSP's 16K registers, so every thread gets 128.
+constexpr int kConvWarp0 = 8;
+constexpr int kProducerWarp = 12;
+constexpr int kMmaWarp = 13;
+constexpr int kThreads = 14 * 32;
+constexpr int kSoftmaxThreads = 256;
 constexpr int ATOM = 128 * 128;            // one [128 rows][128 B] swizzled block
 constexpr int OFF_Q = 0;                   // bf16 Q   : 2 K-blocks (dims 0-63, 64-127)
-constexpr int OFF_K = OFF_Q + 2 * ATOM;    // bf16 K   : [2 buffers][2 K-blocks]
-constexpr int OFF_V = OFF_K + 4 * ATOM;    // f16  V   : [2 buffers][2 dim halves], MN-major
+constexpr int OFF_K = OFF_Q + 2 * ATOM;    // bf16 K   : 2 K-blocks (one tile)
+constexpr int OFF_V = OFF_K + 2 * ATOM;    // f16  V   : [2 buffers][2 dim halves], MN-major
 constexpr int I8_TILE = BN * 128;          // 16 KB of int8 codes
 constexpr int OFF_I8 = OFF_V + 4 * ATOM;   // [2 stages][K, V]
-constexpr int OFF_SC = OFF_I8 + 2 * 2 * I8_TILE;   // k-scale * qk_mul [BN], v-scale [BN]
-constexpr int OFF_BAR = OFF_SC + 2 * BN * 4;
+constexpr int OFF_SC = OFF_I8 + 2 * 2 * I8_TILE;   // [2 tiles][k-scale*qk_mul [BN], v-scale [BN]]
+constexpr int OFF_RED = OFF_SC + 2 * 2 * BN * 4;   // [2 tiles][2 column halves][BM] row exchange
+constexpr int OFF_BAR = OFF_RED + 2 * 2 * BM * 4;
 enum {
-    B_KV_FULL = 0, B_KV_EMPTY = 2, B_KC_FULL = 4, B_KC_FREE = 6, B_VC_FULL = 8, B_VC_FREE = 10,
-    B_S_FULL = 12, B_P_FULL = 15, B_PV_BUF = 18, B_Q_FULL = 21, B_DRAIN, NBARS
+    B_KV_FULL = 0, B_KV_EMPTY = 2, B_KC_FULL = 4, B_KC_FREE = 5, B_VC_FULL = 6, B_VC_FREE = 8,
+    B_S_FULL = 10, B_P_FULL = 13, B_PV_BUF = 16, B_Q_FULL = 19, B_DRAIN, NBARS
 };
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;      // [0] tmem base, [1] abort flag
 constexpr int SMEM = 1024 + OFF_MISC + 16;
@@ -86,11 +101,14 @@ struct Smem {
     __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(base + OFF_MISC); }
 };
 
-// Bounded wait that also gives up as soon as another role has aborted.
+// Bounded wait that also gives up as soon as another role has aborted.  The
+// waiting thread sleeps in try_wait (up to kSuspendNs per round) rather than
+// spinning, so idle roles leave the issue slots to the softmax and converter.
+constexpr uint32_t kSuspendNs = 100000;
 __device__ __forceinline__ bool wait_abortable(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, kSuspendNs)) {
         if (*abort_flag) return false;
         if (clock64() - t0 > kWaitBudgetCycles) {
             *abort_flag = 1;
@@ -152,13 +170,25 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         "r"(0u), "r"(0u), "r"(0u));
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
-        "%13,%14,%15,%16};"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
         ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
-        "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]),
-        "r"(v[14]), "r"(v[15])
+        "r"(v[7])
         : "memory");
 }
 
@@ -182,24 +212,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// tcgen05.ld without the wait; call tmem_wait_ld() before using v.
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float (&v)[32]) {
-    uint32_t* r = reinterpret_cast<uint32_t*>(v);
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-          "=r"(r[31])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
@@ -287,6 +299,42 @@ __device__ __forceinline__ void named_bar(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Named barrier that also ORs a flag over its threads: every participant
+// learns whether any of them failed, so all leave a loop at the same point.
+__device__ __forceinline__ bool bar_any(int id, int threads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "bar.red.or.pred p, %1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(id), "r"(threads), "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+
+
+
+// Output row of query row r of this CTA's block.  Recomputed from the block
+// index (read through asm volatile, so the compiler cannot reuse the values
+// from the kernel's start): nothing of it stays live through the tile loop,
+// whose register pressure is at the limit.
+__device__ __forceinline__ float* out_row(const PrefillArgs& a, int r, bool& live) {
+    uint32_t bid;
+    asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(bid));
+    const int H = a.num_heads, HKV = a.num_kv_heads, GROUP = H / HKV;
+    const int nqb = (a.n_new + BM - 1) / BM;
+    int idx = (int)bid;
+    const int jh = idx % GROUP;  idx /= GROUP;
+    const int qb = nqb - 1 - (idx % nqb);  idx /= nqb;
+    const int h = idx % HKV + HKV * jh;
+    const int seq = idx / HKV;
+    const int qpos = qb * BM + r;
+    live = qpos < a.n_new;
+    return a.out + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmap_k,
                    const __grid_constant__ CUtensorMap tmap_v, const PrefillArgs a) {
@@ -323,17 +371,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(S.bar(B_KV_FULL + i), 1);
             mbar_init(S.bar(B_KV_EMPTY + i), 4);
-            mbar_init(S.bar(B_KC_FULL + i), 4);
-            mbar_init(S.bar(B_KC_FREE + i), 1);
             mbar_init(S.bar(B_VC_FULL + i), 4);
             mbar_init(S.bar(B_VC_FREE + i), 1);
         }
+        mbar_init(S.bar(B_KC_FULL), 4);
+        mbar_init(S.bar(B_KC_FREE), 1);
         for (int i = 0; i < NSP; ++i) {
             mbar_init(S.bar(B_S_FULL + i), 1);
-            mbar_init(S.bar(B_P_FULL + i), 4);
+            mbar_init(S.bar(B_P_FULL + i), 8);
             mbar_init(S.bar(B_PV_BUF + i), 1);
         }
-        mbar_init(S.bar(B_Q_FULL), 4);
+        mbar_init(S.bar(B_Q_FULL), 8);
         mbar_init(S.bar(B_DRAIN), 1);
         *S.abort_flag() = 0;
         fence_mbar_init();
@@ -349,15 +397,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *S.tmem_slot();
     volatile int* abort_flag = S.abort_flag();
     uint8_t* Qs = S.base + OFF_Q;
+    uint8_t* Kc = S.base + OFF_K;
     uint8_t* I8 = S.base + OFF_I8;
-    float* sc_k = reinterpret_cast<float*>(S.base + OFF_SC);
-    float* sc_v = sc_k + BN;
-    auto Kc = [&](int b) { return S.base + OFF_K + b * 2 * ATOM; };
     auto Vc = [&](int b) { return S.base + OFF_V + b * 2 * ATOM; };
 
-    if (warp == kProducerWarp) {
-        // ================================================================ TMA
-        if (lane == 0) {
+    if (warp >= kProducerWarp) {
+        if (warp == kProducerWarp && lane == 0) {
+            // ============================================================ TMA
             const uint64_t pol = l2_policy_evict_first();
             int issued = 0;
             for (int j = 0; j < ntiles; ++j) {
@@ -377,27 +423,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                        clock64() - t0 < kWaitBudgetCycles) {
                 }
             }
-        }
-    } else if (warp == kMmaWarp) {
-        // ================================================================ MMA
-        if (lane == 0) {
+        } else if (warp == kMmaWarp && lane == 0) {
+            // ============================================================ MMA
             bool ok = wait_abortable(S.bar(B_Q_FULL), 0, abort_flag);
-            // QK^T of tile j into S/P buffer j % 3
+            // S = Q K^T of tile j into S/P buffer j % 3
             auto qk = [&](int j) -> bool {
-                const int kb = j & 1, sb = j % NSP;
-                if (!wait_abortable(S.bar(B_KC_FULL + kb), (j >> 1) & 1, abort_flag)) return false;
+                const int sb = j % NSP;
+                if (!wait_abortable(S.bar(B_KC_FULL), j & 1, abort_flag)) return false;
                 if (j >= NSP && !wait_abortable(S.bar(B_PV_BUF + sb), ((j / NSP) - 1) & 1, abort_flag))
                     return false;   // PV of tile j - 3 has read its p' out of this buffer
                 tc_fence_after();
-                const uint8_t* kc = Kc(kb);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const int o = (kk >> 2) * ATOM + (kk & 3) * 32;
-                    umma(tmem + sb * BN, umma_desc(Qs + o, 16, 1024), umma_desc(kc + o, 16, 1024),
+                    umma(tmem + sb * BN, umma_desc(Qs + o, 16, 1024), umma_desc(Kc + o, 16, 1024),
                          kIdescQK, kk > 0);
                 }
                 umma_commit(S.bar(B_S_FULL + sb));
-                umma_commit(S.bar(B_KC_FREE + kb));
+                umma_commit(S.bar(B_KC_FREE));
                 return true;
             };
             if (ok) ok = qk(0);
@@ -411,12 +454,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint8_t* vc = Vc(vb);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    // tokens 16kk..16kk+15: chunk kk/2 of 32 tokens holds hi in its
-                    // first 16 columns and lo in the next 16
-                    const uint32_t a = tmem + sb * BN + 32 * (kk >> 1) + 8 * (kk & 1);
+                    // tokens 16kk..16kk+15: p' hi in columns 16kk..16kk+7, lo in
+                    // the next 8 (two f16 per column)
+                    const uint32_t at = tmem + sb * BN + 16 * kk;
                     const uint64_t vbd = umma_desc(vc + kk * 16 * 128, ATOM, 1024);
-                    umma_ts(tmem + TM_O, a, vbd, kIdescPV, j > 0 || kk > 0);
-                    umma_ts(tmem + TM_O, a + 16, vbd, kIdescPV, true);
+                    umma_ts(tmem + TM_O, at, vbd, kIdescPV, j > 0 || kk > 0);
+                    umma_ts(tmem + TM_O, at + 8, vbd, kIdescPV, true);
                 }
                 umma_commit(S.bar(B_PV_BUF + sb));
                 umma_commit(S.bar(B_VC_FREE + vb));
@@ -428,46 +471,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             while (!mbar_try_wait(S.bar(B_DRAIN), 0) && clock64() - t0 < kWaitBudgetCycles) {
             }
         }
-    } else if (warp >= 4) {
+    } else if (warp >= kConvWarp0) {
         // ================================================================ convert
-        const int t = threadIdx.x - 128;     // token row of the tile
+        const int t = threadIdx.x - kConvWarp0 * 32;     // token row of the tile
         for (int j = 0; j < ntiles; ++j) {
-            const int st = j & 1, b = j & 1;
+            const int st = j & 1;
             if (!warp_wait_abortable(S.bar(B_KV_FULL + st), (j >> 1) & 1, abort_flag)) break;
-            if (j >= 2 && !warp_wait_abortable(S.bar(B_KC_FREE + b), ((j >> 1) - 1) & 1, abort_flag)) break;
-            convert_k_row(I8 + (2 * st) * I8_TILE, Kc(b), t);
+            // QK of the previous tile has finished reading the converted K
+            if (j >= 1 && !warp_wait_abortable(S.bar(B_KC_FREE), (j - 1) & 1, abort_flag)) break;
+            convert_k_row(I8 + (2 * st) * I8_TILE, Kc, t);
             fence_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(S.bar(B_KC_FULL + b));
-            if (j >= 2 && !warp_wait_abortable(S.bar(B_VC_FREE + b), ((j >> 1) - 1) & 1, abort_flag)) break;
-            convert_v_row(I8 + (2 * st + 1) * I8_TILE, Vc(b), t);
+            if (lane == 0) mbar_arrive(S.bar(B_KC_FULL));
+            if (j >= 2 && !warp_wait_abortable(S.bar(B_VC_FREE + st), ((j >> 1) - 1) & 1, abort_flag)) break;
+            convert_v_row(I8 + (2 * st + 1) * I8_TILE, Vc(st), t);
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(S.bar(B_VC_FULL + b));
+                mbar_arrive(S.bar(B_VC_FULL + st));
                 mbar_arrive(S.bar(B_KV_EMPTY + st));
             }
         }
     } else {
         // ================================================================ softmax
-        const int r = threadIdx.x;             // query row of the block == TMEM lane
+        const int st = threadIdx.x;            // 0..255
+        const int half = warp >> 2;            // column half of every tile
+        const int c0 = half * 64;
+        const int r = (warp & 3) * 32 + lane;  // query row of the block == TMEM lane
         const bool live = r < rows;
         const int qpos = q0 + r;               // row within the appended chunk
         const int limit = live ? past + qpos : -1;   // last kv slot this row may see
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        float* scb = reinterpret_cast<float*>(S.base + OFF_SC);
+        float* red = reinterpret_cast<float*>(S.base + OFF_RED);
 
-        // Q row -> bf16, K-major swizzled
+        // Q row -> bf16, K-major swizzled: this thread's 64 dims are K-block `half`
         {
-            const float* qp = a.q + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D;
+            const float* qp =
+                a.q + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D + c0;
+            uint8_t* blk = Qs + half * ATOM;
 #pragma unroll 4
-            for (int c = 0; c < 16; ++c) {   // 16 chunks of 8 dims
+            for (int c = 0; c < 8; ++c) {   // 8 chunks of 8 dims
                 float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
                 if (live) {
                     x0 = reinterpret_cast<const float4*>(qp)[2 * c];
                     x1 = reinterpret_cast<const float4*>(qp)[2 * c + 1];
                 }
-                uint8_t* blk = Qs + (c >> 3) * ATOM;
-                *reinterpret_cast<uint4*>(blk + swz(r, c & 7)) =
+                *reinterpret_cast<uint4*>(blk + swz(r, c)) =
                     make_uint4(pack_bf16(x0.x, x0.y), pack_bf16(x0.z, x0.w), pack_bf16(x1.x, x1.y),
                                pack_bf16(x1.z, x1.w));
             }
@@ -476,62 +526,60 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(S.bar(B_Q_FULL));
         }
 
-        auto scale_at = [&](const float* arr, int slot) -> float {
-            return a.row_scales ? arr[slot] : arr[(size_t)slot * HKV + g];
+        // per-token scales of a tile: thread st loads k-scale * qk_mul of column
+        // st (st < 128) or v-scale of column st - 128, one tile ahead
+        const int sc_col = st & (BN - 1);
+        const float* sc_src = st < BN ? a.key_scales : a.val_scales;
+        const float sc_mul = st < BN ? a.qk_mul : 1.0f;
+        auto load_scale = [&](int j) -> float {
+            const int slot = off + j * BN + sc_col;
+            if (j * BN + sc_col >= len) return 0.0f;
+            return (a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g]) * sc_mul;
         };
-        // per-token scales of tile j for column r (prefetched one tile ahead)
-        auto load_scales = [&](int j, float& ks, float& vs) {
-            const int slot = off + j * BN + r;
-            const bool in = j * BN + r < len;
-            ks = in ? scale_at(a.key_scales, slot) * a.qk_mul : 0.0f;
-            vs = in ? scale_at(a.val_scales, slot) : 0.0f;
-        };
-        float ks_next, vs_next;
-        load_scales(0, ks_next, vs_next);
-        float m_run = -INFINITY, l_run = 0.0f;
-        bool ok = true;
+        float sc_next = load_scale(0);
+        float m_run = -INFINITY, l_run = 0.0f;   // l_run: this thread's columns only
+        bool bad = false;                        // a bounded wait of this warp gave up
 
-        for (int j = 0; j < ntiles && ok; ++j) {
-            const int sb = j % NSP;
-            named_bar(2, 128);        // previous tile's scales are no longer read
-            sc_k[r] = ks_next;
-            sc_v[r] = vs_next;
-            named_bar(2, 128);
-            if (j + 1 < ntiles) load_scales(j + 1, ks_next, vs_next);
-
-            if (!warp_wait_abortable(S.bar(B_S_FULL + sb), (j / NSP) & 1, abort_flag)) { ok = false; break; }
+        int j = 0;
+        for (; j < ntiles; ++j) {
+            const int sb = j % NSP, par = j & 1;
+            float* sck = scb + par * 2 * BN;
+            sck[st] = sc_next;
+            if (j + 1 < ntiles) sc_next = load_scale(j + 1);
+            bad |= !warp_wait_abortable(S.bar(B_S_FULL + sb), (j / NSP) & 1, abort_flag);
+            // tile j's scales are visible to all, and all agree whether to go on
+            if (bar_any(1, kSoftmaxThreads, bad)) break;
             tc_fence_after();
-            const uint32_t s_addr = lane_base + sb * BN;
-            const int kv0 = j * BN;
+            const uint32_t s_addr = lane_base + sb * BN + c0;
+            const int kv0 = j * BN + c0;
             // columns past a row's causal limit exist only near the diagonal or
             // in a partial block (rows >= `rows` have limit -1)
-            const bool masked_tile = kv0 + BN - 1 > past + q0 || rows < BM;
-            const float4* sk4 = reinterpret_cast<const float4*>(sc_k);
-            const float4* sv4 = reinterpret_cast<const float4*>(sc_v);
-            // pass 1: row max of s = S * k_scale * qk_mul
+            const bool masked_tile = j * BN + BN - 1 > past + q0 || rows < BM;
+            const float4* sk4 = reinterpret_cast<const float4*>(sck + c0);
+            const float4* sv4 = reinterpret_cast<const float4*>(sck + BN + c0);
+            // pass 1: max over this thread's 64 columns of s = S * k_scale * qk_mul
             float tmax = -INFINITY;
 #pragma unroll
-            for (int k = 0; k < 4; k += 2) {
-                float v0[32], v1[32];
-                tmem_ld32_nowait(s_addr + 32 * k, v0);
-                tmem_ld32_nowait(s_addr + 32 * k + 32, v1);
-                tmem_wait_ld();
+            for (int k = 0; k < 2; ++k) {
+                float v0[32];
+                tmem_ld32(s_addr + 32 * k, v0);
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
-                    const float4 ka = sk4[(32 * k + i) / 4], kb = sk4[(32 * k + 32 + i) / 4];
+                    const float4 ka = sk4[(32 * k + i) / 4];
                     float a4[4] = {v0[i] * ka.x, v0[i + 1] * ka.y, v0[i + 2] * ka.z, v0[i + 3] * ka.w};
-                    float b4[4] = {v1[i] * kb.x, v1[i + 1] * kb.y, v1[i + 2] * kb.z, v1[i + 3] * kb.w};
                     if (masked_tile) {
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) {
+                        for (int u = 0; u < 4; ++u)
                             if (kv0 + 32 * k + i + u > limit) a4[u] = -INFINITY;
-                            if (kv0 + 32 * k + 32 + i + u > limit) b4[u] = -INFINITY;
-                        }
                     }
                     tmax = fmaxf(tmax, fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3])));
-                    tmax = fmaxf(tmax, fmaxf(fmaxf(b4[0], b4[1]), fmaxf(b4[2], b4[3])));
                 }
             }
+            // row maximum over both halves (both threads of a row compute the
+            // same m_run, corr and p scale from it)
+            red[(par * 2 + half) * BM + r] = tmax;
+            named_bar(1, kSoftmaxThreads);
+            tmax = fmaxf(tmax, red[(par * 2 + (half ^ 1)) * BM + r]);
             float corr = 1.0f;
             if (tmax > m_run + kLazyRescale) {
                 corr = fast_exp2(m_run - tmax);
@@ -540,33 +588,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             l_run *= corr;
             const float neg_m = m_run == -INFINITY ? 0.0f : -m_run;
 
-            // rescale O only when some row's maximum jumped (rare): O must
-            // first hold every earlier tile's contribution
+            // rescale this thread's half of the O row only when some row's
+            // maximum jumped (rare): O must first hold every earlier tile
             if (j >= 1 && __any_sync(kFull, corr != 1.0f)) {
                 const int pj = j - 1;
-                if (!warp_wait_abortable(S.bar(B_PV_BUF + pj % NSP), (pj / NSP) & 1, abort_flag)) { ok = false; break; }
-                tc_fence_after();
+                if (warp_wait_abortable(S.bar(B_PV_BUF + pj % NSP), (pj / NSP) & 1, abort_flag)) {
+                    tc_fence_after();
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    float o[32];
-                    tmem_ld32(lane_base + TM_O + 32 * k, o);
+                    for (int k = 0; k < 2; ++k) {
+                        float o[32];
+                        tmem_ld32(lane_base + TM_O + c0 + 32 * k, o);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= corr;
-                    tmem_st32(lane_base + TM_O + 32 * k, o);
+                        for (int i = 0; i < 32; ++i) o[i] *= corr;
+                        tmem_st32(lane_base + TM_O + c0 + 32 * k, o);
+                    }
+                } else {
+                    bad = true;
                 }
             }
             // pass 2: p' = 2^(s - m) * v_scale as an f16 pair hi + lo (hi =
             // f16(p'), lo = f16(p' - hi)), written over the chunk's own S
-            // columns once they have been read: chunk k (tokens 32k..32k+31)
-            // keeps hi in its first 16 columns and lo in the next 16
+            // columns once they have been read: 16 tokens 16k..16k+15 keep hi
+            // in their first 8 columns and lo in the next 8
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                float v[32];
-                tmem_ld32(s_addr + 32 * k, v);
-                uint32_t hi[16], lo[16];
+                float v[16];
+                tmem_ld16(s_addr + 16 * k, v);
+                uint32_t hi[8], lo[8];
 #pragma unroll
-                for (int u = 0; u < 32; u += 4) {
-                    const int c = 32 * k + u;
+                for (int u = 0; u < 16; u += 4) {
+                    const int c = 16 * k + u;
                     const float4 kf = sk4[c / 4], vf = sv4[c / 4];
                     float e[4] = {fmaf(v[u], kf.x, neg_m), fmaf(v[u + 1], kf.y, neg_m),
                                   fmaf(v[u + 2], kf.z, neg_m), fmaf(v[u + 3], kf.w, neg_m)};
@@ -589,33 +640,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                         lo[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&ll);
                     }
                 }
-                tmem_st16(s_addr + 32 * k, hi);
-                tmem_st16(s_addr + 32 * k + 16, lo);
+                tmem_st8(s_addr + 16 * k, hi);
+                tmem_st8(s_addr + 16 * k + 8, lo);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(S.bar(B_P_FULL + sb));
         }
-        // ---- epilogue: O / l for live rows
-        const int lj = ntiles - 1;
-        if (ok && warp_wait_abortable(S.bar(B_PV_BUF + lj % NSP), (lj / NSP) & 1, abort_flag)) {
+        // ---- epilogue: O / l for live rows, l summed over both halves
+        const bool ran = j == ntiles;
+        if (ran) {
+            const int lj = ntiles - 1;
+            bad |= !warp_wait_abortable(S.bar(B_PV_BUF + lj % NSP), (lj / NSP) & 1, abort_flag);
+            red[((ntiles & 1) * 2 + half) * BM + r] = l_run;
+        }
+        // every softmax thread reaches this barrier exactly once
+        const bool failed = bar_any(1, kSoftmaxThreads, bad || !ran);
+        if (!failed) {
             tc_fence_after();
-            float* op = a.out + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D;
-            const float inv = (live && l_run > 0.0f) ? __fdiv_rn(1.0f, l_run) : 0.0f;
+            const float l = l_run + red[((ntiles & 1) * 2 + (half ^ 1)) * BM + r];
+            bool row_live;
+            float* op = out_row(a, r, row_live) + c0;
+            const uint32_t o_base = *S.tmem_slot() + ((uint32_t)((warp & 3) * 32) << 16) + TM_O + c0;
+            const float inv = (row_live && l > 0.0f) ? __fdiv_rn(1.0f, l) : 0.0f;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < 2; ++k) {
                 float o[32];
-                tmem_ld32(lane_base + TM_O + 32 * k, o);
-                if (live) {
+                tmem_ld32(o_base + 32 * k, o);
+                if (row_live) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
                         reinterpret_cast<float4*>(op + 32 * k)[i / 4] =
                             make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
                 }
             }
+        } else if (lane == 0) {
+            flag_error(a.err, EC_DEVERR_TIMEOUT);
         }
-        if (!ok && lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
     }
 
     tc_fence_before();
