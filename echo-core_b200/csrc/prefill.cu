@@ -170,23 +170,43 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         "r"(0u), "r"(0u), "r"(0u));
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
+// 16-lane tensor-memory shapes.  For a base address at lane L, column C and
+// thread t (g = t / 4, q = t % 4):
+//   16x256b, repetition n: v[4n+0], v[4n+1] = lane L+g,   columns C+8n+2q, +1
+//                          v[4n+2], v[4n+3] = lane L+g+8, the same columns
+//   16x128b, repetition r: v[2r+0] = lane L+g, column C+4r+q; v[2r+1] = lane L+g+8
+#define EC_R4(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3])
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : EC_R4(0), EC_R4(4) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : EC_R4(0), EC_R4(4), EC_R4(8), EC_R4(12), EC_R4(16), EC_R4(20), EC_R4(24), EC_R4(28)
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+#undef EC_R4
+__device__ __forceinline__ void tmem_st_16x256b_x2(uint32_t taddr, const float (&v)[8]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+        "tcgen05.st.sync.aligned.16x256b.x2.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+        ::"r"(taddr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]),
+        "f"(v[7])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st_16x128b_x4(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x128b.x4.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
         ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
         "r"(v[7])
         : "memory");
@@ -195,42 +215,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(smem_addr(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-          "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
-        "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
-        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
-        "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])),
-        "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
-        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
-        "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
-        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
-        "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
-        "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
-        "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-        : "memory");
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Byte offset of 16-byte chunk c of row r in a [rows][128 B] 128B-swizzled block.
@@ -500,8 +484,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = (warp & 3) * 32 + lane;  // query row of the block == TMEM lane
         const bool live = r < rows;
         const int qpos = q0 + r;               // row within the appended chunk
-        const int limit = live ? past + qpos : -1;   // last kv slot this row may see
-        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         float* scb = reinterpret_cast<float*>(S.base + OFF_SC);
         float* red = reinterpret_cast<float*>(S.base + OFF_RED);
 
@@ -536,9 +518,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (j * BN + sc_col >= len) return 0.0f;
             return (a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g]) * sc_mul;
         };
+
+        // From here on a thread works in the 16-lane layout: quad g = lane / 4,
+        // q = lane % 4.  It owns the rows rw[k] = 32*(warp%4) + 16*(k/2) + g +
+        // 8*(k%2) (k = 0..3) and, in every tile, the 16 columns c0 + 8n + 2q,
+        // c0 + 8n + 2q + 1 (n = 0..7), so its 32 per-column scales sit in
+        // registers for the whole tile.  A row's 64 columns of this half are
+        // spread over the four threads of a quad.
+        const int gq = lane >> 2, qq = lane & 3;
+        int rlim[4];                               // last kv slot each row may see
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int rw = (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1);
+            rlim[k] = rw < rows ? past + q0 + rw : -1;
+        }
+        auto lanes_of = [&](int blk) -> uint32_t {  // TMEM lane field of block blk
+            return (uint32_t)((warp & 3) * 32 + 16 * blk) << 16;
+        };
+
         float sc_next = load_scale(0);
-        float m_run = -INFINITY, l_run = 0.0f;   // l_run: this thread's columns only
-        bool bad = false;                        // a bounded wait of this warp gave up
+        float m_run[4], l_run[4];                  // l_run: this thread's columns only
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { m_run[k] = -INFINITY; l_run[k] = 0.0f; }
+        bool bad = false;                          // a bounded wait of this warp gave up
 
         int j = 0;
         for (; j < ntiles; ++j) {
@@ -550,129 +552,184 @@ __global__ void __launch_bounds__(kThreads, 1)
             // tile j's scales are visible to all, and all agree whether to go on
             if (bar_any(1, kSoftmaxThreads, bad)) break;
             tc_fence_after();
-            const uint32_t s_addr = lane_base + sb * BN + c0;
-            const int kv0 = j * BN + c0;
+            float ks[16], vs[16];                  // scales of this thread's columns
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                const float2 k2 = *reinterpret_cast<const float2*>(sck + c0 + 8 * n + 2 * qq);
+                const float2 v2 = *reinterpret_cast<const float2*>(sck + BN + c0 + 8 * n + 2 * qq);
+                ks[2 * n] = k2.x; ks[2 * n + 1] = k2.y;
+                vs[2 * n] = v2.x; vs[2 * n + 1] = v2.y;
+            }
+            const uint32_t s_col = tmem + sb * BN + c0;
+            const int kv0 = j * BN + c0 + 2 * qq;  // kv slot of column c0 + 2q
             // columns past a row's causal limit exist only near the diagonal or
             // in a partial block (rows >= `rows` have limit -1)
             const bool masked_tile = j * BN + BN - 1 > past + q0 || rows < BM;
-            const float4* sk4 = reinterpret_cast<const float4*>(sck + c0);
-            const float4* sv4 = reinterpret_cast<const float4*>(sck + BN + c0);
-            // pass 1: max over this thread's 64 columns of s = S * k_scale * qk_mul
-            float tmax = -INFINITY;
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                float v0[32];
-                tmem_ld32(s_addr + 32 * k, v0);
-#pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    const float4 ka = sk4[(32 * k + i) / 4];
-                    float a4[4] = {v0[i] * ka.x, v0[i + 1] * ka.y, v0[i + 2] * ka.z, v0[i + 3] * ka.w};
-                    if (masked_tile) {
-#pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            if (kv0 + 32 * k + i + u > limit) a4[u] = -INFINITY;
-                    }
-                    tmax = fmaxf(tmax, fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3])));
-                }
-            }
-            // row maximum over both halves (both threads of a row compute the
-            // same m_run, corr and p scale from it)
-            red[(par * 2 + half) * BM + r] = tmax;
-            named_bar(1, kSoftmaxThreads);
-            tmax = fmaxf(tmax, red[(par * 2 + (half ^ 1)) * BM + r]);
-            float corr = 1.0f;
-            if (tmax > m_run + kLazyRescale) {
-                corr = fast_exp2(m_run - tmax);
-                m_run = tmax;
-            }
-            l_run *= corr;
-            const float neg_m = m_run == -INFINITY ? 0.0f : -m_run;
 
-            // rescale this thread's half of the O row only when some row's
-            // maximum jumped (rare): O must first hold every earlier tile
-            if (j >= 1 && __any_sync(kFull, corr != 1.0f)) {
+            // pass 1: row maxima of s = S * k_scale * qk_mul over this half
+            float tmax[4];
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                float v[32];
+                tmem_ld_16x256b_x8(s_col + lanes_of(blk), v);
+                float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+                for (int n = 0; n < 8; ++n) {
+                    float a0 = v[4 * n] * ks[2 * n], a1 = v[4 * n + 1] * ks[2 * n + 1];
+                    float b0 = v[4 * n + 2] * ks[2 * n], b1 = v[4 * n + 3] * ks[2 * n + 1];
+                    if (masked_tile) {
+                        const int c = kv0 + 8 * n;
+                        if (c > rlim[2 * blk]) a0 = -INFINITY;
+                        if (c + 1 > rlim[2 * blk]) a1 = -INFINITY;
+                        if (c > rlim[2 * blk + 1]) b0 = -INFINITY;
+                        if (c + 1 > rlim[2 * blk + 1]) b1 = -INFINITY;
+                    }
+                    m0 = fmaxf(m0, fmaxf(a0, a1));
+                    m1 = fmaxf(m1, fmaxf(b0, b1));
+                }
+                tmax[2 * blk] = m0;
+                tmax[2 * blk + 1] = m1;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                tmax[k] = fmaxf(tmax[k], __shfl_xor_sync(kFull, tmax[k], 1));
+                tmax[k] = fmaxf(tmax[k], __shfl_xor_sync(kFull, tmax[k], 2));
+            }
+            // row maximum over both halves (every thread of a row computes the
+            // same m_run, corr and p scale from it)
+            if (qq == 0) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    red[(par * 2 + half) * BM + (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)] =
+                        tmax[k];
+            }
+            named_bar(1, kSoftmaxThreads);
+            float corr[4], neg_m[4];
+            bool any_corr = false;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float t = fmaxf(
+                    tmax[k],
+                    red[(par * 2 + (half ^ 1)) * BM + (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)]);
+                corr[k] = 1.0f;
+                if (t > m_run[k] + kLazyRescale) {
+                    corr[k] = fast_exp2(m_run[k] - t);
+                    m_run[k] = t;
+                    any_corr = true;
+                }
+                l_run[k] *= corr[k];
+                neg_m[k] = m_run[k] == -INFINITY ? 0.0f : -m_run[k];
+            }
+
+            // rescale this half of the O rows only when some row's maximum
+            // jumped (rare): O must first hold every earlier tile
+            if (j >= 1 && __any_sync(kFull, any_corr)) {
                 const int pj = j - 1;
                 if (warp_wait_abortable(S.bar(B_PV_BUF + pj % NSP), (pj / NSP) & 1, abort_flag)) {
                     tc_fence_after();
 #pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                        float o[32];
-                        tmem_ld32(lane_base + TM_O + c0 + 32 * k, o);
+                    for (int blk = 0; blk < 2; ++blk) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= corr;
-                        tmem_st32(lane_base + TM_O + c0 + 32 * k, o);
+                        for (int G = 0; G < 4; ++G) {
+                            float o[8];
+                            const uint32_t oa = tmem + TM_O + c0 + 16 * G + lanes_of(blk);
+                            tmem_ld_16x256b_x2(oa, o);
+#pragma unroll
+                            for (int i = 0; i < 8; i += 4) {
+                                o[i] *= corr[2 * blk];
+                                o[i + 1] *= corr[2 * blk];
+                                o[i + 2] *= corr[2 * blk + 1];
+                                o[i + 3] *= corr[2 * blk + 1];
+                            }
+                            tmem_st_16x256b_x2(oa, o);
+                        }
                     }
                 } else {
                     bad = true;
                 }
             }
             // pass 2: p' = 2^(s - m) * v_scale as an f16 pair hi + lo (hi =
-            // f16(p'), lo = f16(p' - hi)), written over the chunk's own S
-            // columns once they have been read: 16 tokens 16k..16k+15 keep hi
-            // in their first 8 columns and lo in the next 8
+            // f16(p'), lo = f16(p' - hi)), written over the S columns just
+            // read.  Tokens 16G..16G+15 of the half keep their hi words (token
+            // pairs) in columns 16G..16G+7 and lo words in the next 8.
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float v[16];
-                tmem_ld16(s_addr + 16 * k, v);
-                uint32_t hi[8], lo[8];
+            for (int blk = 0; blk < 2; ++blk) {
 #pragma unroll
-                for (int u = 0; u < 16; u += 4) {
-                    const int c = 16 * k + u;
-                    const float4 kf = sk4[c / 4], vf = sv4[c / 4];
-                    float e[4] = {fmaf(v[u], kf.x, neg_m), fmaf(v[u + 1], kf.y, neg_m),
-                                  fmaf(v[u + 2], kf.z, neg_m), fmaf(v[u + 3], kf.w, neg_m)};
-                    if (masked_tile) {
+                for (int G = 0; G < 4; ++G) {
+                    float v[8];
+                    const uint32_t ga = s_col + 16 * G + lanes_of(blk);
+                    tmem_ld_16x256b_x2(ga, v);
+                    uint32_t w[8];
 #pragma unroll
-                        for (int w = 0; w < 4; ++w)
-                            if (kv0 + c + w > limit) e[w] = -INFINITY;
+                    for (int h2 = 0; h2 < 2; ++h2) {          // repetition n = 2G + h2
+                        const int n = 2 * G + h2;
+#pragma unroll
+                        for (int rr = 0; rr < 2; ++rr) {      // row g or g + 8
+                            const int k = 2 * blk + rr;
+                            float e0 = fmaf(v[4 * h2 + 2 * rr], ks[2 * n], neg_m[k]);
+                            float e1 = fmaf(v[4 * h2 + 2 * rr + 1], ks[2 * n + 1], neg_m[k]);
+                            if (masked_tile) {
+                                const int c = kv0 + 8 * n;
+                                if (c > rlim[k]) e0 = -INFINITY;
+                                if (c + 1 > rlim[k]) e1 = -INFINITY;
+                            }
+                            const float p0 = fast_exp2(e0), p1 = fast_exp2(e1);
+                            l_run[k] += p0 + p1;
+                            const float pv0 = p0 * vs[2 * n], pv1 = p1 * vs[2 * n + 1];
+                            const __half2 hh = __floats2half2_rn(pv0, pv1);
+                            const float2 hf = __half22float2(hh);
+                            const __half2 ll = __floats2half2_rn(pv0 - hf.x, pv1 - hf.y);
+                            w[2 * h2 + rr] = *reinterpret_cast<const uint32_t*>(&hh);
+                            w[4 + 2 * h2 + rr] = *reinterpret_cast<const uint32_t*>(&ll);
+                        }
                     }
-                    float pr[4];
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) pr[w] = fast_exp2(e[w]);
-                    l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
-                    const float pv[4] = {pr[0] * vf.x, pr[1] * vf.y, pr[2] * vf.z, pr[3] * vf.w};
-#pragma unroll
-                    for (int w = 0; w < 4; w += 2) {
-                        const __half2 hh = __floats2half2_rn(pv[w], pv[w + 1]);
-                        const float2 hf = __half22float2(hh);
-                        const __half2 ll = __floats2half2_rn(pv[w] - hf.x, pv[w + 1] - hf.y);
-                        hi[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&hh);
-                        lo[(u + w) / 2] = *reinterpret_cast<const uint32_t*>(&ll);
-                    }
+                    tmem_st_16x128b_x4(ga, w);
                 }
-                tmem_st8(s_addr + 16 * k, hi);
-                tmem_st8(s_addr + 16 * k + 8, lo);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(S.bar(B_P_FULL + sb));
         }
-        // ---- epilogue: O / l for live rows, l summed over both halves
+        // ---- epilogue: O / l for live rows, l summed over the quad and both halves
         const bool ran = j == ntiles;
         if (ran) {
             const int lj = ntiles - 1;
             bad |= !warp_wait_abortable(S.bar(B_PV_BUF + lj % NSP), (lj / NSP) & 1, abort_flag);
-            red[((ntiles & 1) * 2 + half) * BM + r] = l_run;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                l_run[k] += __shfl_xor_sync(kFull, l_run[k], 1);
+                l_run[k] += __shfl_xor_sync(kFull, l_run[k], 2);
+            }
+            if (qq == 0) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    red[((ntiles & 1) * 2 + half) * BM + (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)] =
+                        l_run[k];
+            }
         }
         // every softmax thread reaches this barrier exactly once
         const bool failed = bar_any(1, kSoftmaxThreads, bad || !ran);
         if (!failed) {
             tc_fence_after();
-            const float l = l_run + red[((ntiles & 1) * 2 + (half ^ 1)) * BM + r];
-            bool row_live;
-            float* op = out_row(a, r, row_live) + c0;
-            const uint32_t o_base = *S.tmem_slot() + ((uint32_t)((warp & 3) * 32) << 16) + TM_O + c0;
-            const float inv = (row_live && l > 0.0f) ? __fdiv_rn(1.0f, l) : 0.0f;
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
+            for (int blk = 0; blk < 2; ++blk) {
                 float o[32];
-                tmem_ld32(o_base + 32 * k, o);
-                if (row_live) {
+                tmem_ld_16x256b_x8(*S.tmem_slot() + TM_O + c0 + lanes_of(blk), o);
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        reinterpret_cast<float4*>(op + 32 * k)[i / 4] =
-                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                for (int rr = 0; rr < 2; ++rr) {
+                    const int k = 2 * blk + rr;
+                    const int rw = (warp & 3) * 32 + 16 * blk + gq + 8 * rr;
+                    const float l = l_run[k] + red[((ntiles & 1) * 2 + (half ^ 1)) * BM + rw];
+                    bool row_live;
+                    float* op = out_row(a, rw, row_live) + c0 + 2 * qq;
+                    const float inv = (row_live && l > 0.0f) ? __fdiv_rn(1.0f, l) : 0.0f;
+                    if (row_live) {
+#pragma unroll
+                        for (int n = 0; n < 8; ++n)
+                            *reinterpret_cast<float2*>(op + 8 * n) =
+                                make_float2(o[4 * n + 2 * rr] * inv, o[4 * n + 2 * rr + 1] * inv);
+                    }
                 }
             }
         } else if (lane == 0) {
