@@ -32,6 +32,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "echo-core_b200"))
 
+import ranks  # noqa: E402
 import workloads as W  # noqa: E402
 
 METRIC = "INT8-KV decode attention HBM GB/s (% of peak) and decode tok/s at 32k ctx"
@@ -253,8 +254,7 @@ def run_gpu_arm(args, rank, world, local_rank):
         return run_prefill_arm(args, rank, world, local_rank)
     # ---- shard sequences
     nseq_total = cfg.num_seqs
-    lo = rank * nseq_total // world
-    hi = (rank + 1) * nseq_total // world
+    lo, hi = ranks.shard(nseq_total, rank, world)
     lens0 = cfg.ctx[lo:hi]
     nseq = hi - lo
     layers = cfg.num_layers
@@ -426,8 +426,7 @@ def run_prefill_arm(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     cfg = W.config(5)
     nseq_total = args.seqs or cfg.num_seqs
-    lo = rank * nseq_total // world
-    hi = (rank + 1) * nseq_total // world
+    lo, hi = ranks.shard(nseq_total, rank, world)
     nseq = hi - lo
     past, n_new = cfg.ctx[0], cfg.new_tokens
     gen = torch.Generator(device=dev)
@@ -521,8 +520,7 @@ def run_cp_arm(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     cfg = W.config(4)
     total = cfg.ctx[0]
-    lo = rank * total // world
-    hi = (rank + 1) * total // world
+    lo, hi = ranks.shard(total, rank, world)
     n = hi - lo
     gen = torch.Generator(device=dev)
     gen.manual_seed(cfg.seed * 1000 + rank)
@@ -532,17 +530,18 @@ def run_cp_arm(args, rank, world, local_rank):
     qg = q.clone()
     if world > 1:
         dist.broadcast(qg, 0)
-    po = torch.empty((world, 1, H, D), device=dev)
-    pml = torch.empty((world, 1, H, 2), device=dev)
+    po_local = torch.empty((1, H, D), device=dev)
+    pml_local = torch.empty((1, H, 2), device=dev)
     out = torch.empty((1, H, D), device=dev)
     scale = W.softmax_scale(D)
     stream = torch.cuda.current_stream()
 
     def step():
-        bc.decode_partial(qg, po[rank], pml[rank], H, scale, stream)
+        bc.decode_partial(qg, po_local, pml_local, H, scale, stream)
         if world > 1:
-            dist.all_gather_into_tensor(po, po[rank].contiguous())
-            dist.all_gather_into_tensor(pml, pml[rank].contiguous())
+            po, pml = ranks.gather_partials(po_local, pml_local)
+        else:
+            po, pml = po_local[None], pml_local[None]
         eckv.lse_combine(po, pml, world, 1, H, D, out, stream)
 
     for _ in range(args.warmup):

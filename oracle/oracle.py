@@ -161,6 +161,53 @@ def prefill_attention(keys, values, kscales, vscales, past_len, n_new, q, num_he
     return out.reshape(n_new, num_heads, head_dim)
 
 
+
+def decode_partial(keys, values, kscales, vscales, q, num_heads, num_kv_heads, head_dim,
+                   softmax_scale, mode=SCALE_PER_HEAD):
+    """Unnormalised partial decode state of one sequence slice, in float64:
+    per query head h, m = max_t s_t*log2(e), l = sum_t 2^(s_t*log2(e) - m),
+    o = sum_t 2^(s_t*log2(e) - m) * v_t, with s_t = softmax_scale * q_h . k_t
+    over the dequantised codes (query head h reads KV head h % num_kv_heads,
+    src/inference.cpp:335).  An empty slice gives m = -inf, l = 0, o = 0.
+    Restates the state ec_decode_attention_partial exchanges between ranks;
+    the reference itself has no such state (it keeps one sequence on one
+    device)."""
+    keys = np.asarray(keys, np.int8).reshape(-1, num_kv_heads, head_dim).astype(np.float64)
+    values = np.asarray(values, np.int8).reshape(-1, num_kv_heads, head_dim).astype(np.float64)
+    n = keys.shape[0]
+    if mode == SCALE_ROW:
+        ks = np.repeat(np.asarray(kscales, np.float64).reshape(n, 1), num_kv_heads, 1)
+        vs = np.repeat(np.asarray(vscales, np.float64).reshape(n, 1), num_kv_heads, 1)
+    else:
+        ks = np.asarray(kscales, np.float64).reshape(n, num_kv_heads)
+        vs = np.asarray(vscales, np.float64).reshape(n, num_kv_heads)
+    q = np.asarray(q, np.float64).reshape(num_heads, head_dim)
+    o = np.zeros((num_heads, head_dim))
+    ml = np.zeros((num_heads, 2))
+    for h in range(num_heads):
+        g = h % num_kv_heads
+        if n == 0:
+            ml[h] = (-np.inf, 0.0)
+            continue
+        s = softmax_scale * (keys[:, g, :] @ q[h]) * ks[:, g] * np.log2(np.e)
+        m = s.max()
+        p = np.exp2(s - m)
+        ml[h] = (m, p.sum())
+        o[h] = (p * vs[:, g]) @ values[:, g, :]
+    return o, ml
+
+
+def lse_combine(part_o, part_ml):
+    """Merges stacked partial states [parts][heads][dim], [parts][heads][2]
+    (rank order) into the normalised output [heads][dim]."""
+    part_o = np.asarray(part_o, np.float64)
+    part_ml = np.asarray(part_ml, np.float64)
+    m = part_ml[..., 0].max(axis=0)
+    w = np.where(np.isfinite(part_ml[..., 0]), np.exp2(part_ml[..., 0] - m), 0.0)
+    l = (part_ml[..., 1] * w).sum(axis=0)
+    o = (part_o * w[..., None]).sum(axis=0)
+    return o / l[:, None]
+
 # -------------------------------------------------------- the reference itself
 def ref_quantize_per_token_symmetric(x, num_tokens, num_elements):
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
