@@ -44,13 +44,14 @@ def gather_partials(part_o, part_ml, group=None):
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
-    out_o = torch.empty((world,) + tuple(part_o.shape), dtype=part_o.dtype, device=part_o.device)
-    out_ml = torch.empty((world,) + tuple(part_ml.shape), dtype=part_ml.dtype,
-                         device=part_ml.device)
+    # one collective: (O, m, l) packed per rank, split again after the gather
+    no = part_o.numel()
+    flat = torch.cat([part_o.reshape(-1), part_ml.reshape(-1)])
+    out = torch.empty((world, flat.numel()), dtype=flat.dtype, device=flat.device)
     if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(out_o, part_o.contiguous(), group=group)
-        dist.all_gather_into_tensor(out_ml, part_ml.contiguous(), group=group)
+        dist.all_gather_into_tensor(out, flat, group=group)
     else:
-        dist.all_gather(list(out_o.unbind(0)), part_o.contiguous(), group=group)
-        dist.all_gather(list(out_ml.unbind(0)), part_ml.contiguous(), group=group)
+        dist.all_gather(list(out.unbind(0)), flat, group=group)
+    out_o = out[:, :no].reshape((world,) + tuple(part_o.shape))
+    out_ml = out[:, no:].reshape((world,) + tuple(part_ml.shape))
     return out_o, out_ml
