@@ -499,7 +499,7 @@ def run_prefill_arm(args, rank, world, local_rank):
         "value": round(flops * args.steps / (ms_max * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 Q/K, f16 P/V, fp32 accumulate",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 (bf16-cast Q, exact int8 K/V codes), f16 hi/lo P, fp32 accumulate",
         "data": "synthetic", "config": {"workload": cfg.name, "seqs": nseq_total, "past": past,
                                           "new_tokens": n_new, "q_heads": H, "kv_heads": HKV,
                                           "head_dim": D, "flops_per_step": flops},

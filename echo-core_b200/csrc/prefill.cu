@@ -89,7 +89,7 @@ constexpr float kLazyRescale = 8.0f;
 constexpr unsigned kFull = 0xffffffffu;
 
 // Instruction descriptors (kind::f16, fp32 accumulate, M = 128, N = 128).
-constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | (16u << 17) | (8u << 24);
+constexpr uint32_t kIdescQK = (1u << 4) | (0u << 7) | (0u << 10) | (16u << 17) | (8u << 24);
 constexpr uint32_t kIdescPV = (1u << 4) | (0u << 7) | (0u << 10) | (1u << 16) | (16u << 17) | (8u << 24);
 
 struct Smem {
@@ -220,34 +220,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 // Byte offset of 16-byte chunk c of row r in a [rows][128 B] 128B-swizzled block.
 __device__ __forceinline__ int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// int8 code row (a 128-byte swizzled TMA row) -> bf16 K-major row t of Ks.
-__device__ __forceinline__ void convert_k_row(const uint8_t* src, uint8_t* ks, int t) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {   // source chunk c: dims 16c .. 16c+15
-        const uint4 w = *reinterpret_cast<const uint4*>(src + swz(t, c));
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-        uint32_t o[8];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            float2 lo, hi;
-            i8x4_to_f2x2(ww[q], lo, hi);
-            o[2 * q] = pack_bf16(lo.x, lo.y);
-            o[2 * q + 1] = pack_bf16(hi.x, hi.y);
-        }
-        uint8_t* blk = ks + (c >> 2) * ATOM;
-        const int cb = 2 * (c & 3);
-        *reinterpret_cast<uint4*>(blk + swz(t, cb)) = make_uint4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<uint4*>(blk + swz(t, cb + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
-    }
-}
-
-// int8 code row -> f16 MN-major token row t of Vs (two 64-dim halves).
-__device__ __forceinline__ void convert_v_row(const uint8_t* src, uint8_t* vs, int t) {
+// int8 code row (a 128-byte swizzled TMA row) -> f16 token row t of a
+// [2 dim halves][128 tokens][64 dims] 128B-swizzled operand: the K-major
+// layout of K for QK^T and the MN-major layout of V for PV are the same bytes.
+__device__ __forceinline__ void convert_row_f16(const uint8_t* src, uint8_t* vs, int t) {
     const __half2 bias = __floats2half2_rn(1152.0f, 1152.0f);  // 1024 + 128
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -463,12 +439,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!warp_wait_abortable(S.bar(B_KV_FULL + st), (j >> 1) & 1, abort_flag)) break;
             // QK of the previous tile has finished reading the converted K
             if (j >= 1 && !warp_wait_abortable(S.bar(B_KC_FREE), (j - 1) & 1, abort_flag)) break;
-            convert_k_row(I8 + (2 * st) * I8_TILE, Kc, t);
+            convert_row_f16(I8 + (2 * st) * I8_TILE, Kc, t);
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(S.bar(B_KC_FULL));
             if (j >= 2 && !warp_wait_abortable(S.bar(B_VC_FREE + st), ((j >> 1) - 1) & 1, abort_flag)) break;
-            convert_v_row(I8 + (2 * st + 1) * I8_TILE, Vc(st), t);
+            convert_row_f16(I8 + (2 * st + 1) * I8_TILE, Vc(st), t);
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -487,21 +463,53 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* scb = reinterpret_cast<float*>(S.base + OFF_SC);
         float* red = reinterpret_cast<float*>(S.base + OFF_RED);
 
-        // Q row -> bf16, K-major swizzled: this thread's 64 dims are K-block `half`
+        // Q: cast to bf16 (the contract), then scaled by 2^qe, one power of two
+        // for the whole CTA that brings max |q| into [2^14, 2^15), and stored
+        // as f16.  Every bf16 value in range is exact in f16 after that
+        // scaling (8 significant bits; only magnitudes below 2^-31 of the CTA
+        // maximum lose bits), so QK^T runs f16 x f16 with exact int8 codes as
+        // f16 K, and 2^-qe joins the k-scale multiplier.  K-major, swizzled:
+        // this thread's 64 dims are K-block `half`.
+        float q_inv = 1.0f;
         {
             const float* qp =
                 a.q + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D + c0;
+            float x[64];
+            float amax = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (live) v4 = reinterpret_cast<const float4*>(qp)[c];
+                x[4 * c] = __bfloat162float(__float2bfloat16_rn(v4.x));
+                x[4 * c + 1] = __bfloat162float(__float2bfloat16_rn(v4.y));
+                x[4 * c + 2] = __bfloat162float(__float2bfloat16_rn(v4.z));
+                x[4 * c + 3] = __bfloat162float(__float2bfloat16_rn(v4.w));
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(x[4 * c]), fabsf(x[4 * c + 1])),
+                                         fmaxf(fabsf(x[4 * c + 2]), fabsf(x[4 * c + 3]))));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, o));
+            float* qmax = red + 2 * 2 * BM - 8;    // first used by tile 1's exchange
+            if (lane == 0) qmax[warp] = amax;
+            named_bar(1, kSoftmaxThreads);
+#pragma unroll
+            for (int w = 0; w < 8; ++w) amax = fmaxf(amax, qmax[w]);
+            int qe = 0;
+            if (amax > 0.0f) {
+                int ex;
+                frexpf(amax, &ex);                 // amax = f * 2^ex, f in [0.5, 1)
+                qe = min(120, max(-120, 15 - ex));   // keeps 2^qe and 2^-qe normal
+            }
+            const float q_mul = ldexpf(1.0f, qe);
+            q_inv = ldexpf(1.0f, -qe);
             uint8_t* blk = Qs + half * ATOM;
-#pragma unroll 4
+#pragma unroll
             for (int c = 0; c < 8; ++c) {   // 8 chunks of 8 dims
-                float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-                if (live) {
-                    x0 = reinterpret_cast<const float4*>(qp)[2 * c];
-                    x1 = reinterpret_cast<const float4*>(qp)[2 * c + 1];
-                }
-                *reinterpret_cast<uint4*>(blk + swz(r, c)) =
-                    make_uint4(pack_bf16(x0.x, x0.y), pack_bf16(x0.z, x0.w), pack_bf16(x1.x, x1.y),
-                               pack_bf16(x1.z, x1.w));
+                __half2 hq[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    hq[u] = __floats2half2_rn(x[8 * c + 2 * u] * q_mul, x[8 * c + 2 * u + 1] * q_mul);
+                *reinterpret_cast<uint4*>(blk + swz(r, c)) = *reinterpret_cast<const uint4*>(hq);
             }
             fence_async_smem();
             __syncwarp();
@@ -512,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // st (st < 128) or v-scale of column st - 128, one tile ahead
         const int sc_col = st & (BN - 1);
         const float* sc_src = st < BN ? a.key_scales : a.val_scales;
-        const float sc_mul = st < BN ? a.qk_mul : 1.0f;
+        const float sc_mul = st < BN ? a.qk_mul * q_inv : 1.0f;
         auto load_scale = [&](int j) -> float {
             const int slot = off + j * BN + sc_col;
             if (j * BN + sc_col >= len) return 0.0f;

@@ -25,7 +25,7 @@ def _bf16_round(x):
     return torch.from_numpy(np.ascontiguousarray(x)).bfloat16().float().numpy()
 
 
-def _case(torch, eckv, pasts, n_new, H, hkv, seed, mode=0, rows=None):
+def _case(torch, eckv, pasts, n_new, H, hkv, seed, mode=0, rows=None, qmul=None):
     """Builds caches of `pasts` tokens, appends n_new tokens per sequence on
     the GPU, runs prefill; returns GPU output and the oracle check rows."""
     rng = np.random.default_rng(seed)
@@ -50,6 +50,8 @@ def _case(torch, eckv, pasts, n_new, H, hkv, seed, mode=0, rows=None):
     vn = np.stack([vf[p:] for (kf, vf), p in zip(seqs, pasts)])
     bc.append(torch.from_numpy(kn).cuda(), torch.from_numpy(vn).cuda(), n_new)
     q = W.queries(rng, len(pasts) * n_new, H, D).reshape(len(pasts), n_new, H, D)
+    if qmul is not None:
+        q = (q * np.asarray(qmul, np.float32).reshape(1, -1, 1, 1)).astype(np.float32)
     out = torch.full((len(pasts), n_new, H, D), float("nan"), device="cuda")
     bc.prefill(torch.from_numpy(q).cuda(), out, n_new, H, W.softmax_scale(D))
     torch.cuda.synchronize()
@@ -111,3 +113,25 @@ def test_prefill_bad_table_flagged(cuda):
     torch.cuda.synchronize()
     assert bc.device_error() == eckv.DEVERR_BAD_TABLE
     assert not out[1].cpu().numpy().any()
+
+
+@pytest.mark.parametrize("scale", [1e-3, 40.0])
+def test_prefill_query_magnitudes(cuda, scale):
+    """Queries far from unit scale (the f16 staging of Q uses one power-of-two
+    scale per CTA): tiny queries give near-uniform attention, large ones a
+    near-one-hot softmax."""
+    import torch
+    import eckv
+    for got, want, what in _case(torch, eckv, [200, 37], 150, 16, 4, 11,
+                                 qmul=np.full(150, scale)):
+        assert_attn_close(got, want, what)
+
+
+def test_prefill_mixed_row_magnitudes(cuda):
+    """Rows of one 128-row block differ by 10^5 in magnitude: the CTA-wide
+    scale comes from the largest row, the small rows keep their precision."""
+    import torch
+    import eckv
+    qmul = np.where(np.arange(128) % 3 == 0, 30.0, 3e-4)
+    for got, want, what in _case(torch, eckv, [300], 128, 8, 2, 12, qmul=qmul):
+        assert_attn_close(got, want, what)
