@@ -255,6 +255,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// max of three (one sm_100 instruction)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 __device__ __forceinline__ void named_bar(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -521,10 +528,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sc_col = st & (BN - 1);
         const float* sc_src = st < BN ? a.key_scales : a.val_scales;
         const float sc_mul = st < BN ? a.qk_mul * q_inv : 1.0f;
+        // (raw value: the multiply waits until the next tile, when the load has
+        // landed, so the in-order warp does not stall on it here)
         auto load_scale = [&](int j) -> float {
             const int slot = off + j * BN + sc_col;
             if (j * BN + sc_col >= len) return 0.0f;
-            return (a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g]) * sc_mul;
+            return a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g];
         };
 
         // From here on a thread works in the 16-lane layout: quad g = lane / 4,
@@ -554,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (; j < ntiles; ++j) {
             const int sb = j % NSP, par = j & 1;
             float* sck = scb + par * 2 * BN;
-            sck[st] = sc_next;
+            sck[st] = sc_next * sc_mul;
             if (j + 1 < ntiles) sc_next = load_scale(j + 1);
             bad |= !warp_wait_abortable(S.bar(B_S_FULL + sb), (j / NSP) & 1, abort_flag);
             // tile j's scales are visible to all, and all agree whether to go on
@@ -592,8 +601,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (c > rlim[2 * blk + 1]) b0 = -INFINITY;
                         if (c + 1 > rlim[2 * blk + 1]) b1 = -INFINITY;
                     }
-                    m0 = fmaxf(m0, fmaxf(a0, a1));
-                    m1 = fmaxf(m1, fmaxf(b0, b1));
+                    m0 = fmax3(m0, a0, a1);
+                    m1 = fmax3(m1, b0, b1);
                 }
                 tmax[2 * blk] = m0;
                 tmax[2 * blk + 1] = m1;
