@@ -184,6 +184,16 @@ __device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, float (&v)[8]
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
+        : EC_R4(0), EC_R4(4), EC_R4(8), EC_R4(12) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
     asm volatile(
@@ -672,19 +682,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int blk = 0; blk < 2; ++blk) {
 #pragma unroll
-                for (int G = 0; G < 4; ++G) {
-                    float v[8];
-                    const uint32_t ga = s_col + 16 * G + lanes_of(blk);
-                    tmem_ld_16x256b_x2(ga, v);
-                    uint32_t w[8];
+                for (int GG = 0; GG < 2; ++GG) {              // two 16-token groups per load
+                    float v[16];
+                    const uint32_t ga = s_col + 32 * GG + lanes_of(blk);
+                    tmem_ld_16x256b_x4(ga, v);
+                    uint32_t w[2][8];
 #pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2) {          // repetition n = 2G + h2
-                        const int n = 2 * G + h2;
+                    for (int h4 = 0; h4 < 4; ++h4) {          // repetition n = 4GG + h4
+                        const int n = 4 * GG + h4, G = h4 >> 1, h2 = h4 & 1;
 #pragma unroll
                         for (int rr = 0; rr < 2; ++rr) {      // row g or g + 8
                             const int k = 2 * blk + rr;
-                            float e0 = fmaf(v[4 * h2 + 2 * rr], ks[2 * n], neg_m[k]);
-                            float e1 = fmaf(v[4 * h2 + 2 * rr + 1], ks[2 * n + 1], neg_m[k]);
+                            float e0 = fmaf(v[4 * h4 + 2 * rr], ks[2 * n], neg_m[k]);
+                            float e1 = fmaf(v[4 * h4 + 2 * rr + 1], ks[2 * n + 1], neg_m[k]);
                             if (masked_tile) {
                                 const int c = kv0 + 8 * n;
                                 if (c > rlim[k]) e0 = -INFINITY;
@@ -696,11 +706,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const __half2 hh = __floats2half2_rn(pv0, pv1);
                             const float2 hf = __half22float2(hh);
                             const __half2 ll = __floats2half2_rn(pv0 - hf.x, pv1 - hf.y);
-                            w[2 * h2 + rr] = *reinterpret_cast<const uint32_t*>(&hh);
-                            w[4 + 2 * h2 + rr] = *reinterpret_cast<const uint32_t*>(&ll);
+                            w[G][2 * h2 + rr] = *reinterpret_cast<const uint32_t*>(&hh);
+                            w[G][4 + 2 * h2 + rr] = *reinterpret_cast<const uint32_t*>(&ll);
                         }
                     }
-                    tmem_st_16x128b_x4(ga, w);
+                    tmem_st_16x128b_x4(ga, w[0]);
+                    tmem_st_16x128b_x4(ga + 16, w[1]);
                 }
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
