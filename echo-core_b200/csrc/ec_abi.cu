@@ -63,6 +63,7 @@ struct ec_kv_cache {
     void* ws;
     size_t ws_bytes;
     ec::DecodePlan plan;
+    float* stage;        // device staging of the host-pointer step: q | k | v | out
 };
 
 extern "C" {
@@ -145,6 +146,7 @@ int ec_kv_cache_create(const ec_model_config* config, int scale_mode, ec_kv_cach
     kc->ws = nullptr;
     kc->ws_bytes = 0;
     kc->plan = ec::DecodePlan{32, 1};
+    kc->stage = nullptr;
     cudaGetDevice(&kc->device);
     kc->layers.assign(c.num_layers, ec_kv_layer{});
 
@@ -207,6 +209,7 @@ void ec_kv_cache_destroy(ec_kv_cache* cache) {
     cudaDeviceSynchronize();
     cudaFree(cache->slab);
     cudaFree(cache->ws);
+    cudaFree(cache->stage);
     cudaSetDevice(prev);
     delete cache;
 }
@@ -312,6 +315,55 @@ int ec_kv_cache_attention(ec_kv_cache* cache, uint32_t layer_idx, const float* q
     a.mode = ec::kOut;
     cudaError_t e = ec::launch_decode(a, (int)c.num_kv_heads, cache->plan, cache->ws, as_stream(stream));
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_cache_attention launch");
+}
+
+int ec_kv_cache_step(ec_kv_cache* cache, uint32_t layer_idx, const float* q, const float* k_proj,
+                     const float* v_proj, float* attn_out, float softmax_scale, ec_stream_t stream) {
+    if (!cache) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_step: null cache");
+    if (layer_idx >= cache->cfg.num_layers)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_step: layer %u out of range", layer_idx);
+    // full layer: refuse before attending, so a failed step changes nothing
+    if (cache->layers[layer_idx].seq_len >= cache->cfg.max_seq_len)
+        return fail(EC_ERR_CAPACITY, "kv_cache_step: layer %u is full (%u tokens)", layer_idx,
+                    cache->cfg.max_seq_len);
+    // attention over the cache as it stands, then this token's append: the
+    // order of src/inference.cpp:330-414
+    int rc = ec_kv_cache_attention(cache, layer_idx, q, attn_out, softmax_scale, stream);
+    if (rc != EC_OK) return rc;
+    return ec_kv_cache_append(cache, layer_idx, k_proj, v_proj, stream);
+}
+
+int ec_kv_cache_step_host(ec_kv_cache* cache, uint32_t layer_idx, const float* q,
+                          const float* k_proj, const float* v_proj, float* attn_out,
+                          float softmax_scale) {
+    if (!cache || !q || !k_proj || !v_proj || !attn_out)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_step_host: null argument");
+    const ec_model_config& c = cache->cfg;
+    const size_t nq = (size_t)c.num_heads * c.head_dim;
+    const size_t nkv = (size_t)c.num_kv_heads * c.head_dim;
+    // four 256-byte-aligned slots: q, k, v, out
+    auto r64 = [](size_t n) { return (n + 63) & ~size_t(63); };
+    const size_t oq = 0, ok = r64(nq), ov = ok + r64(nkv), oo = ov + r64(nkv), total = oo + r64(nq);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(cache->device);
+    cudaError_t e = cudaSuccess;
+    if (!cache->stage) e = cudaMalloc(&cache->stage, total * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemcpy(cache->stage + oq, q, nq * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(cache->stage + ok, k_proj, nkv * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(cache->stage + ov, v_proj, nkv * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaSetDevice(prev);
+        return cuda_fail(e, "kv_cache_step_host: staging");
+    }
+    int rc = ec_kv_cache_step(cache, layer_idx, cache->stage + oq, cache->stage + ok,
+                              cache->stage + ov, cache->stage + oo, softmax_scale, nullptr);
+    if (rc == EC_OK) {
+        e = cudaMemcpy(attn_out, cache->stage + oo, nq * 4, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = cuda_fail(e, "kv_cache_step_host: read back");
+    }
+    cudaSetDevice(prev);
+    return rc;
 }
 
 // ------------------------------------------------------------ batched cache

@@ -49,7 +49,7 @@ EXPORTS = (
     "ec_kv_cache_seq_len", "ec_kv_cache_reset", "ec_kv_cache_attention",
     "ec_kv_batch_append", "ec_decode_workspace_size", "ec_decode_attention",
     "ec_decode_attention_partial", "ec_lse_combine", "ec_prefill_attention",
-    "ec_decode_attention_noalloc",
+    "ec_decode_attention_noalloc", "ec_kv_cache_step", "ec_kv_cache_step_host",
 )
 
 

@@ -162,6 +162,23 @@ EC_API int ec_kv_cache_reset(ec_kv_cache* cache);
  * A layer of length 0 gives zeros (src/inference.cpp:331). */
 EC_API int ec_kv_cache_attention(ec_kv_cache* cache, uint32_t layer_idx, const float* q, float* out,
                           float softmax_scale, ec_stream_t stream);
+/* One token of one layer of InferenceEngine::attention minus its weight
+ * matvecs (src/inference.cpp:321-414): attention of q over the layer's cached
+ * tokens (the cache before this token, as :330-392 read it), then the append
+ * of this token's k/v (:414).  q [num_heads*head_dim], k_proj / v_proj
+ * [num_kv_heads*head_dim], attn_out [num_heads*head_dim]: device pointers,
+ * asynchronous on the stream.  EC_ERR_CAPACITY (and nothing done) when the
+ * layer is full. */
+EC_API int ec_kv_cache_step(ec_kv_cache* cache, uint32_t layer_idx, const float* q,
+                            const float* k_proj, const float* v_proj, float* attn_out,
+                            float softmax_scale, ec_stream_t stream);
+/* ec_kv_cache_step for an engine whose buffers live in host memory, as the
+ * reference's q_proj_ / k_proj_ / v_proj_ / attn_out_ do (include/inference.h:
+ * 21-27): copies q/k/v to a device staging area owned by the cache, runs the
+ * step and copies attn_out back.  Synchronous. */
+EC_API int ec_kv_cache_step_host(ec_kv_cache* cache, uint32_t layer_idx, const float* q,
+                                 const float* k_proj, const float* v_proj, float* attn_out,
+                                 float softmax_scale);
 
 /* ------------------------------------------------------------------------
  * Batched ragged cache: per-sequence contiguous slabs inside caller-owned

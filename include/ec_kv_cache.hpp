@@ -10,7 +10,9 @@
 //   - layer(i) returns the KVCacheLayer view with device pointers;
 //   - append(i, k, v) takes device pointers to the token's fp32 K/V
 //     projections and quantizes them on the GPU;
-//   - attention(i, q, out) is the KV half of InferenceEngine::attention.
+//   - attention(i, q, out) is the KV half of InferenceEngine::attention;
+//   - step / step_host(i, q, k, v, attn_out) are InferenceEngine::attention
+//     without its weight matvecs: attention, then the token's append.
 // Errors throw std::runtime_error carrying ec_last_error(); the reference
 // used assert (compiled out) and std::runtime_error (src/inference.cpp:22).
 #pragma once
@@ -58,6 +60,21 @@ public:
     void attention(uint32_t layer_idx, const float* q, float* out, float softmax_scale,
                    ec_stream_t stream = nullptr) {
         check(ec_kv_cache_attention(h_, layer_idx, q, out, softmax_scale, stream));
+    }
+    // One token of InferenceEngine::attention without its weight matvecs
+    // (src/inference.cpp:321-414): attend over the layer's cached tokens, then
+    // append this token's k/v.  Device pointers, asynchronous.
+    void step(uint32_t layer_idx, const float* q_proj, const float* k_proj, const float* v_proj,
+              float* attn_out, float softmax_scale, ec_stream_t stream = nullptr) {
+        check(ec_kv_cache_step(h_, layer_idx, q_proj, k_proj, v_proj, attn_out, softmax_scale,
+                               stream));
+    }
+    // The same for host buffers (the reference engine's q_proj_, k_proj_,
+    // v_proj_, attn_out_); synchronous.
+    void step_host(uint32_t layer_idx, const float* q_proj, const float* k_proj,
+                   const float* v_proj, float* attn_out, float softmax_scale) {
+        check(ec_kv_cache_step_host(h_, layer_idx, q_proj, k_proj, v_proj, attn_out,
+                                    softmax_scale));
     }
     ec_kv_cache* handle() const { return h_; }
 
