@@ -248,6 +248,8 @@ def run_gpu_arm(args, rank, world, local_rank):
     if args.ctx:
         cfg.ctx = [args.ctx] * len(cfg.ctx)
         cfg.name += f"_ctx{args.ctx}"
+    if args.kv_fp32:
+        return run_f32_arm(args, rank, world, local_rank, cfg)
     if cfgn == 4:
         return run_cp_arm(args, rank, world, local_rank)
     if cfgn == 5:
@@ -412,6 +414,61 @@ def run_gpu_arm(args, rank, world, local_rank):
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_line()
     print(json.dumps(line), flush=True)
+
+
+def run_f32_arm(args, rank, world, local_rank, cfg):
+    """Decode over the fp32 cache mode (use_kv_quantization = false): one
+    sequence of 65,536 tokens (or --ctx) per rank through the cache object,
+    16 Q / 4 KV heads; bytes = the K and V rows, 4096 per token (268 MB per
+    rank, above L2)."""
+    import torch
+    import torch.distributed as dist
+    import eckv
+    dev = torch.device("cuda", local_rank)
+    L = args.ctx or 65536
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(cfg.seed * 1000 + rank)
+    c = eckv.KVCache(num_heads=H, num_kv_heads=HKV, head_dim=D, num_layers=1, max_seq_len=L,
+                     use_kv_quantization=False)
+    row = HKV * D
+    # the cache's own append (a plain fp32 copy per token, src/kv_cache.cpp:106-110)
+    kbuf = torch.randn((L, row), generator=gen, device=dev)
+    vbuf = torch.randn((L, row), generator=gen, device=dev)
+    for t in range(L):
+        c.append(0, kbuf[t], vbuf[t])
+    del kbuf, vbuf
+    q = torch.randn((H, D), generator=gen, device=dev)
+    out = torch.empty((H, D), device=dev)
+    scale = W.softmax_scale(D)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        c.attention(0, q, out, scale, stream)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        c.attention(0, q, out, scale, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        peak, kind = peaks()
+        nbytes = L * row * 4 * 2 * world
+        gbs = nbytes * args.steps / (float(t[0]) * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": "decode attention over the fp32 KV cache (use_kv_quantization=false) GB/s",
+            "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(float(t[0]) / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic N(0,1) K/V/Q",
+            "config": {"workload": f"fp32_cache_decode_ctx{L}", "ctx": L, "q_heads": H,
+                       "kv_heads": HKV, "head_dim": D},
+            "pct_of_hbm_peak": round(100 * gbs / (peak * world), 1), "peak_kind": kind}), flush=True)
+    c.close()
 
 
 def run_prefill_arm(args, rank, world, local_rank):
@@ -585,6 +642,8 @@ def main():
                     help="override the sequence count (small profiling cases)")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
     ap.add_argument("--ctx", type=int, default=None, help="override every sequence's context")
+    ap.add_argument("--kv-fp32", action="store_true",
+                    help="decode over the fp32 cache mode (one sequence per rank)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -47,6 +47,14 @@ bool decode_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t 
     return g == 1 || g == 2 || g == 4;
 }
 
+// The fp32-cache kernel: any num_kv_heads, query groups of 1, 2, 4 or 8.
+bool f32_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim) {
+    if (head_dim != 128 || num_kv_heads == 0 || num_heads == 0 || num_heads % num_kv_heads)
+        return false;
+    const uint32_t g = num_heads / num_kv_heads;
+    return g == 1 || g == 2 || g == 4 || g == 8;
+}
+
 cudaStream_t as_stream(ec_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
 }  // namespace
@@ -184,6 +192,18 @@ int ec_kv_cache_create(const ec_model_config* config, int scale_mode, ec_kv_cach
             }
         }
     }
+    if (!c.use_kv_quantization && c.num_layers > 0 &&
+        f32_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim)) {
+        kc->ws_bytes = ec::f32_decode_workspace_bytes((int)c.max_seq_len, (int)c.num_heads);
+        if (kc->ws_bytes) {
+            cudaError_t e = cudaMalloc(&kc->ws, kc->ws_bytes);
+            if (e != cudaSuccess) {
+                cudaFree(kc->slab);
+                delete kc;
+                return cuda_fail(e, "kv_cache_create: decode workspace");
+            }
+        }
+    }
     if (c.use_kv_quantization && c.num_layers > 0 &&
         decode_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim)) {
         kc->plan = ec::plan_decode(1, (int)c.max_seq_len, num_sms_current());
@@ -290,8 +310,17 @@ int ec_kv_cache_attention(ec_kv_cache* cache, uint32_t layer_idx, const float* q
     if (!cache || !q || !out) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_attention: null argument");
     const ec_model_config& c = cache->cfg;
     if (layer_idx >= c.num_layers) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_attention: layer out of range");
-    if (!c.use_kv_quantization)
-        return fail(EC_ERR_UNSUPPORTED, "kv_cache_attention: the fp32 cache mode has no GPU attention kernel yet");
+    if (!c.use_kv_quantization) {
+        // FP32 mode (src/inference.cpp:346-358, 386-393)
+        if (!f32_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim))
+            return fail(EC_ERR_UNSUPPORTED, "kv_cache_attention (fp32 cache): needs head_dim 128 and num_heads / num_kv_heads in {1, 2, 4, 8}");
+        if (!aligned16(q) || !aligned16(out)) return fail(EC_ERR_MISALIGNED, "kv_cache_attention: q/out not 16-byte aligned");
+        const ec_kv_layer& L = cache->layers[layer_idx];
+        cudaError_t e = ec::launch_decode_f32(L.keys_fp32, L.values_fp32, (int)c.num_kv_heads,
+                                              (int)c.num_heads, (int)L.seq_len, q, softmax_scale,
+                                              out, cache->ws, as_stream(stream));
+        return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_cache_attention (fp32 cache) launch");
+    }
     if (!decode_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim))
         return fail(EC_ERR_UNSUPPORTED, "kv_cache_attention: needs head_dim 128, num_kv_heads 4|8, group 1|2|4");
     if (!aligned16(q) || !aligned16(out)) return fail(EC_ERR_MISALIGNED, "kv_cache_attention: q/out not 16-byte aligned");

@@ -94,4 +94,15 @@ int set_last_error(int status, const char* msg);
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
                                int num_seqs, int num_heads, float* out, cudaStream_t st);
 
+// Decode attention over the fp32 cache mode (use_kv_quantization = false):
+// keys / values [len][num_kv_heads][128] fp32, q [num_heads][128] unscaled,
+// out [num_heads][128].  Split-K over chunks of kF32ChunkTokens tokens; the
+// workspace holds (m, l, O) per (chunk, head).
+constexpr int kF32ChunkTokens = 128;
+int f32_decode_chunks(int len);
+size_t f32_decode_workspace_bytes(int max_len, int num_heads);
+cudaError_t launch_decode_f32(const float* keys, const float* values, int num_kv_heads,
+                              int num_heads, int len, const float* q, float q_mul, float* out,
+                              void* ws, cudaStream_t st);
+
 }  // namespace ec

@@ -208,6 +208,49 @@ void oracle_decode_attention(const int8_t* keys, const int8_t* values,
 }
 
 /*
+ * FP32 cache mode of the same loop (use_kv_quantization = false): scores over
+ * keys_fp32 (src/inference.cpp:346-358), the softmax of :361-375 and P.V over
+ * values_fp32 (:386-393); layout [pos][num_kv_heads][head_dim] fp32
+ * (src/kv_cache.cpp:59-70).  Same operation order as the int8 restatement.
+ */
+void oracle_decode_attention_f32(const float* keys, const float* values, uint32_t kv_len,
+                                 const float* q, float* out, uint32_t num_heads,
+                                 uint32_t num_kv_heads, uint32_t head_dim, float softmax_scale,
+                                 float* scores) {
+    const uint32_t kv_dim = num_kv_heads * head_dim;
+    float* qs = (float*)malloc(sizeof(float) * (size_t)num_heads * head_dim);
+    for (uint32_t i = 0; i < num_heads * head_dim; ++i) qs[i] = q[i] * softmax_scale;
+    memset(out, 0, sizeof(float) * (size_t)num_heads * head_dim);
+    if (kv_len == 0) { free(qs); return; }
+    for (uint32_t h = 0; h < num_heads; ++h) {
+        const uint32_t kv_head = h % num_kv_heads;
+        const float* head_q = qs + (size_t)h * head_dim;
+        for (uint32_t pos = 0; pos < kv_len; ++pos) {
+            float score = 0.0f;
+            const float* key_head = keys + (size_t)pos * kv_dim + (size_t)kv_head * head_dim;
+            for (uint32_t d = 0; d < head_dim; ++d) score += head_q[d] * key_head[d];
+            scores[pos] = score;
+        }
+        float max_score = scores[0];
+        for (uint32_t i = 1; i < kv_len; ++i)
+            if (scores[i] > max_score) max_score = scores[i];
+        float sum = 0.0f;
+        for (uint32_t i = 0; i < kv_len; ++i) {
+            scores[i] = expf(scores[i] - max_score);
+            sum += scores[i];
+        }
+        const float inv_sum = 1.0f / sum;
+        for (uint32_t i = 0; i < kv_len; ++i) scores[i] *= inv_sum;
+        float* head_out = out + (size_t)h * head_dim;
+        for (uint32_t pos = 0; pos < kv_len; ++pos) {
+            const float* val_head = values + (size_t)pos * kv_dim + (size_t)kv_head * head_dim;
+            for (uint32_t d = 0; d < head_dim; ++d) head_out[d] += scores[pos] * val_head[d];
+        }
+    }
+    free(qs);
+}
+
+/*
  * Chunked-prefill attention.  The reference has no chunked prefill: it feeds
  * a prompt one token at a time (src/main.cpp:404-405), each token running the
  * decode loop above over the cache as it stands after that token's append

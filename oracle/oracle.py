@@ -52,6 +52,8 @@ def lib():
                                              _u32, ctypes.c_int]
         L.oracle_decode_attention.argtypes = [_i8p, _i8p, _f32p, _f32p, _u32, _f32p, _f32p, _u32,
                                               _u32, _u32, ctypes.c_float, ctypes.c_int, _f32p]
+        L.oracle_decode_attention_f32.argtypes = [_f32p, _f32p, _u32, _f32p, _f32p, _u32, _u32,
+                                                  _u32, ctypes.c_float, _f32p]
         L.oracle_prefill_attention.argtypes = [_i8p, _i8p, _f32p, _f32p, _u32, _u32, _f32p, _f32p,
                                                _u32, _u32, _u32, ctypes.c_float, ctypes.c_int, _f32p]
         _lib = L
@@ -91,6 +93,10 @@ def ref():
         L.ref_attn_load.restype = ctypes.c_int
         L.ref_attn_step.argtypes = [vp, _u32, _f32p, _f32p]
         L.ref_attn_step.restype = ctypes.c_int
+        L.ref_attn_f32_create.argtypes = [_u32, _u32, _u32, _u32]
+        L.ref_attn_f32_create.restype = vp
+        L.ref_attn_f32_run.argtypes = [vp, _u32, _f32p, _f32p, _f32p, _f32p]
+        L.ref_attn_f32_run.restype = ctypes.c_int
         _ref = L
     return _ref
 
@@ -142,6 +148,21 @@ def decode_attention(keys, values, kscales, vscales, kv_len, q, num_heads, num_k
                                   _p(vscales, _f32p), kv_len, _p(q, _f32p), _p(out, _f32p),
                                   num_heads, num_kv_heads, head_dim, ctypes.c_float(softmax_scale),
                                   mode, _p(scratch, _f32p))
+    return out.reshape(num_heads, head_dim)
+
+
+def decode_attention_f32(keys, values, kv_len, q, num_heads, num_kv_heads, head_dim,
+                         softmax_scale):
+    """FP32 cache mode (use_kv_quantization = false) of the decode loop:
+    keys / values [kv_len, num_kv_heads*head_dim] fp32."""
+    keys = np.ascontiguousarray(keys, np.float32)
+    values = np.ascontiguousarray(values, np.float32)
+    q = np.ascontiguousarray(q, np.float32).reshape(-1)
+    out = np.zeros(num_heads * head_dim, np.float32)
+    scratch = np.zeros(max(kv_len, 1), np.float32)
+    lib().oracle_decode_attention_f32(_p(keys, _f32p), _p(values, _f32p), kv_len, _p(q, _f32p),
+                                      _p(out, _f32p), num_heads, num_kv_heads, head_dim,
+                                      ctypes.c_float(softmax_scale), _p(scratch, _f32p))
     return out.reshape(num_heads, head_dim)
 
 
@@ -274,6 +295,32 @@ class RefKVCache:
         k = np.ctypeslib.as_array(ctypes.cast(ptrs[4], _f32p), (n * row,)).copy()
         v = np.ctypeslib.as_array(ctypes.cast(ptrs[5], _f32p), (n * row,)).copy()
         return k.reshape(n, row), v.reshape(n, row)
+
+
+class RefAttentionF32:
+    """The reference's attention loop in its FP32 cache mode
+    (src/inference.cpp:346-358, 386-393)."""
+
+    def __init__(self, num_heads, num_kv_heads, head_dim, max_seq_len):
+        self.h = ref().ref_attn_f32_create(num_heads, num_kv_heads, head_dim, max_seq_len)
+        self.H, self.d = num_heads, head_dim
+
+    def close(self):
+        if self.h:
+            ref().ref_attn_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def run(self, keys, values, kv_len, q):
+        keys = np.ascontiguousarray(keys, np.float32)
+        values = np.ascontiguousarray(values, np.float32)
+        q = np.ascontiguousarray(q, np.float32).reshape(-1)
+        out = np.zeros(self.H * self.d, np.float32)
+        if ref().ref_attn_f32_run(self.h, kv_len, _p(keys, _f32p), _p(values, _f32p),
+                                  _p(q, _f32p), _p(out, _f32p)) != 0:
+            raise ValueError("kv_len must be below the engine's max_seq_len")
+        return out.reshape(self.H, self.d)
 
 
 class RefAttention:

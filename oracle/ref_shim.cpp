@@ -220,4 +220,42 @@ int ref_attn_step(void* h, uint32_t kv_len, const float* q, float* out) {
     return 0;
 }
 
+// ---- the FP32 cache mode of InferenceEngine::attention ----
+// (use_kv_quantization = false: src/inference.cpp:346-358, 386-393)
+void* ref_attn_f32_create(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                          uint32_t max_seq_len) {
+    ModelConfig c = make_config(num_heads, num_kv_heads, head_dim, 1, max_seq_len, false);
+    auto* r = new RefAttn{std::make_unique<InferenceEngine>(c), num_heads, num_kv_heads, head_dim,
+                          max_seq_len};
+    WeightLayout L = WeightLayout::compute(c);
+    std::vector<uint16_t> w(L.total_size / sizeof(uint16_t), 0);
+    const size_t hidden = c.hidden_dim;
+    const size_t lb = L.token_embedding_size;
+    const uint16_t one = 0x3C00;
+    for (size_t i = 0; i < hidden; ++i) {
+        w[(lb + L.q_proj_offset) / 2 + i * hidden + i] = one;
+        w[(lb + L.o_proj_offset) / 2 + i * hidden + i] = one;
+    }
+    r->eng->load_weights(w.data());
+    return r;
+}
+
+// One decode step of layer 0 over kv_len fp32 cached tokens
+// ([pos][num_kv_heads][head_dim]); q unscaled.  -1 if no room for the append.
+int ref_attn_f32_run(void* h, uint32_t kv_len, const float* keys, const float* values,
+                     const float* q, float* out) {
+    RefAttn* r = static_cast<RefAttn*>(h);
+    if (kv_len >= r->max_seq_len) return -1;
+    KVCache& cache = *(r->eng.get()->*get(CacheTag()));
+    cache.reset();
+    KVCacheLayer& l = cache.layer(0);
+    const size_t row = static_cast<size_t>(r->num_kv_heads) * r->head_dim;
+    std::memcpy(l.keys_fp32, keys, kv_len * row * sizeof(float));
+    std::memcpy(l.values_fp32, values, kv_len * row * sizeof(float));
+    l.seq_len = kv_len;
+    clear_projections(r);
+    (r->eng.get()->*get(AttentionTag()))(0, q, out);
+    return 0;
+}
+
 }  // extern "C"

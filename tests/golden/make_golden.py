@@ -82,12 +82,30 @@ def attention_golden():
     np.savez_compressed(os.path.join(HERE, "attention.npz"), **out)
 
 
+def attention_f32_golden():
+    """The same loop in its FP32 cache mode (use_kv_quantization = false,
+    src/inference.cpp:346-358, 386-393), run by the reference."""
+    out = {}
+    for tag, H, hkv, L, seed in (("a", 16, 4, 1, 0), ("b", 16, 4, 23, 1), ("c", 8, 2, 9, 2)):
+        rng = np.random.default_rng(300 + seed)
+        k = W.kv_rows(rng, L, hkv, 128)
+        v = W.kv_rows(rng, L, hkv, 128)
+        q = W.queries(rng, 1, H, 128)[0]
+        r = O.RefAttentionF32(H, hkv, 128, L + 1)
+        o = r.run(k, v, L, q)
+        r.close()
+        out.update({f"{tag}_keys": k, f"{tag}_values": v, f"{tag}_q": q, f"{tag}_out": o,
+                    f"{tag}_shape": np.array([H, hkv, L])})
+    np.savez_compressed(os.path.join(HERE, "attention_f32.npz"), **out)
+
+
 if __name__ == "__main__":
     if not O.ref_available():
         sys.exit("oracle/_ref/libecref.so is not built")
     quant_golden()
     kvcache_golden()
     attention_golden()
+    attention_f32_golden()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

@@ -175,3 +175,28 @@ def test_decode_attention_matches_reference_build(L, H):
     r.close()
     got = O.decode_attention(kq, vq, ks, vs, L, q, H, hkv, d, W.softmax_scale(d))
     assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c"])
+def test_decode_attention_f32_matches_golden(golden, tag):
+    """FP32 cache mode (src/inference.cpp:346-358, 386-393): the restatement
+    reproduces the reference's bytes."""
+    g = golden("attention_f32.npz")
+    H, hkv, L = (int(x) for x in g[f"{tag}_shape"])
+    out = O.decode_attention_f32(g[f"{tag}_keys"], g[f"{tag}_values"], L, g[f"{tag}_q"], H, hkv,
+                                 128, W.softmax_scale(128))
+    assert np.array_equal(bits(out), bits(g[f"{tag}_out"]))
+
+
+@needs_ref
+@pytest.mark.parametrize("L,H,hkv", [(1, 16, 4), (77, 16, 4), (300, 8, 8), (40, 32, 4)])
+def test_decode_attention_f32_matches_reference_build(L, H, hkv):
+    rng = np.random.default_rng(L + H + hkv)
+    k = W.kv_rows(rng, L, hkv, 128)
+    v = W.kv_rows(rng, L, hkv, 128)
+    q = W.queries(rng, 1, H, 128)[0]
+    r = O.RefAttentionF32(H, hkv, 128, L + 1)
+    want = r.run(k, v, L, q)
+    r.close()
+    got = O.decode_attention_f32(k, v, L, q, H, hkv, 128, W.softmax_scale(128))
+    assert np.array_equal(bits(got), bits(want))
