@@ -395,6 +395,137 @@ int ec_kv_cache_step_host(ec_kv_cache* cache, uint32_t layer_idx, const float* q
     return rc;
 }
 
+// ------------------------------------------------------------ snapshots
+// Host image of a cache object's contents: a header (magic, version, shape,
+// scale mode, per-layer lengths) followed, per layer, by the used prefix of
+// each buffer: int8 K and V codes plus K and V scales ([len][num_kv_heads],
+// or [len] for ROW scales), or the fp32 K and V rows.  Little-endian, packed.
+namespace {
+constexpr char kSnapMagic[8] = {'E', 'C', 'K', 'V', 'S', 'N', 'A', 'P'};
+constexpr uint32_t kSnapVersion = 1;
+struct SnapHeader {
+    char magic[8];
+    uint32_t version, num_heads, num_kv_heads, head_dim, num_layers, max_seq_len;
+    uint32_t use_kv_quantization, scale_mode;
+};
+struct LayerBytes { size_t codes, scales, fp32; };
+LayerBytes layer_bytes(const ec_kv_cache* c, uint32_t len) {
+    const size_t row = (size_t)c->cfg.num_kv_heads * c->cfg.head_dim;
+    const size_t ns = c->scale_mode == EC_SCALE_ROW ? 1 : c->cfg.num_kv_heads;
+    if (c->cfg.use_kv_quantization) return {len * row, len * ns * sizeof(float), 0};
+    return {0, 0, len * row * sizeof(float)};
+}
+size_t snapshot_bytes(const ec_kv_cache* c) {
+    size_t b = sizeof(SnapHeader) + (size_t)c->cfg.num_layers * sizeof(uint32_t);
+    for (const auto& L : c->layers) {
+        const LayerBytes lb = layer_bytes(c, L.seq_len);
+        b += 2 * (lb.codes + lb.scales + lb.fp32);
+    }
+    return b;
+}
+}  // namespace
+
+size_t ec_kv_cache_snapshot_size(const ec_kv_cache* cache) {
+    return cache ? snapshot_bytes(cache) : 0;
+}
+
+int ec_kv_cache_snapshot(const ec_kv_cache* cache, void* host, size_t bytes) {
+    if (!cache || !host) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_snapshot: null argument");
+    const size_t need = snapshot_bytes(cache);
+    if (bytes < need)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_snapshot: buffer of %zu bytes, need %zu", bytes, need);
+    uint8_t* p = static_cast<uint8_t*>(host);
+    SnapHeader h;
+    std::memcpy(h.magic, kSnapMagic, 8);
+    h.version = kSnapVersion;
+    h.num_heads = cache->cfg.num_heads;
+    h.num_kv_heads = cache->cfg.num_kv_heads;
+    h.head_dim = cache->cfg.head_dim;
+    h.num_layers = cache->cfg.num_layers;
+    h.max_seq_len = cache->cfg.max_seq_len;
+    h.use_kv_quantization = cache->cfg.use_kv_quantization ? 1u : 0u;
+    h.scale_mode = (uint32_t)cache->scale_mode;
+    std::memcpy(p, &h, sizeof h);
+    p += sizeof h;
+    for (const auto& L : cache->layers) {
+        std::memcpy(p, &L.seq_len, sizeof(uint32_t));
+        p += sizeof(uint32_t);
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(cache->device);
+    cudaError_t e = cudaDeviceSynchronize();   // appends in flight land first
+    for (size_t l = 0; e == cudaSuccess && l < cache->layers.size(); ++l) {
+        const ec_kv_layer& L = cache->layers[l];
+        const LayerBytes lb = layer_bytes(cache, L.seq_len);
+        const void* src[4] = {L.keys_int8, L.values_int8, L.key_scales, L.val_scales};
+        const size_t len[4] = {lb.codes, lb.codes, lb.scales, lb.scales};
+        const void* srcf[2] = {L.keys_fp32, L.values_fp32};
+        for (int i = 0; e == cudaSuccess && i < 4 && cache->cfg.use_kv_quantization; ++i) {
+            if (len[i]) e = cudaMemcpy(p, src[i], len[i], cudaMemcpyDeviceToHost);
+            p += len[i];
+        }
+        for (int i = 0; e == cudaSuccess && i < 2 && !cache->cfg.use_kv_quantization; ++i) {
+            if (lb.fp32) e = cudaMemcpy(p, srcf[i], lb.fp32, cudaMemcpyDeviceToHost);
+            p += lb.fp32;
+        }
+    }
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_cache_snapshot");
+}
+
+int ec_kv_cache_restore(ec_kv_cache* cache, const void* host, size_t bytes) {
+    if (!cache || !host) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_restore: null argument");
+    const uint8_t* p = static_cast<const uint8_t*>(host);
+    SnapHeader h;
+    if (bytes < sizeof h) return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_restore: truncated header");
+    std::memcpy(&h, p, sizeof h);
+    p += sizeof h;
+    if (std::memcmp(h.magic, kSnapMagic, 8) != 0 || h.version != kSnapVersion)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_restore: not a version-%u cache snapshot", kSnapVersion);
+    const ec_model_config& c = cache->cfg;
+    if (h.num_heads != c.num_heads || h.num_kv_heads != c.num_kv_heads || h.head_dim != c.head_dim ||
+        h.num_layers != c.num_layers || h.use_kv_quantization != (c.use_kv_quantization ? 1u : 0u) ||
+        h.scale_mode != (uint32_t)cache->scale_mode)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_restore: snapshot shape or mode differs from the cache's");
+    if (bytes < sizeof h + (size_t)h.num_layers * sizeof(uint32_t))
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_restore: truncated length table");
+    std::vector<uint32_t> lens(h.num_layers);
+    std::memcpy(lens.data(), p, lens.size() * sizeof(uint32_t));
+    p += lens.size() * sizeof(uint32_t);
+    size_t need = sizeof h + lens.size() * sizeof(uint32_t);
+    for (uint32_t n : lens) {
+        if (n > c.max_seq_len)
+            return fail(EC_ERR_CAPACITY, "kv_cache_restore: a layer holds %u tokens, the cache %u", n, c.max_seq_len);
+        const LayerBytes lb = layer_bytes(cache, n);
+        need += 2 * (lb.codes + lb.scales + lb.fp32);
+    }
+    if (bytes < need)
+        return fail(EC_ERR_INVALID_ARGUMENT, "kv_cache_restore: %zu bytes, the header describes %zu", bytes, need);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(cache->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    for (size_t l = 0; e == cudaSuccess && l < cache->layers.size(); ++l) {
+        ec_kv_layer& L = cache->layers[l];
+        const LayerBytes lb = layer_bytes(cache, lens[l]);
+        void* dst[4] = {L.keys_int8, L.values_int8, L.key_scales, L.val_scales};
+        const size_t len[4] = {lb.codes, lb.codes, lb.scales, lb.scales};
+        void* dstf[2] = {L.keys_fp32, L.values_fp32};
+        for (int i = 0; e == cudaSuccess && i < 4 && c.use_kv_quantization; ++i) {
+            if (len[i]) e = cudaMemcpy(dst[i], p, len[i], cudaMemcpyHostToDevice);
+            p += len[i];
+        }
+        for (int i = 0; e == cudaSuccess && i < 2 && !c.use_kv_quantization; ++i) {
+            if (lb.fp32) e = cudaMemcpy(dstf[i], p, lb.fp32, cudaMemcpyHostToDevice);
+            p += lb.fp32;
+        }
+        if (e == cudaSuccess) L.seq_len = lens[l];
+    }
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_cache_restore");
+}
+
 // ------------------------------------------------------------ batched cache
 static int check_batch(const ec_kv_batch* b, const char* who) {
     if (!b) return fail(EC_ERR_INVALID_ARGUMENT, "%s: batch is NULL", who);

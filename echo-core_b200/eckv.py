@@ -50,6 +50,7 @@ EXPORTS = (
     "ec_kv_batch_append", "ec_decode_workspace_size", "ec_decode_attention",
     "ec_decode_attention_partial", "ec_lse_combine", "ec_prefill_attention",
     "ec_decode_attention_noalloc", "ec_kv_cache_step", "ec_kv_cache_step_host",
+    "ec_kv_cache_snapshot_size", "ec_kv_cache_snapshot", "ec_kv_cache_restore",
 )
 
 
@@ -218,6 +219,20 @@ class KVCache:
     def attention(self, idx: int, q, out, softmax_scale: float, stream=None) -> None:
         check(lib().ec_kv_cache_attention(self._h, idx, _ptr(q), _ptr(out),
                                           ctypes.c_float(softmax_scale), _stream(stream)))
+
+    def snapshot(self) -> bytes:
+        """Host image of the cache's contents (ec_kv_cache_snapshot)."""
+        L = lib()
+        L.ec_kv_cache_snapshot_size.restype = ctypes.c_size_t
+        n = L.ec_kv_cache_snapshot_size(self._h)
+        buf = ctypes.create_string_buffer(n)
+        check(L.ec_kv_cache_snapshot(self._h, buf, ctypes.c_size_t(n)))
+        return buf.raw
+
+    def restore(self, image: bytes) -> None:
+        """Replaces the cache's contents with a snapshot (ec_kv_cache_restore)."""
+        buf = ctypes.create_string_buffer(bytes(image), len(image))
+        check(lib().ec_kv_cache_restore(self._h, buf, ctypes.c_size_t(len(image))))
 
 
 # ---------------------------------------------------------------- BatchCache

@@ -180,6 +180,19 @@ EC_API int ec_kv_cache_step_host(ec_kv_cache* cache, uint32_t layer_idx, const f
                                  const float* k_proj, const float* v_proj, float* attn_out,
                                  float softmax_scale);
 
+/* Cache snapshots (persistence; the reference keeps its cache only in
+ * process memory).  ec_kv_cache_snapshot writes the cache's contents into a
+ * host buffer of ec_kv_cache_snapshot_size() bytes: a header (magic
+ * "ECKVSNAP", version, shape, scale mode, per-layer lengths) and, per layer,
+ * the used prefix of each buffer.  ec_kv_cache_restore loads such an image
+ * into a cache of the same shape and mode, replacing its contents and
+ * lengths; a mismatched or truncated image gives EC_ERR_INVALID_ARGUMENT (or
+ * EC_ERR_CAPACITY for a layer longer than max_seq_len) and changes nothing.
+ * Both synchronise the device. */
+EC_API size_t ec_kv_cache_snapshot_size(const ec_kv_cache* cache);
+EC_API int ec_kv_cache_snapshot(const ec_kv_cache* cache, void* host, size_t bytes);
+EC_API int ec_kv_cache_restore(ec_kv_cache* cache, const void* host, size_t bytes);
+
 /* ------------------------------------------------------------------------
  * Batched ragged cache: per-sequence contiguous slabs inside caller-owned
  * device buffers, addressed through an int32 offset / capacity / length
