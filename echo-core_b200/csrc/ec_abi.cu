@@ -4,6 +4,7 @@
 // KVCacheLayer, ModelConfig) onto device memory, picks the split plan and
 // launches the kernels.  No exception crosses the ABI; every failure returns
 // an ec_status and records a one-line reason for ec_last_error().
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -573,6 +574,68 @@ int ec_kv_batch_append(const ec_kv_batch* b, const float* k, const float* v,
     cudaError_t e = ec::launch_append(a, (int)b->num_kv_heads, b->scale_mode == EC_SCALE_ROW,
                                       as_stream(stream));
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_batch_append launch");
+}
+
+// 1 / base^(i/d), i = 0, 2, .., 126 (echo-core-zig src/inference/engine.zig:
+// 477-478: freq = 1.0 / pow(f32, base, i / head_dim), all in fp32)
+static void rope_inv_freq(float base, float* out64) {
+    for (int i = 0; i < 128; i += 2)
+        out64[i / 2] = 1.0f / std::pow(base, static_cast<float>(i) / 128.0f);
+}
+
+int ec_kv_batch_append_rope(const ec_kv_batch* b, const float* k, const float* v,
+                            uint32_t tokens_per_seq, const ec_rope_desc* k_desc,
+                            ec_stream_t stream) {
+    int rc = check_batch(b, "kv_batch_append_rope");
+    if (rc) return rc;
+    if (!k_desc) return fail(EC_ERR_INVALID_ARGUMENT, "kv_batch_append_rope: rope descriptor NULL");
+    if (tokens_per_seq == 0 || b->num_seqs == 0) return EC_OK;
+    if (!k || !v) return fail(EC_ERR_INVALID_ARGUMENT, "kv_batch_append_rope: k/v NULL");
+    if (b->head_dim != 128 || !(b->num_kv_heads == 1 || b->num_kv_heads == 2 || b->num_kv_heads == 4 ||
+                                b->num_kv_heads == 8))
+        return fail(EC_ERR_UNSUPPORTED, "kv_batch_append_rope: needs head_dim 128 and num_kv_heads 1|2|4|8");
+    if (!aligned16(k) || !aligned16(v)) return fail(EC_ERR_MISALIGNED, "kv_batch_append_rope: k/v not 16-byte aligned");
+    if (k_desc->norm_weight && (reinterpret_cast<uintptr_t>(k_desc->norm_weight) & 7))
+        return fail(EC_ERR_MISALIGNED, "kv_batch_append_rope: norm weight not 8-byte aligned");
+    if ((uint64_t)b->num_seqs * tokens_per_seq > 0x7fffffffull)
+        return fail(EC_ERR_UNSUPPORTED, "kv_batch_append_rope: too many tokens in one call");
+    ec::AppendArgs a{};
+    a.k = k;
+    a.v = v;
+    a.keys = b->keys;
+    a.values = b->values;
+    a.key_scales = b->key_scales;
+    a.val_scales = b->val_scales;
+    a.seq_offset = b->seq_offset;
+    a.seq_capacity = b->seq_capacity;
+    a.seq_len = b->seq_len;
+    a.err = b->error_word;
+    a.total_slots = b->total_slots;
+    a.num_seqs = (int)b->num_seqs;
+    a.n_new = (int)tokens_per_seq;
+    a.k_norm_w = k_desc->norm_weight;
+    a.rope = k_desc->rope_base > 0.0f;
+    if (a.rope) rope_inv_freq(k_desc->rope_base, a.inv_freq);
+    cudaError_t e = ec::launch_append_rope(a, (int)b->num_kv_heads, b->scale_mode == EC_SCALE_ROW,
+                                           as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_batch_append_rope launch");
+}
+
+int ec_rope_rows(float* x, uint32_t rows, uint32_t num_heads, uint32_t head_dim,
+                 const int32_t* positions, const ec_rope_desc* desc, ec_stream_t stream) {
+    if (!x || !desc) return fail(EC_ERR_INVALID_ARGUMENT, "rope_rows: null argument");
+    if (rows == 0 || num_heads == 0) return EC_OK;
+    if (head_dim != 128) return fail(EC_ERR_UNSUPPORTED, "rope_rows: needs head_dim 128");
+    const bool rope = desc->rope_base > 0.0f;
+    if (rope && !positions) return fail(EC_ERR_INVALID_ARGUMENT, "rope_rows: positions NULL");
+    if (!aligned16(x)) return fail(EC_ERR_MISALIGNED, "rope_rows: x not 16-byte aligned");
+    if (desc->norm_weight && (reinterpret_cast<uintptr_t>(desc->norm_weight) & 7))
+        return fail(EC_ERR_MISALIGNED, "rope_rows: norm weight not 8-byte aligned");
+    float inv_freq[64] = {};
+    if (rope) rope_inv_freq(desc->rope_base, inv_freq);
+    cudaError_t e = ec::launch_rope_rows(x, rows, num_heads, positions, desc->norm_weight, rope ? 1 : 0,
+                                         inv_freq, as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "rope_rows launch");
 }
 
 size_t ec_decode_workspace_size(uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim,

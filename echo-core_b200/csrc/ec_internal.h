@@ -23,6 +23,12 @@ struct AppendArgs {
     uint64_t total_slots;
     int num_seqs;
     int n_new;
+    // K pre-processing of echo-core-zig (src/inference/engine.zig): per-head
+    // RMS norm with an fp16 weight (:521-532), then RoPE (:466-518).  Used by
+    // the rope variant of the append kernel only.
+    const uint16_t* k_norm_w;     // fp16 [128] or null: no norm
+    int rope;                     // 0: no rotation
+    float inv_freq[64];           // 1 / base^(2i/128), computed on the host
 };
 
 struct DecodeArgs {
@@ -55,6 +61,12 @@ enum { kOut = 0, kPartial = 1 };
 cudaError_t launch_quantize_rows(const float* in, int8_t* out, float* scales, uint32_t rows,
                                  uint32_t n, cudaStream_t st);
 cudaError_t launch_append(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st);
+cudaError_t launch_append_rope(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st);
+// In-place per-head RMS norm (fp16 weight, may be null) and RoPE of rows of
+// num_heads * 128 floats, row r at position positions[r].
+cudaError_t launch_rope_rows(float* x, uint32_t rows, uint32_t num_heads, const int32_t* positions,
+                             const uint16_t* norm_w, int rope, const float* inv_freq64,
+                             cudaStream_t st);
 cudaError_t launch_fused_dequant_dot(const float* q, const int8_t* k, const float* s, float* out,
                                      uint32_t dim, uint32_t seq_len, cudaStream_t st);
 

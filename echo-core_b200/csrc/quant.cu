@@ -10,6 +10,8 @@
 // not be compiled with fast-math.
 #include <cstdint>
 
+#include <cuda_fp16.h>
+
 #include "ec_common.cuh"
 #include "ec_internal.h"
 
@@ -161,7 +163,197 @@ __global__ void bump_lengths_kernel(AppendArgs a) {
     a.seq_len[s] = len + a.n_new;
 }
 
+// ------------------------------------------------- head norm + RoPE on K
+// echo-core-zig applies, to each token's K before it enters the cache, a
+// per-head RMS norm (src/inference/engine.zig:521-532: rms = sqrt(sum k^2 / d
+// + 1e-6); k = k * (1/rms) * w) and rotary position embedding over
+// interleaved pairs (:466-518: angle = pos * freq_i, freq_i = 1/base^(i/d);
+// (k0, k1) -> (k0 cos - k1 sin, k0 sin + k1 cos)).  Products and sums are
+// rounded one at a time (no contraction), as the Zig code computes them; the
+// sines and cosines are computed in double and rounded to fp32.
+struct PairRot { float c0, s0, c1, s1; };
+
+__device__ __forceinline__ PairRot pair_rotation(int pos, int lane, const float* inv_freq) {
+    // lane holds dims 4*lane .. 4*lane+3: pairs 2*lane and 2*lane+1
+    const float a0 = __fmul_rn((float)pos, inv_freq[2 * lane]);
+    const float a1 = __fmul_rn((float)pos, inv_freq[2 * lane + 1]);
+    double s0, c0, s1, c1;
+    sincos((double)a0, &s0, &c0);
+    sincos((double)a1, &s1, &c1);
+    return {(float)c0, (float)s0, (float)c1, (float)s1};
+}
+
+__device__ __forceinline__ float4 rotate(float4 x, const PairRot& r) {
+    float4 y;
+    y.x = __fsub_rn(__fmul_rn(x.x, r.c0), __fmul_rn(x.y, r.s0));
+    y.y = __fadd_rn(__fmul_rn(x.x, r.s0), __fmul_rn(x.y, r.c0));
+    y.z = __fsub_rn(__fmul_rn(x.z, r.c1), __fmul_rn(x.w, r.s1));
+    y.w = __fadd_rn(__fmul_rn(x.z, r.s1), __fmul_rn(x.w, r.c1));
+    return y;
+}
+
+// per-head RMS norm of one 128-float head held as float4 per lane
+__device__ __forceinline__ float4 head_rms_norm(float4 x, const uint16_t* w, int lane) {
+    float ss = __fadd_rn(__fadd_rn(__fmul_rn(x.x, x.x), __fmul_rn(x.y, x.y)),
+                         __fadd_rn(__fmul_rn(x.z, x.z), __fmul_rn(x.w, x.w)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
+    const float inv = __fdiv_rn(1.0f, rms);
+    const ushort4 wb = reinterpret_cast<const ushort4*>(w)[lane];
+    float4 y;
+    y.x = __fmul_rn(__fmul_rn(x.x, inv), __half2float(__ushort_as_half(wb.x)));
+    y.y = __fmul_rn(__fmul_rn(x.y, inv), __half2float(__ushort_as_half(wb.y)));
+    y.z = __fmul_rn(__fmul_rn(x.z, inv), __half2float(__ushort_as_half(wb.z)));
+    y.w = __fmul_rn(__fmul_rn(x.w, inv), __half2float(__ushort_as_half(wb.w)));
+    return y;
+}
+
+// append_kernel with K normed and rotated at its cache position before
+// quantization (one warp per (sequence, new token), as append_kernel)
+template <int HKV, bool ROW>
+__global__ void __launch_bounds__(256) append_rope_kernel(AppendArgs a) {
+    constexpr int D = 128;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int s = warp / a.n_new;
+    const int i = warp - s * a.n_new;
+    if (s >= a.num_seqs) return;
+    TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, a.host_offset, a.host_capacity,
+                 a.host_length, a.total_slots};
+    int32_t off, cap, len;
+    if (!tv.load(s, a.err, off, cap, len)) {
+        if (i == 0 && lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
+        return;
+    }
+    if ((int64_t)len + a.n_new > cap) {
+        if (i == 0 && lane == 0) flag_error(a.err, EC_DEVERR_OVERFLOW);
+        return;
+    }
+    const int pos = len + i;                  // the token's position in its sequence
+    const int64_t slot = (int64_t)off + pos;
+    const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
+    PairRot rot{};
+    if (a.rope) rot = pair_rotation(pos, lane, a.inv_freq);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const float* src = (t == 0 ? a.k : a.v) + src_row;
+        int8_t* dst = (t == 0 ? a.keys : a.values) + (size_t)slot * (HKV * D);
+        float* sc = t == 0 ? a.key_scales : a.val_scales;
+        float4 x[HKV];
+#pragma unroll
+        for (int g = 0; g < HKV; ++g) {
+            x[g] = __ldcs(reinterpret_cast<const float4*>(src) + g * 32 + lane);
+            if (t == 0) {
+                if (a.k_norm_w) x[g] = head_rms_norm(x[g], a.k_norm_w, lane);
+                if (a.rope) x[g] = rotate(x[g], rot);
+            }
+        }
+        float amax[HKV];
+#pragma unroll
+        for (int g = 0; g < HKV; ++g)
+            amax[g] = fmaxf(fmaxf(fabsf(x[g].x), fabsf(x[g].y)), fmaxf(fabsf(x[g].z), fabsf(x[g].w)));
+        if (ROW) {
+            float m = amax[0];
+#pragma unroll
+            for (int g = 1; g < HKV; ++g) m = fmaxf(m, amax[g]);
+            m = warp_max(m);
+#pragma unroll
+            for (int g = 0; g < HKV; ++g) amax[g] = m;
+        } else {
+#pragma unroll
+            for (int g = 0; g < HKV; ++g) amax[g] = warp_max(amax[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < HKV; ++g) {
+            const float scale = scale_of(amax[g]);
+            const float inv = __fdiv_rn(1.0f, scale);
+            const uint32_t b0 = (uint32_t)(q_body(x[g].x, inv) & 0xff);
+            const uint32_t b1 = (uint32_t)(q_body(x[g].y, inv) & 0xff);
+            const uint32_t b2 = (uint32_t)(q_body(x[g].z, inv) & 0xff);
+            const uint32_t b3 = (uint32_t)(q_body(x[g].w, inv) & 0xff);
+            reinterpret_cast<uint32_t*>(dst + g * D)[lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+            if (lane == 0) {
+                if (ROW) {
+                    if (g == 0) sc[slot] = scale;
+                } else {
+                    sc[(size_t)slot * HKV + g] = scale;
+                }
+            }
+        }
+    }
+}
+
+struct RopeRowsArgs {
+    float* x;
+    const int32_t* positions;
+    const uint16_t* norm_w;
+    uint32_t rows, num_heads;
+    int rope;
+    float inv_freq[64];
+};
+
+// one warp per (row, head): the Q side of the same pre-processing
+__global__ void __launch_bounds__(256) rope_rows_kernel(RopeRowsArgs a) {
+    const uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= (uint64_t)a.rows * a.num_heads) return;
+    const uint32_t r = (uint32_t)(w / a.num_heads);
+    float4* p = reinterpret_cast<float4*>(a.x + w * 128) + lane;
+    float4 x = *p;
+    if (a.norm_w) x = head_rms_norm(x, a.norm_w, lane);
+    if (a.rope) x = rotate(x, pair_rotation(a.positions[r], lane, a.inv_freq));
+    *p = x;
+}
+
 // ---------------------------------------------------------------- launchers
+cudaError_t launch_append_rope(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st) {
+    const int64_t warps = (int64_t)a.num_seqs * a.n_new;
+    if (warps == 0) return cudaSuccess;
+    const int threads = 256;
+    const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+#define EC_APPEND_CASE(H)                                                                      \
+    case H:                                                                                    \
+        if (row_mode) append_rope_kernel<H, true><<<(unsigned)blocks, threads, 0, st>>>(a);   \
+        else append_rope_kernel<H, false><<<(unsigned)blocks, threads, 0, st>>>(a);           \
+        break;
+    switch (num_kv_heads) {
+        EC_APPEND_CASE(1)
+        EC_APPEND_CASE(2)
+        EC_APPEND_CASE(4)
+        EC_APPEND_CASE(8)
+        default: return cudaErrorInvalidValue;
+    }
+#undef EC_APPEND_CASE
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (a.seq_len != nullptr) {
+        bump_lengths_kernel<<<(a.num_seqs + 127) / 128, 128, 0, st>>>(a);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+cudaError_t launch_rope_rows(float* x, uint32_t rows, uint32_t num_heads, const int32_t* positions,
+                             const uint16_t* norm_w, int rope, const float* inv_freq64,
+                             cudaStream_t st) {
+    const uint64_t warps = (uint64_t)rows * num_heads;
+    if (warps == 0) return cudaSuccess;
+    RopeRowsArgs a{};
+    a.x = x;
+    a.positions = positions;
+    a.norm_w = norm_w;
+    a.rows = rows;
+    a.num_heads = num_heads;
+    a.rope = rope;
+    for (int i = 0; i < 64; ++i) a.inv_freq[i] = inv_freq64[i];
+    const uint64_t blocks = (warps * 32 + 255) / 256;
+    if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
+    rope_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_quantize_rows(const float* in, int8_t* out, float* scales, uint32_t rows,
                                  uint32_t n, cudaStream_t st) {
     if (rows == 0) return cudaSuccess;

@@ -51,6 +51,7 @@ EXPORTS = (
     "ec_decode_attention_partial", "ec_lse_combine", "ec_prefill_attention",
     "ec_decode_attention_noalloc", "ec_kv_cache_step", "ec_kv_cache_step_host",
     "ec_kv_cache_snapshot_size", "ec_kv_cache_snapshot", "ec_kv_cache_restore",
+    "ec_kv_batch_append_rope", "ec_rope_rows",
 )
 
 
@@ -75,6 +76,20 @@ class KVLayer(ctypes.Structure):
                 ("key_scales", ctypes.c_void_p), ("val_scales", ctypes.c_void_p),
                 ("keys_fp32", ctypes.c_void_p), ("values_fp32", ctypes.c_void_p),
                 ("seq_len", ctypes.c_uint32)]
+
+
+class RopeDesc(ctypes.Structure):
+    """ec_rope_desc: rope_base (<= 0: no rotation), fp16 [128] norm weight or NULL."""
+    _fields_ = [("rope_base", ctypes.c_float), ("norm_weight", ctypes.c_void_p)]
+
+
+def rope_rows(x, rows: int, num_heads: int, positions=None, rope_base: float = 10000.0,
+              norm_weight=None, stream=None) -> None:
+    """In-place per-head RMS norm and RoPE of query rows (ec_rope_rows)."""
+    d = RopeDesc(rope_base, _ptr(norm_weight) if norm_weight is not None else None)
+    check(lib().ec_rope_rows(_ptr(x), rows, num_heads, 128,
+                             _ptr(positions) if positions is not None else None,
+                             ctypes.byref(d), _stream(stream)))
 
 
 class KVBatch(ctypes.Structure):
@@ -291,6 +306,15 @@ class BatchCache:
         d = self.desc()
         check(lib().ec_kv_batch_append(ctypes.byref(d), _ptr(k), _ptr(v), tokens_per_seq,
                                        _stream(stream)))
+
+    def append_rope(self, k, v, tokens_per_seq: int, rope_base: float = 10000.0,
+                    norm_weight=None, stream=None) -> None:
+        """append() with K normed and rotated at its cache position
+        (ec_kv_batch_append_rope)."""
+        d = self.desc()
+        r = RopeDesc(rope_base, _ptr(norm_weight) if norm_weight is not None else None)
+        check(lib().ec_kv_batch_append_rope(ctypes.byref(d), _ptr(k), _ptr(v), tokens_per_seq,
+                                            ctypes.byref(r), _stream(stream)))
 
     def decode(self, q, out, num_heads: int, softmax_scale: float, stream=None) -> None:
         d = self.desc()

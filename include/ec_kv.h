@@ -224,6 +224,30 @@ typedef struct ec_kv_batch {
 EC_API int ec_kv_batch_append(const ec_kv_batch* batch, const float* k, const float* v,
                        uint32_t tokens_per_seq, ec_stream_t stream);
 
+/* K pre-processing of echo-core-zig before the cache append
+ * (src/inference/engine.zig:544-559): a per-head RMS norm with an fp16 weight
+ * (:521-532; rms = sqrt(sum x^2 / 128 + 1e-6), x = x * (1/rms) * w), then
+ * rotary position embedding over interleaved pairs (:466-518; angle =
+ * pos * freq_i, freq_i = 1 / rope_base^(i/128); (x0, x1) -> (x0 cos - x1 sin,
+ * x0 sin + x1 cos)).  rope_base <= 0 skips the rotation, a NULL norm_weight
+ * (device, fp16 [128], 8-byte aligned) skips the norm. */
+typedef struct ec_rope_desc {
+    float rope_base;                /* 10000 in echo-core-zig */
+    const uint16_t* norm_weight;
+} ec_rope_desc;
+
+/* ec_kv_batch_append with K normed and rotated at each new token's position
+ * (its sequence's length before the call, plus its index in the chunk) before
+ * quantization; V as ec_kv_batch_append. */
+EC_API int ec_kv_batch_append_rope(const ec_kv_batch* batch, const float* k_new,
+                                   const float* v_new, uint32_t tokens_per_seq,
+                                   const ec_rope_desc* k_desc, ec_stream_t stream);
+/* The same norm and rotation in place on rows of num_heads * head_dim floats
+ * (the queries), row r at position positions[r] (device int32; may be NULL
+ * when rope_base <= 0). */
+EC_API int ec_rope_rows(float* x, uint32_t rows, uint32_t num_heads, uint32_t head_dim,
+                        const int32_t* positions, const ec_rope_desc* desc, ec_stream_t stream);
+
 /* Workspace (device bytes) ec_decode_attention needs for this batch shape on
  * the current device. */
 EC_API size_t ec_decode_workspace_size(uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim,

@@ -251,6 +251,46 @@ void oracle_decode_attention_f32(const float* keys, const float* values, uint32_
 }
 
 /*
+ * K pre-processing of echo-core-zig before its cache append
+ * (src/inference/engine.zig:544-559): per-head RMS norm with an fp16 weight
+ * (applyHeadNorm, :521-532) then RoPE over interleaved pairs (applyRoPE,
+ * :466-518).  x: [num_heads][head_dim] fp32 in place; norm_w: head_dim fp32
+ * values of the fp16 weight, or NULL; rope_base <= 0: no rotation.  Every
+ * product and sum is rounded on its own (volatile), as the Zig code evaluates
+ * them without contraction.
+ */
+void oracle_norm_rope(float* x, uint32_t num_heads, uint32_t head_dim, uint32_t pos,
+                      const float* norm_w, float rope_base) {
+    for (uint32_t h = 0; h < num_heads; ++h) {
+        float* p = x + (size_t)h * head_dim;
+        if (norm_w) {
+            float rms = 0.0f;
+            for (uint32_t i = 0; i < head_dim; ++i) {
+                volatile float sq = p[i] * p[i];
+                rms += sq;
+            }
+            rms = sqrtf(rms / (float)head_dim + 1e-6f);
+            const float inv_rms = 1.0f / rms;
+            for (uint32_t i = 0; i < head_dim; ++i) {
+                volatile float t = p[i] * inv_rms;
+                p[i] = t * norm_w[i];
+            }
+        }
+        if (rope_base > 0.0f) {
+            for (uint32_t i = 0; i < head_dim; i += 2) {
+                const float freq = 1.0f / powf(rope_base, (float)i / (float)head_dim);
+                volatile float angle = (float)pos * freq;
+                const float c = cosf(angle), s = sinf(angle);
+                const float x0 = p[i], x1 = p[i + 1];
+                volatile float a = x0 * c, b = x1 * s, d = x0 * s, e = x1 * c;
+                p[i] = a - b;
+                p[i + 1] = d + e;
+            }
+        }
+    }
+}
+
+/*
  * Chunked-prefill attention.  The reference has no chunked prefill: it feeds
  * a prompt one token at a time (src/main.cpp:404-405), each token running the
  * decode loop above over the cache as it stands after that token's append

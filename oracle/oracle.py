@@ -54,6 +54,7 @@ def lib():
                                               _u32, _u32, ctypes.c_float, ctypes.c_int, _f32p]
         L.oracle_decode_attention_f32.argtypes = [_f32p, _f32p, _u32, _f32p, _f32p, _u32, _u32,
                                                   _u32, ctypes.c_float, _f32p]
+        L.oracle_norm_rope.argtypes = [_f32p, _u32, _u32, _u32, _f32p, ctypes.c_float]
         L.oracle_prefill_attention.argtypes = [_i8p, _i8p, _f32p, _f32p, _u32, _u32, _f32p, _f32p,
                                                _u32, _u32, _u32, ctypes.c_float, ctypes.c_int, _f32p]
         _lib = L
@@ -164,6 +165,17 @@ def decode_attention_f32(keys, values, kv_len, q, num_heads, num_kv_heads, head_
                                       _p(out, _f32p), num_heads, num_kv_heads, head_dim,
                                       ctypes.c_float(softmax_scale), _p(scratch, _f32p))
     return out.reshape(num_heads, head_dim)
+
+
+def norm_rope(x, pos, rope_base=10000.0, norm_w=None):
+    """echo-core-zig's per-head RMS norm (fp32 values of the fp16 weight, or
+    None) then RoPE at position pos, on x [num_heads, 128]; returns a copy."""
+    x = np.array(x, np.float32, copy=True, order="C")
+    H, d = x.shape
+    w = None if norm_w is None else np.ascontiguousarray(norm_w, np.float32)
+    lib().oracle_norm_rope(_p(x, _f32p), H, d, pos, _p(w, _f32p) if w is not None else None,
+                           ctypes.c_float(rope_base))
+    return x
 
 
 def prefill_attention(keys, values, kscales, vscales, past_len, n_new, q, num_heads,
