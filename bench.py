@@ -593,8 +593,14 @@ def run_cp_arm(args, rank, world, local_rank):
     scale = W.softmax_scale(D)
     stream = torch.cuda.current_stream()
 
+    fused = world > 1 and not args.cp_nccl
+    cx = ranks.CPExchange(1, H) if fused else None
+
     def step():
         bc.decode_partial(qg, po_local, pml_local, H, scale, stream)
+        if fused:
+            cx.combine(po_local, pml_local, out, stream)     # exchange + merge, one kernel
+            return
         if world > 1:
             po, pml = ranks.gather_partials(po_local, pml_local)
         else:
@@ -625,8 +631,13 @@ def run_cp_arm(args, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(float(t[0]) / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": cfg.name, "ctx": total, "parallelism": f"context-split x{world}"},
+            "config": {"workload": cfg.name, "ctx": total, "parallelism": f"context-split x{world}",
+                       "exchange": ("peer stores + merge in one kernel (ec_cp_exchange_combine)"
+                                    if fused else "NCCL all-gather + ec_lse_combine"
+                                    if world > 1 else "none")},
             "pct_of_hbm_peak": round(100 * gbs / (peak * world), 1)}), flush=True)
+    if cx is not None:
+        cx.close()
 
 
 def main():
@@ -642,6 +653,8 @@ def main():
                     help="override the sequence count (small profiling cases)")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
     ap.add_argument("--ctx", type=int, default=None, help="override every sequence's context")
+    ap.add_argument("--cp-nccl", action="store_true",
+                    help="config 4: exchange partials with an NCCL all-gather instead of peer stores")
     ap.add_argument("--kv-fp32", action="store_true",
                     help="decode over the fp32 cache mode (one sequence per rank)")
     args = ap.parse_args()

@@ -1,0 +1,114 @@
+// cp_exchange.cu -- the context-parallel exchange and merge in one kernel,
+// over NVLink peer memory (one process per GPU).
+//
+// Context parallelism splits one long sequence's cached tokens across ranks;
+// each rank computes the unnormalised partial (m, l, O) of its slice per
+// (sequence, head) (ec_decode_attention_partial).  Instead of an all-gather
+// followed by a merge launch, every CTA of this kernel owns one (sequence,
+// head): it stores its rank's partial into slot [rank] of every rank's
+// receive buffer with plain peer stores (CUDA IPC mappings, no multicast),
+// publishes a per-(sequence, head) flag with release semantics, waits with
+// acquire loads until every rank's flag for this step has arrived in its own
+// buffer, and merges the world's partials in rank order.  Receive buffers are
+// double-buffered by step parity: a fast rank publishing step e+1 never
+// overwrites what a slow rank is still merging for step e.  Every wait is
+// bounded (about 1 s of clock64 cycles); a wait that runs out records
+// EC_DEVERR_TIMEOUT in the error word and the CTA writes zeros.
+#include <cstdint>
+
+#include "ec_common.cuh"
+#include "ec_internal.h"
+
+namespace ec {
+namespace {
+
+constexpr int D = 128;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(D) cp_exchange_kernel(CpExchangeArgs a) {
+    const int s = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const int S = a.num_seqs, H = a.num_heads, W = a.world;
+    const size_t sh = (size_t)s * H + h;
+    const int par = a.epoch & 1;
+    // per rank buffer: [2 parities][W ranks][S][H] of O (D floats), ml (2), flag (1)
+    const size_t n_sh = (size_t)S * H;
+    auto o_at = [&](float* base, int p, int r) { return base + ((size_t)(p * W + r) * n_sh + sh) * D; };
+    auto ml_at = [&](float* base, int p, int r) {
+        return base + (size_t)2 * W * n_sh * D + ((size_t)(p * W + r) * n_sh + sh) * 2;
+    };
+    auto flag_at = [&](float* base, int p, int r) {
+        return reinterpret_cast<uint32_t*>(base + (size_t)2 * W * n_sh * (D + 2)) +
+               (size_t)(p * W + r) * n_sh + sh;
+    };
+
+    // ---- publish this rank's partial into slot [rank] of every rank's buffer
+    const float o = a.part_o[sh * D + d];
+    const float ml = d < 2 ? a.part_ml[sh * 2 + d] : 0.0f;
+    for (int r = 0; r < W; ++r) {
+        float* base = a.peer_base[r];
+        o_at(base, par, a.rank)[d] = o;
+        if (d < 2) ml_at(base, par, a.rank)[d] = ml;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (d == 0)
+        for (int r = 0; r < W; ++r) st_release_sys(flag_at(a.peer_base[r], par, a.rank), a.epoch);
+
+    // ---- wait for every rank's flag of this step in the local buffer
+    __shared__ int s_bad;
+    if (d == 0) {
+        int bad = 0;
+        float* mine = a.peer_base[a.rank];
+        for (int r = 0; r < W && !bad; ++r) {
+            const uint32_t* f = flag_at(mine, par, r);
+            if (ld_acquire_sys(f) == a.epoch) continue;
+            const long long t0 = clock64();
+            while (ld_acquire_sys(f) != a.epoch) {
+                if (clock64() - t0 > kWaitBudgetCycles) { bad = 1; break; }
+                __nanosleep(64);
+            }
+        }
+        if (bad) flag_error(a.err, EC_DEVERR_TIMEOUT);
+        s_bad = bad;
+    }
+    __syncthreads();
+    float* mine = a.peer_base[a.rank];
+    if (s_bad) {
+        a.out[sh * D + d] = 0.0f;
+        return;
+    }
+    // ---- merge in rank order (the LSE merge of ec_lse_combine)
+    float M = -INFINITY;
+    for (int r = 0; r < W; ++r) M = fmaxf(M, ml_at(mine, par, r)[0]);
+    float so = 0.0f, sl = 0.0f;
+    for (int r = 0; r < W; ++r) {
+        const float* mlr = ml_at(mine, par, r);
+        const float f = mlr[0] == -INFINITY ? 0.0f : exp2f(mlr[0] - M);
+        so += f * o_at(mine, par, r)[d];
+        sl += f * mlr[1];
+    }
+    a.out[sh * D + d] = sl > 0.0f ? __fdiv_rn(so, sl) : 0.0f;
+}
+
+}  // namespace
+
+size_t cp_exchange_buffer_bytes(int world, int num_seqs, int num_heads) {
+    const size_t n = (size_t)2 * world * num_seqs * num_heads;
+    return n * (D + 2) * sizeof(float) + n * sizeof(uint32_t);
+}
+
+cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st) {
+    if (a.num_seqs <= 0 || a.num_heads <= 0) return cudaSuccess;
+    cp_exchange_kernel<<<dim3(a.num_seqs, a.num_heads), D, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace ec

@@ -527,6 +527,111 @@ int ec_kv_cache_restore(ec_kv_cache* cache, const void* host, size_t bytes) {
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_cache_restore");
 }
 
+// ------------------------------------------------- context-parallel comm
+struct ec_cp_comm {
+    int world, rank, num_seqs, num_heads, device;
+    float* local;                        // this rank's receive buffer
+    float* peers[ec::kCpMaxWorld];       // opened IPC mappings (own slot = local)
+    bool opened;
+};
+
+int ec_cp_comm_create(uint32_t world, uint32_t rank, uint32_t num_seqs, uint32_t num_heads,
+                      ec_cp_comm** out, void* ipc_handle) {
+    if (!out || !ipc_handle) return fail(EC_ERR_INVALID_ARGUMENT, "cp_comm_create: null argument");
+    if (world == 0 || world > (uint32_t)ec::kCpMaxWorld || rank >= world)
+        return fail(EC_ERR_INVALID_ARGUMENT, "cp_comm_create: world %u / rank %u (world at most %d)",
+                    world, rank, ec::kCpMaxWorld);
+    if (num_seqs == 0 || num_heads == 0 || (uint64_t)num_seqs * num_heads > 148u * 16u)
+        return fail(EC_ERR_UNSUPPORTED, "cp_comm_create: num_seqs * num_heads must be in 1..2368");
+    ec_cp_comm* c = new (std::nothrow) ec_cp_comm();
+    if (!c) return fail(EC_ERR_CUDA, "cp_comm_create: host allocation failed");
+    c->world = (int)world;
+    c->rank = (int)rank;
+    c->num_seqs = (int)num_seqs;
+    c->num_heads = (int)num_heads;
+    c->opened = false;
+    cudaGetDevice(&c->device);
+    const size_t bytes = ec::cp_exchange_buffer_bytes(c->world, c->num_seqs, c->num_heads);
+    cudaError_t e = cudaMalloc(&c->local, bytes);
+    if (e == cudaSuccess) e = cudaMemset(c->local, 0, bytes);   // flags start below epoch 1
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->local);
+    if (e != cudaSuccess) {
+        cudaFree(c->local);
+        delete c;
+        return cuda_fail(e, "cp_comm_create: receive buffer");
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == EC_CP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(ipc_handle, &h, sizeof h);
+    for (auto& p : c->peers) p = nullptr;
+    c->peers[c->rank] = c->local;
+    *out = c;
+    return EC_OK;
+}
+
+int ec_cp_comm_open(ec_cp_comm* c, const void* handles) {
+    if (!c || !handles) return fail(EC_ERR_INVALID_ARGUMENT, "cp_comm_open: null argument");
+    if (c->opened) return fail(EC_ERR_INVALID_ARGUMENT, "cp_comm_open: already open");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(c->device);
+    const uint8_t* hp = static_cast<const uint8_t*>(handles);
+    cudaError_t e = cudaSuccess;
+    int r = 0;
+    for (; r < c->world && e == cudaSuccess; ++r) {
+        if (r == c->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hp + (size_t)r * EC_CP_HANDLE_BYTES, sizeof h);
+        void* p = nullptr;
+        e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        c->peers[r] = static_cast<float*>(p);
+    }
+    if (e != cudaSuccess) {
+        for (int q = 0; q < c->world; ++q)
+            if (q != c->rank && c->peers[q]) { cudaIpcCloseMemHandle(c->peers[q]); c->peers[q] = nullptr; }
+        cudaSetDevice(prev);
+        return cuda_fail(e, "cp_comm_open: cudaIpcOpenMemHandle of a peer's buffer");
+    }
+    c->opened = true;
+    cudaSetDevice(prev);
+    return EC_OK;
+}
+
+void ec_cp_comm_destroy(ec_cp_comm* c) {
+    if (!c) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < c->world; ++r)
+        if (r != c->rank && c->peers[r]) cudaIpcCloseMemHandle(c->peers[r]);
+    cudaFree(c->local);
+    cudaSetDevice(prev);
+    delete c;
+}
+
+int ec_cp_exchange_combine(ec_cp_comm* c, const float* part_o, const float* part_ml,
+                           uint32_t epoch, float* out, ec_stream_t stream) {
+    if (!c || !part_o || !part_ml || !out)
+        return fail(EC_ERR_INVALID_ARGUMENT, "cp_exchange_combine: null argument");
+    if (!c->opened && c->world > 1)
+        return fail(EC_ERR_INVALID_ARGUMENT, "cp_exchange_combine: comm not opened");
+    if (epoch == 0) return fail(EC_ERR_INVALID_ARGUMENT, "cp_exchange_combine: epoch must start at 1");
+    ec::CpExchangeArgs a{};
+    for (int r = 0; r < c->world; ++r) a.peer_base[r] = c->peers[r];
+    a.part_o = part_o;
+    a.part_ml = part_ml;
+    a.out = out;
+    a.err = nullptr;
+    a.world = c->world;
+    a.rank = c->rank;
+    a.num_seqs = c->num_seqs;
+    a.num_heads = c->num_heads;
+    a.epoch = epoch;
+    cudaError_t e = ec::launch_cp_exchange(a, as_stream(stream));
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, "cp_exchange_combine launch");
+}
+
 // ------------------------------------------------------------ batched cache
 static int check_batch(const ec_kv_batch* b, const char* who) {
     if (!b) return fail(EC_ERR_INVALID_ARGUMENT, "%s: batch is NULL", who);

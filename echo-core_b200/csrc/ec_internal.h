@@ -106,6 +106,20 @@ int set_last_error(int status, const char* msg);
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
                                int num_seqs, int num_heads, float* out, cudaStream_t st);
 
+// Context-parallel exchange + merge over peer memory (cp_exchange.cu).
+constexpr int kCpMaxWorld = 8;
+struct CpExchangeArgs {
+    float* peer_base[kCpMaxWorld];   // every rank's receive buffer, this rank's own included
+    const float* part_o;             // this rank's partial O [num_seqs][num_heads][128]
+    const float* part_ml;            // and (m, l) [num_seqs][num_heads][2]
+    float* out;                      // merged output [num_seqs][num_heads][128]
+    int32_t* err;
+    int world, rank, num_seqs, num_heads;
+    uint32_t epoch;
+};
+size_t cp_exchange_buffer_bytes(int world, int num_seqs, int num_heads);
+cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st);
+
 // Decode attention over the fp32 cache mode (use_kv_quantization = false):
 // keys / values [len][num_kv_heads][128] fp32, q [num_heads][128] unscaled,
 // out [num_heads][128].  Split-K over chunks of kF32ChunkTokens tokens; the

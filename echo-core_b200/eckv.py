@@ -52,6 +52,7 @@ EXPORTS = (
     "ec_decode_attention_noalloc", "ec_kv_cache_step", "ec_kv_cache_step_host",
     "ec_kv_cache_snapshot_size", "ec_kv_cache_snapshot", "ec_kv_cache_restore",
     "ec_kv_batch_append_rope", "ec_rope_rows",
+    "ec_cp_comm_create", "ec_cp_comm_open", "ec_cp_exchange_combine", "ec_cp_comm_destroy",
 )
 
 

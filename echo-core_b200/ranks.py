@@ -12,6 +12,9 @@ data layout and need no new arithmetic:
   (m, l, O) of its slice with ``ec_decode_attention_partial``, the states are
   all-gathered (``gather_partials``) and every rank merges them, in rank
   order, with ``ec_lse_combine``.  That all-gather is the only exchange.
+  ``CPExchange`` does the exchange and the merge in one kernel instead: each
+  rank stores its partial straight into every rank's receive buffer over
+  NVLink (CUDA IPC peer mappings) and merges once all have arrived.
 
 Process groups come from ``torch.distributed`` (NCCL on GPUs, gloo for the
 CPU tests of this module); nothing here computes attention.
@@ -55,3 +58,54 @@ def gather_partials(part_o, part_ml, group=None):
     out_o = out[:, :no].reshape((world,) + tuple(part_o.shape))
     out_ml = out[:, no:].reshape((world,) + tuple(part_ml.shape))
     return out_o, out_ml
+
+
+class CPExchange:
+    """The context-parallel exchange and merge in one kernel over NVLink peer
+    memory (ec_cp_exchange_combine), in place of ``gather_partials`` plus
+    ``ec_lse_combine``.
+
+    Construction is collective: every rank creates its receive buffer and the
+    ranks swap CUDA IPC handles over the process group (any backend; the
+    handles are 64 bytes of host data).  ``combine`` is called by every rank
+    once per step, in the same order; ``close`` is collective too, so that no
+    rank frees its buffer while a peer may still store into it."""
+
+    def __init__(self, num_seqs: int, num_heads: int, group=None):
+        import ctypes
+        import torch.distributed as dist
+        import eckv
+        self._lib = eckv.lib()
+        self._group = group
+        dist_on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if dist_on else 1
+        self.rank = dist.get_rank(group) if dist_on else 0
+        handle = (ctypes.c_char * 64)()
+        self._h = ctypes.c_void_p()
+        eckv.check(self._lib.ec_cp_comm_create(self.world, self.rank, num_seqs, num_heads,
+                                               ctypes.byref(self._h), handle))
+        if self.world > 1:
+            got = [None] * self.world
+            dist.all_gather_object(got, bytes(handle), group=group)
+            blob = b"".join(got)
+            eckv.check(self._lib.ec_cp_comm_open(self._h, ctypes.create_string_buffer(blob, len(blob))))
+        self.epoch = 0
+
+    def combine(self, part_o, part_ml, out, stream=None) -> None:
+        import ctypes
+        import eckv
+        self.epoch += 1
+        eckv.check(self._lib.ec_cp_exchange_combine(self._h, eckv._ptr(part_o), eckv._ptr(part_ml),
+                                                    ctypes.c_uint32(self.epoch), eckv._ptr(out),
+                                                    eckv._stream(stream)))
+
+    def close(self) -> None:
+        if not getattr(self, "_h", None) or not self._h.value:
+            return
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self._group)
+        self._lib.ec_cp_comm_destroy(self._h)
+        self._h = None

@@ -277,6 +277,28 @@ EC_API int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t nu
                    uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim, float* out,
                    ec_stream_t stream);
 
+/* Context parallelism with the exchange and the merge in one kernel over
+ * NVLink peer memory, instead of an all-gather plus ec_lse_combine.  One
+ * process per GPU.  Each rank creates a comm (a receive buffer on its
+ * current device, double-buffered by step parity) and gets its 64-byte CUDA
+ * IPC handle; the ranks exchange handles (any host channel, e.g. a
+ * torch.distributed all-gather of the bytes, in rank order) and open them.
+ * Per step every rank calls ec_cp_exchange_combine with its partial state
+ * from ec_decode_attention_partial and the same epoch (1, 2, 3, ...): its
+ * partial is stored into every rank's buffer, and the merged output (rank
+ * order, as ec_lse_combine) is written once every rank's partial for that
+ * epoch has arrived.  Waits are bounded (about 1 s); a rank that never
+ * arrives makes the others flag EC_DEVERR_TIMEOUT and write zeros.
+ * world <= 8; num_seqs * num_heads <= 2368 (one CTA each, all resident). */
+#define EC_CP_HANDLE_BYTES 64
+typedef struct ec_cp_comm ec_cp_comm;
+EC_API int ec_cp_comm_create(uint32_t world, uint32_t rank, uint32_t num_seqs,
+                             uint32_t num_heads, ec_cp_comm** out, void* ipc_handle);
+EC_API int ec_cp_comm_open(ec_cp_comm* comm, const void* handles);
+EC_API int ec_cp_exchange_combine(ec_cp_comm* comm, const float* part_o, const float* part_ml,
+                                  uint32_t epoch, float* out, ec_stream_t stream);
+EC_API void ec_cp_comm_destroy(ec_cp_comm* comm);
+
 /* Chunked-prefill attention.  The reference has no chunked prefill: it feeds
  * a prompt one token at a time (src/main.cpp:404-405), each token running the
  * decode loop of src/inference.cpp:321-392 over the cache as it stands after
