@@ -648,6 +648,22 @@ cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t 
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// Tensor map over [rows][hkv * 128] fp32 (the fp32 cache mode); box = one
+// head's 128 floats x box_rows tokens, no swizzle.
+cudaError_t make_f32_row_map(CUtensorMap* m, const float* base, int hkv, uint64_t rows,
+                             int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)hkv * D, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)hkv * D * sizeof(float)};
+    const cuuint32_t box[2] = {D, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms) {
     DecodePlan best{T, 1};
     if (max_seq_len <= 0 || num_seqs <= 0) return best;

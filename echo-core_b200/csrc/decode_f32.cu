@@ -28,26 +28,65 @@ constexpr int D = 128;
 constexpr int kWarps = 4;
 constexpr unsigned kFull = 0xffffffffu;
 
+// 2-D tiled TMA load (no multicast) with an L2 eviction hint.
+__device__ __forceinline__ void tma_load_2d_f(void* dst, const CUtensorMap* map, int x, int y,
+                                              uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 template <int GROUP>
-__global__ void __launch_bounds__(kWarps * 32)
-    decode_f32_kernel(const float* __restrict__ keys, const float* __restrict__ values, int hkv,
-                      int len, int chunk_tokens, const float* __restrict__ q, float q_mul,
+struct F32Geo {
+    static constexpr int T = 32 / GROUP;                   // tokens per batch; GROUP * T = 32
+    static constexpr int STAGE = T * 2 * D * 4;            // K and V rows of one batch
+    // A multiple of the 4 consumer warps: stage s is always consumed by warp
+    // s % 4, whose successive uses of it are then exactly one barrier phase
+    // apart (a waiter two phases ahead would alias the parity).
+    static constexpr int NST = STAGE <= 8192 ? 8 : 4;
+    // + 128: the dynamic region starts after the static merge arrays, at an
+    // offset that need not be 128-byte aligned (tensor copies require it)
+    static constexpr int SMEM = 128 + NST * STAGE + 2 * NST * 8;
+    static_assert(NST % 4 == 0, "stages must be a multiple of the consumer warps");
+};
+
+// 4 consumer warps (0-3) and one producer warp (4).  The producer streams the
+// chunk's K and V rows batch by batch into a ring of NST shared-memory
+// stages with 512-byte bulk copies (one per row, no multicast); consumer warp
+// w takes batches w, w+4, w+8, ... and keeps its own online-softmax state.
+template <int GROUP>
+__global__ void __launch_bounds__((kWarps + 1) * 32)
+    decode_f32_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                      const __grid_constant__ CUtensorMap tmap_v, int hkv, int len,
+                      int chunk_tokens, const float* __restrict__ q, float q_mul,
                       float* __restrict__ part_o, float* __restrict__ part_ml) {
-    constexpr int T = 32 / GROUP;             // tokens per batch; GROUP * T = 32
+    using G = F32Geo<GROUP>;
+    constexpr int T = G::T, NST = G::NST;
     constexpr int LOGT = T == 32 ? 5 : T == 16 ? 4 : T == 8 ? 3 : T == 4 ? 2 : 1;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                               ~uintptr_t(127));
+    float* ring = reinterpret_cast<float*>(smem);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * G::STAGE);
+    uint64_t* empty = full + NST;
     const int chunk = blockIdx.x, g = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = hkv * GROUP;
-    const size_t row = (size_t)hkv * D;       // floats per token
+    const int c0 = chunk * chunk_tokens;
+    const int c1 = min(len, c0 + chunk_tokens);
+    const int nb = (c1 - c0 + T - 1) / T;     // batches in this chunk
 
-    // q of the group's heads, scaled as src/inference.cpp:322-325 does
-    float qr[GROUP][4];
-#pragma unroll
-    for (int j = 0; j < GROUP; ++j) {
-        const float4 x = reinterpret_cast<const float4*>(q + (size_t)(g + j * hkv) * D)[lane];
-        qr[j][0] = x.x * q_mul; qr[j][1] = x.y * q_mul;
-        qr[j][2] = x.z * q_mul; qr[j][3] = x.w * q_mul;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NST; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        fence_mbar_init();
     }
+    __syncthreads();
+
     float o[GROUP][4], m_run[GROUP], l_run[GROUP];
 #pragma unroll
     for (int j = 0; j < GROUP; ++j) {
@@ -57,100 +96,122 @@ __global__ void __launch_bounds__(kWarps * 32)
         for (int u = 0; u < 4; ++u) o[j][u] = 0.0f;
     }
 
-    const int c0 = chunk * chunk_tokens;
-    const int c1 = min(len, c0 + chunk_tokens);
-    const int per = (c1 - c0 + kWarps - 1) / kWarps;
-    const int w0 = c0 + warp * per, w1 = min(c1, w0 + per);
-    const int mh = lane >> LOGT;              // this lane's head after the reduction
-    constexpr float kLog2e = 1.4426950408889634f;
-
-    for (int t0 = w0; t0 < w1; t0 += T) {
-        // ---- the batch's K and V rows, all loads in flight together where the
-        // registers allow (groups 2 and 4: 8 or 16 tokens); groups 1 and 8
-        // load each row where it is used
-        constexpr bool kEarly = GROUP == 2 || GROUP == 4;
-        float4 kr[T], vr[T];
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-            kr[t] = vr[t] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (kEarly && t0 + t < w1) {
-                const size_t base = (size_t)(t0 + t) * row + (size_t)g * D;
-                kr[t] = __ldcs(reinterpret_cast<const float4*>(keys + base) + lane);
-                vr[t] = __ldcs(reinterpret_cast<const float4*>(values + base) + lane);
+    if (warp == kWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int issued = 0;
+            for (int b = 0; b < nb; ++b) {
+                const int s = b % NST;
+                if (b >= NST && !mbar_wait(&empty[s], ((b / NST) - 1) & 1)) {
+                    flag_error(nullptr, EC_DEVERR_TIMEOUT);
+                    break;
+                }
+                const int t0 = c0 + b * T;
+                // two boxes of [T tokens][128 floats] (rows past the cache read as
+                // zeros; rows past the chunk are masked by the consumer)
+                mbar_arrive_expect_tx(&full[s], (uint32_t)G::STAGE);
+                float* st = ring + (size_t)s * (G::STAGE / 4);
+                tma_load_2d_f(st, &tmap_k, g * D, t0, &full[s], pol);
+                tma_load_2d_f(st + T * D, &tmap_v, g * D, t0, &full[s], pol);
+                issued = b + 1;
             }
+            // never leave with copies in flight into this CTA's shared memory
+            for (int b = max(0, issued - NST); b < issued; ++b) mbar_wait(&full[b % NST], (b / NST) & 1);
         }
-        // ---- scores: GROUP x T partial dots, then a reduce-scatter
-        float v[32];
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-            float4 k = kr[t];
-            if (!kEarly && t0 + t < w1)
-                k = __ldcs(reinterpret_cast<const float4*>(keys + (size_t)(t0 + t) * row + (size_t)g * D) + lane);
-#pragma unroll
-            for (int j = 0; j < GROUP; ++j)
-                v[j * T + t] = fmaf(qr[j][0], k.x, fmaf(qr[j][1], k.y, fmaf(qr[j][2], k.z, qr[j][3] * k.w)));
-        }
-#pragma unroll
-        for (int n = 16; n >= 1; n >>= 1) {       // lane L ends with index L
-            const bool up = lane & n;
-#pragma unroll
-            for (int i = 0; i < n; ++i) {
-                const float keep = up ? v[i + n] : v[i];
-                const float send = up ? v[i] : v[i + n];
-                v[i] = keep + __shfl_xor_sync(kFull, send, n);
-            }
-        }
-        const int mt = lane & (T - 1);
-        float s = t0 + mt < w1 ? v[0] * kLog2e : -INFINITY;
-        // ---- online softmax per head (the T lanes of a head are adjacent)
-        float bm = s;
-#pragma unroll
-        for (int n = 1; n < T; n <<= 1) bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, n));
-        float m_new[GROUP];
+    } else {
+        // ------------------------------------------------------------ consumers
+        float qr[GROUP][4];   // q of the group's heads, scaled as src/inference.cpp:322-325 does
 #pragma unroll
         for (int j = 0; j < GROUP; ++j) {
-            m_new[j] = fmaxf(m_run[j], __shfl_sync(kFull, bm, j * T));
-            const float corr = m_new[j] == -INFINITY ? 1.0f : exp2f(m_run[j] - m_new[j]);
-            l_run[j] *= corr;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) o[j][u] *= corr;
-            m_run[j] = m_new[j];
+            const float4 x = reinterpret_cast<const float4*>(q + (size_t)(g + j * hkv) * D)[lane];
+            qr[j][0] = x.x * q_mul; qr[j][1] = x.y * q_mul;
+            qr[j][2] = x.z * q_mul; qr[j][3] = x.w * q_mul;
         }
-        float mine = m_run[0];
+        const int mh = lane >> LOGT;          // this lane's head after the reduction
+        constexpr float kLog2e = 1.4426950408889634f;
+        for (int b = warp; b < nb; b += kWarps) {
+            const int s = b % NST;
+            if (!mbar_wait(&full[s], (b / NST) & 1)) {
+                if (lane == 0) flag_error(nullptr, EC_DEVERR_TIMEOUT);
+                break;
+            }
+            const int t0 = c0 + b * T;
+            const float* st = ring + (size_t)s * (G::STAGE / 4);
+            // ---- scores: GROUP x T partial dots, then a reduce-scatter
+            float v[32];
 #pragma unroll
-        for (int j = 1; j < GROUP; ++j)
-            if (mh == j) mine = m_run[j];
-        const float p = s == -INFINITY ? 0.0f : exp2f(s - mine);
-        float ps = p;
+            for (int t = 0; t < T; ++t) {
+                const float4 k = reinterpret_cast<const float4*>(st + t * D)[lane];
 #pragma unroll
-        for (int n = 1; n < T; n <<= 1) ps += __shfl_xor_sync(kFull, ps, n);
+                for (int j = 0; j < GROUP; ++j)
+                    v[j * T + t] = fmaf(qr[j][0], k.x, fmaf(qr[j][1], k.y, fmaf(qr[j][2], k.z, qr[j][3] * k.w)));
+            }
 #pragma unroll
-        for (int j = 0; j < GROUP; ++j) l_run[j] += __shfl_sync(kFull, ps, j * T);
-        // ---- O += p V
+            for (int n = 16; n >= 1; n >>= 1) {       // lane L ends with index L
+                const bool up = lane & n;
 #pragma unroll
-        for (int t = 0; t < T; ++t) {
-            float4 vv = vr[t];
-            if (!kEarly && t0 + t < w1)
-                vv = __ldcs(reinterpret_cast<const float4*>(values + (size_t)(t0 + t) * row + (size_t)g * D) + lane);
+                for (int i = 0; i < n; ++i) {
+                    const float keep = up ? v[i + n] : v[i];
+                    const float send = up ? v[i] : v[i + n];
+                    v[i] = keep + __shfl_xor_sync(kFull, send, n);
+                }
+            }
+            const int mt = lane & (T - 1);
+            const float sc = t0 + mt < c1 ? v[0] * kLog2e : -INFINITY;
+            // ---- online softmax per head (the T lanes of a head are adjacent)
+            float bm = sc;
+#pragma unroll
+            for (int n = 1; n < T; n <<= 1) bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, n));
 #pragma unroll
             for (int j = 0; j < GROUP; ++j) {
-                const float pj = __shfl_sync(kFull, p, j * T + t);
-                o[j][0] = fmaf(pj, vv.x, o[j][0]); o[j][1] = fmaf(pj, vv.y, o[j][1]);
-                o[j][2] = fmaf(pj, vv.z, o[j][2]); o[j][3] = fmaf(pj, vv.w, o[j][3]);
+                const float mn = fmaxf(m_run[j], __shfl_sync(kFull, bm, j * T));
+                const float corr = mn == -INFINITY ? 1.0f : exp2f(m_run[j] - mn);
+                l_run[j] *= corr;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) o[j][u] *= corr;
+                m_run[j] = mn;
             }
+            float mine = m_run[0];
+#pragma unroll
+            for (int j = 1; j < GROUP; ++j)
+                if (mh == j) mine = m_run[j];
+            const float p = sc == -INFINITY ? 0.0f : exp2f(sc - mine);
+            float ps = p;
+#pragma unroll
+            for (int n = 1; n < T; n <<= 1) ps += __shfl_xor_sync(kFull, ps, n);
+#pragma unroll
+            for (int j = 0; j < GROUP; ++j) l_run[j] += __shfl_sync(kFull, ps, j * T);
+            // ---- O += p V (rows past the chunk end are stale shared memory: p = 0,
+            // and they are skipped so that a stale NaN cannot leak in)
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+                if (t0 + t >= c1) break;
+                const float4 vv = reinterpret_cast<const float4*>(st + (T + t) * D)[lane];
+#pragma unroll
+                for (int j = 0; j < GROUP; ++j) {
+                    const float pj = __shfl_sync(kFull, p, j * T + t);
+                    o[j][0] = fmaf(pj, vv.x, o[j][0]); o[j][1] = fmaf(pj, vv.y, o[j][1]);
+                    o[j][2] = fmaf(pj, vv.z, o[j][2]); o[j][3] = fmaf(pj, vv.w, o[j][3]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
     }
 
     // ---- merge the CTA's warps, write the chunk's (m, l, O) per head
     __shared__ float s_ml[kWarps][GROUP][2];
     __shared__ __align__(16) float s_o[kWarps][GROUP][D];
+    if (warp < kWarps) {
 #pragma unroll
-    for (int j = 0; j < GROUP; ++j) {
-        *reinterpret_cast<float4*>(&s_o[warp][j][4 * lane]) = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
-        if (lane == 0) { s_ml[warp][j][0] = m_run[j]; s_ml[warp][j][1] = l_run[j]; }
+        for (int j = 0; j < GROUP; ++j) {
+            *reinterpret_cast<float4*>(&s_o[warp][j][4 * lane]) = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
+            if (lane == 0) { s_ml[warp][j][0] = m_run[j]; s_ml[warp][j][1] = l_run[j]; }
+        }
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < GROUP * D; idx += kWarps * 32) {
+    for (int idx = threadIdx.x; idx < GROUP * D; idx += (kWarps + 1) * 32) {
         const int j = idx / D, d = idx % D;
         float M = -INFINITY;
 #pragma unroll
@@ -170,29 +231,83 @@ __global__ void __launch_bounds__(kWarps * 32)
 
 }  // namespace
 
-int f32_decode_chunks(int len) { return len <= 0 ? 0 : (len + kF32ChunkTokens - 1) / kF32ChunkTokens; }
+// Chunking: at least 512 tokens per CTA, and no more chunks than about three
+// resident CTAs per SM across the KV heads, so that long contexts run in
+// long-lived CTAs and the log-sum-exp merge sees at most a few hundred parts.
+static int f32_target_chunks(int num_kv_heads) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+            sms = 148;
+    }
+    const int t = 3 * sms / (num_kv_heads > 0 ? num_kv_heads : 1);
+    return t > 0 ? t : 1;
+}
 
-size_t f32_decode_workspace_bytes(int max_len, int num_heads) {
-    return (size_t)f32_decode_chunks(max_len) * num_heads * (D + 2) * sizeof(float);
+static int f32_chunk_tokens(int len, int num_kv_heads) {
+    const int target = f32_target_chunks(num_kv_heads);
+    int ct = (len + target - 1) / target;
+    if (ct < kF32ChunkTokens) ct = kF32ChunkTokens;
+    return (ct + 31) & ~31;
+}
+
+int f32_decode_chunks(int len, int num_kv_heads) {
+    if (len <= 0) return 0;
+    const int ct = f32_chunk_tokens(len, num_kv_heads);
+    return (len + ct - 1) / ct;
+}
+
+size_t f32_decode_workspace_bytes(int max_len, int num_kv_heads, int num_heads) {
+    // the chunk count never exceeds the target, nor the count at the minimum chunk
+    const int by_len = (max_len + kF32ChunkTokens - 1) / kF32ChunkTokens;
+    const int target = f32_target_chunks(num_kv_heads);
+    const int chunks = max_len <= 0 ? 0 : (by_len < target ? by_len : target);
+    return (size_t)chunks * num_heads * (D + 2) * sizeof(float);
 }
 
 cudaError_t launch_decode_f32(const float* keys, const float* values, int num_kv_heads,
                               int num_heads, int len, const float* q, float q_mul, float* out,
                               void* ws, cudaStream_t st) {
     const int group = num_heads / num_kv_heads;
-    const int chunks = f32_decode_chunks(len);
+    const int chunks = f32_decode_chunks(len, num_kv_heads);
+    const int chunk_tokens = f32_chunk_tokens(len, num_kv_heads);
     if (chunks == 0) return cudaMemsetAsync(out, 0, (size_t)num_heads * D * sizeof(float), st);
     float* part_o = static_cast<float*>(ws);
     float* part_ml = part_o + (size_t)chunks * num_heads * D;
     dim3 grid(chunks, num_kv_heads);
+    cudaError_t e = cudaSuccess;
+    CUtensorMap mk, mv;
+    const int box = 32 / group;   // T of the kernel instance
+    if ((e = make_f32_row_map(&mk, keys, num_kv_heads, (uint64_t)len, box)) != cudaSuccess) return e;
+    if ((e = make_f32_row_map(&mv, values, num_kv_heads, (uint64_t)len, box)) != cudaSuccess) return e;
+#define EC_F32_CASE(GR)                                                                        \
+    case GR: {                                                                                 \
+        static unsigned long long done = 0;                                                    \
+        int dev = 0;                                                                           \
+        cudaGetDevice(&dev);                                                                   \
+        const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;                        \
+        if (!bit || !(done & bit)) {                                                           \
+            e = cudaFuncSetAttribute(decode_f32_kernel<GR>,                                    \
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,              \
+                                     F32Geo<GR>::SMEM);                                        \
+            if (e != cudaSuccess) return e;                                                    \
+            done |= bit;                                                                       \
+        }                                                                                      \
+        decode_f32_kernel<GR><<<grid, (kWarps + 1) * 32, F32Geo<GR>::SMEM, st>>>(             \
+            mk, mv, num_kv_heads, len, chunk_tokens, q, q_mul, part_o, part_ml);              \
+        break;                                                                                 \
+    }
     switch (group) {
-        case 1: decode_f32_kernel<1><<<grid, kWarps * 32, 0, st>>>(keys, values, num_kv_heads, len, kF32ChunkTokens, q, q_mul, part_o, part_ml); break;
-        case 2: decode_f32_kernel<2><<<grid, kWarps * 32, 0, st>>>(keys, values, num_kv_heads, len, kF32ChunkTokens, q, q_mul, part_o, part_ml); break;
-        case 4: decode_f32_kernel<4><<<grid, kWarps * 32, 0, st>>>(keys, values, num_kv_heads, len, kF32ChunkTokens, q, q_mul, part_o, part_ml); break;
-        case 8: decode_f32_kernel<8><<<grid, kWarps * 32, 0, st>>>(keys, values, num_kv_heads, len, kF32ChunkTokens, q, q_mul, part_o, part_ml); break;
+        EC_F32_CASE(1)
+        EC_F32_CASE(2)
+        EC_F32_CASE(4)
+        EC_F32_CASE(8)
         default: return cudaErrorInvalidValue;
     }
-    cudaError_t e = cudaGetLastError();
+#undef EC_F32_CASE
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_lse_combine(part_o, part_ml, chunks, 1, num_heads, out, st);
 }

@@ -195,7 +195,8 @@ int ec_kv_cache_create(const ec_model_config* config, int scale_mode, ec_kv_cach
     }
     if (!c.use_kv_quantization && c.num_layers > 0 &&
         f32_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim)) {
-        kc->ws_bytes = ec::f32_decode_workspace_bytes((int)c.max_seq_len, (int)c.num_heads);
+        kc->ws_bytes = ec::f32_decode_workspace_bytes((int)c.max_seq_len, (int)c.num_kv_heads,
+                                                       (int)c.num_heads);
         if (kc->ws_bytes) {
             cudaError_t e = cudaMalloc(&kc->ws, kc->ws_bytes);
             if (e != cudaSuccess) {

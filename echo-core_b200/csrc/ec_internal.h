@@ -82,6 +82,8 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
                           cudaStream_t st);
 // Tensor map over [total_slots][hkv * 128] int8 codes with a 128-byte x
 // box_rows-token box, 128-byte swizzle.
+cudaError_t make_f32_row_map(CUtensorMap* m, const float* base, int hkv, uint64_t rows,
+                             int box_rows);
 cudaError_t make_code_map(CUtensorMap* m, const int8_t* base, int hkv, uint64_t total_slots,
                           int box_rows);
 
@@ -122,11 +124,11 @@ cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st);
 
 // Decode attention over the fp32 cache mode (use_kv_quantization = false):
 // keys / values [len][num_kv_heads][128] fp32, q [num_heads][128] unscaled,
-// out [num_heads][128].  Split-K over chunks of kF32ChunkTokens tokens; the
-// workspace holds (m, l, O) per (chunk, head).
-constexpr int kF32ChunkTokens = 128;
-int f32_decode_chunks(int len);
-size_t f32_decode_workspace_bytes(int max_len, int num_heads);
+// out [num_heads][128].  Split-K over chunks of at least kF32ChunkTokens
+// tokens; the workspace holds (m, l, O) per (chunk, head).
+constexpr int kF32ChunkTokens = 512;   // minimum tokens per CTA
+int f32_decode_chunks(int len, int num_kv_heads);
+size_t f32_decode_workspace_bytes(int max_len, int num_kv_heads, int num_heads);
 cudaError_t launch_decode_f32(const float* keys, const float* values, int num_kv_heads,
                               int num_heads, int len, const float* q, float q_mul, float* out,
                               void* ws, cudaStream_t st);
