@@ -282,14 +282,15 @@ def run_gpu_arm(args, rank, world, local_rank):
     plan_chunks = eckv.lib().ec_decode_workspace_size(nseq, H, D, caches[0].max_seq_len)
     launches_per_layer = 2 + 1 + (1 if plan_chunks > 0 else 0)  # append+bump, decode, combine
 
-    def step(ev=None):
+    def step(ev=None, st=None):
+        st = st or stream
         for l, bc in enumerate(caches):
-            bc.append(kn[l], vn[l], 1, stream)
+            bc.append(kn[l], vn[l], 1, st)
             if ev is not None:
-                ev[l][0].record(stream)
-            bc.decode(q[l], out[l], H, scale, stream)
+                ev[l][0].record(st)
+            bc.decode(q[l], out[l], H, scale, st)
             if ev is not None:
-                ev[l][1].record(stream)
+                ev[l][1].record(st)
 
     def sync_all():
         torch.cuda.synchronize()
@@ -318,10 +319,38 @@ def run_gpu_arm(args, rank, world, local_rank):
     sync_all()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for k in range(args.steps):
-        step(dec_events[k])
-    t_end.record(stream)
+    graph = None
+    if args.graph:
+        # the step's launches captured once and replayed: the timed region then
+        # holds no host launch gaps (the kernels read the device length table,
+        # so every replay appends and attends at the next position).  The
+        # per-launch decode timing comes from an eager pass of the same steps.
+        for k in range(args.steps):
+            step(dec_events[k])
+        torch.cuda.synchronize()
+        for bc in caches:
+            bc.length.sub_(args.steps * new_tok)
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            step(st=side)              # uncaptured run on the capture stream
+        torch.cuda.synchronize()
+        for bc in caches:
+            bc.length.sub_(new_tok)
+        with torch.cuda.graph(graph, stream=side):
+            step(st=torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        sync_all()
+        t_start.record(stream)
+        for k in range(args.steps):
+            graph.replay()
+        t_end.record(stream)
+    else:
+        t_start.record(stream)
+        for k in range(args.steps):
+            step(dec_events[k])
+        t_end.record(stream)
     torch.cuda.synchronize()
     ms = t_start.elapsed_time(t_end)
     clk = clocks.stop() if clocks else None
@@ -398,6 +427,7 @@ def run_gpu_arm(args, rank, world, local_rank):
         "config": {"workload": cfg.name, "layers": layers, "seqs": nseq_total, "ctx": lens0[0],
                    "q_heads": H, "kv_heads": HKV, "head_dim": D,
                    "parallelism": f"sequence-shard x{world} (no collective)",
+                   "launch": "CUDA graph replay" if args.graph else "eager",
                    "l2": "inputs larger than L2 (KV working set per step >> 126 MB)"},
         "tok_s": round(nseq_total * args.steps / (ms_max * 1e-3), 1),
         "pct_of_hbm_peak": round(100 * gbs / (peak * world), 1),
@@ -653,12 +683,16 @@ def main():
                     help="override the sequence count (small profiling cases)")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
     ap.add_argument("--ctx", type=int, default=None, help="override every sequence's context")
+    ap.add_argument("--eager", action="store_true",
+                    help="decode configs: launch every kernel from the host each step instead of "
+                         "replaying the step as a captured CUDA graph")
     ap.add_argument("--cp-nccl", action="store_true",
                     help="config 4: exchange partials with an NCCL all-gather instead of peer stores")
     ap.add_argument("--kv-fp32", action="store_true",
                     help="decode over the fp32 cache mode (one sequence per rank)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    args.graph = not args.eager
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -538,24 +538,55 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, 1)
     }
 }
 
-// Merges the chunk partials of one (sequence, head); one thread per dim.
-__global__ void __launch_bounds__(D) combine_kernel(const DecodeArgs a) {
-    const int seq = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+// Merges the chunk partials of one (sequence, head).  4 warps per dim group:
+// the chunk weights 2^(m_c - M) are computed once into shared memory, then
+// each of kCombineSplit thread groups sums a quarter of the chunks for every
+// dim (independent loads, so a long chunk list is not one serial chain).
+constexpr int kCombineSplit = 4;
+__global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const DecodeArgs a) {
+    const int seq = blockIdx.x, h = blockIdx.y;
+    const int d = threadIdx.x % D, part = threadIdx.x / D;
     const int H = a.num_heads;
     int32_t off, cap, len;
     if (!load_entry(a, seq, off, cap, len)) return;  // flagged by decode_kernel
     const int nch = (len + a.chunk_tokens - 1) / a.chunk_tokens;
     const size_t base = (size_t)seq * a.max_chunks * H + h;
-    float M = -INFINITY;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, a.part_ml[(base + (size_t)c * H) * 2]);
-    float so = 0.0f, sl = 0.0f;
-    for (int c = 0; c < nch; ++c) {
+    __shared__ float s_f[256], s_l[256], s_red[D * kCombineSplit];
+    __shared__ float s_M;
+    // chunk maxima -> M (the plan keeps nch <= 256)
+    float m = -INFINITY;
+    for (int c = threadIdx.x; c < nch; c += D * kCombineSplit) m = fmaxf(m, a.part_ml[(base + (size_t)c * H) * 2]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float M = -INFINITY;
+        for (int w = 0; w < D * kCombineSplit / 32; ++w) M = fmaxf(M, s_red[w]);
+        s_M = M;
+    }
+    __syncthreads();
+    const float M = s_M;
+    for (int c = threadIdx.x; c < nch; c += D * kCombineSplit) {
         const size_t p = base + (size_t)c * H;
         const float mc = a.part_ml[p * 2];
         const float f = mc == -INFINITY ? 0.0f : exp2f(mc - M);
-        so += f * a.part_o[p * D + d];
-        sl += f * a.part_ml[p * 2 + 1];
+        s_f[c] = f;
+        s_l[c] = f * a.part_ml[p * 2 + 1];
     }
+    __syncthreads();
+    float so = 0.0f;
+#pragma unroll 4
+    for (int c = part; c < nch; c += kCombineSplit)
+        so += s_f[c] * a.part_o[(base + (size_t)c * H) * D + d];
+    s_red[part * D + d] = so;
+    __syncthreads();
+    if (part != 0) return;
+    so = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kCombineSplit; ++q) so += s_red[q * D + d];
+    float sl = 0.0f;
+    for (int c = 0; c < nch; ++c) sl += s_l[c];
     const size_t oi = ((size_t)seq * H + h) * D + d;
     if (a.mode == kOut) {
         a.out[oi] = nch ? __fdiv_rn(so, sl) : 0.0f;
@@ -675,8 +706,9 @@ DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms) {
         const int kk = (max_seq_len + chunk - 1) / chunk;
         const long long ctas = (long long)num_seqs * kk;
         const long long waves = (ctas + num_sms - 1) / num_sms;
-        // per-CTA time ~ its tokens plus a fixed prologue; a combine pass when split
-        const double cost = (double)waves * (chunk + 48) + (kk > 1 ? 64.0 : 0.0);
+        // per-CTA time ~ its tokens plus a fixed prologue; a combine pass when
+        // split, growing with the number of chunks it merges
+        const double cost = (double)waves * (chunk + 48) + (kk > 1 ? 64.0 + 0.5 * kk : 0.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = DecodePlan{chunk, kk};
@@ -705,7 +737,7 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
     EC_DEC(4, 4) EC_DEC(4, 2) EC_DEC(4, 1) EC_DEC(8, 4) EC_DEC(8, 2) EC_DEC(8, 1)
 #undef EC_DEC
     if (e != cudaSuccess || plan.max_chunks <= 1) return e;
-    combine_kernel<<<dim3(a.num_seqs, a.num_heads), D, 0, st>>>(a);
+    combine_kernel<<<dim3(a.num_seqs, a.num_heads), D * kCombineSplit, 0, st>>>(a);
     return cudaGetLastError();
 }
 
