@@ -117,8 +117,7 @@ __device__ __forceinline__ bool load_entry(const DecodeArgs& a, int s, int32_t& 
     len = a.seq_len ? a.seq_len[s] : a.host_length;
     // len is also bounded by the tokens the grid covers (max_chunks chunks),
     // which the host sized from its max_seq_len bound.
-    return off >= 0 && cap >= 0 && len >= 0 && len <= cap &&
-           (uint64_t)off + (uint64_t)cap <= a.total_slots &&
+    return page_entry_ok(a.pages, off, cap, len, a.total_slots) &&
            (int64_t)len <= (int64_t)a.max_chunks * a.chunk_tokens;
 }
 
@@ -150,8 +149,8 @@ __device__ __forceinline__ void consumer_barrier(int threads) {
 template <int HKV>
 __device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMap* tk,
                                            const CUtensorMap* tv, uint8_t* stages, uint64_t* full,
-                                           uint64_t* empty, int j, int n, int64_t slot0,
-                                           uint64_t pol, int lane) {
+                                           uint64_t* empty, int j, int n, int seq, int32_t off,
+                                           int t0, uint64_t pol, int lane) {
     using G = Geo<HKV>;
     const int s = j % G::kStages;
     bool ok = true;
@@ -159,7 +158,14 @@ __device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMa
     ok = __shfl_sync(kFull, ok, 0);
     if (!ok) return false;
     const int ntok = min(T, n - j * T);
-    const int64_t slot = slot0 + (int64_t)j * T;
+    // a tile never crosses a page (pages are multiples of 128 tokens); a bad
+    // page id is flagged and slot 0 read instead, so that the pipeline still
+    // completes and nothing outside the pool is touched
+    int64_t slot;
+    if (!page_slot(a.pages, seq, off, t0 + j * T, a.total_slots, slot)) {
+        if (lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
+        slot = 0;
+    }
     uint8_t* st = stages + s * G::STAGE;
     // the boxes always land whole (rows past the tensor are zero-filled)
     const uint32_t kvb = 2u * G::KV_TILE;
@@ -257,10 +263,9 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, 1)
         // ============================================================ producer
         // Keeps the ring full: refills a stage as soon as every consumer warp
         // has released it, independent of the consumers' own progress.
-        const int64_t slot0 = (int64_t)off + t0;
         const uint64_t pol = l2_policy_evict_first();
         for (int j = 0; j < ntiles; ++j) {
-            if (!issue_tile<HKV>(a, &tmap_k, &tmap_v, stages, full, empty, j, n, slot0, pol, lane)) {
+            if (!issue_tile<HKV>(a, &tmap_k, &tmap_v, stages, full, empty, j, n, seq, off, t0, pol, lane)) {
                 if (lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
                 break;
             }

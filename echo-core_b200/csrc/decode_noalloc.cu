@@ -108,6 +108,7 @@ int ec_decode_attention_noalloc(const ec_kv_batch* b, const float* q, float* out
     a.seq_len = b->seq_len;
     a.err = b->error_word;
     a.total_slots = b->total_slots;
+    a.pages = ec::page_map_of(b);
     a.q = q;
     a.out = out;
     a.q_mul = softmax_scale;

@@ -636,9 +636,18 @@ int ec_cp_exchange_combine(ec_cp_comm* c, const float* part_o, const float* part
 // ------------------------------------------------------------ batched cache
 static int check_batch(const ec_kv_batch* b, const char* who) {
     if (!b) return fail(EC_ERR_INVALID_ARGUMENT, "%s: batch is NULL", who);
-    if (!b->keys || !b->values || !b->key_scales || !b->val_scales || !b->seq_offset ||
-        !b->seq_capacity || !b->seq_len)
+    if (!b->keys || !b->values || !b->key_scales || !b->val_scales ||
+        (!b->seq_offset && !b->page_table) || !b->seq_capacity || !b->seq_len)
         return fail(EC_ERR_INVALID_ARGUMENT, "%s: null buffer in batch", who);
+    if (b->page_table) {
+        const uint32_t p = b->page_tokens;
+        if (p < 128 || (p & (p - 1)) || p > (1u << 24))
+            return fail(EC_ERR_INVALID_ARGUMENT, "%s: page_tokens must be a power of two >= 128", who);
+        if (b->max_pages == 0 || b->total_slots % p)
+            return fail(EC_ERR_INVALID_ARGUMENT, "%s: paged batch needs max_pages > 0 and total_slots a multiple of page_tokens", who);
+        if ((uint64_t)b->max_pages * p > 0x7fffffffull)
+            return fail(EC_ERR_INVALID_ARGUMENT, "%s: max_pages * page_tokens must fit int32", who);
+    }
     if (b->scale_mode != EC_SCALE_PER_HEAD && b->scale_mode != EC_SCALE_ROW)
         return fail(EC_ERR_INVALID_ARGUMENT, "%s: bad scale_mode", who);
     if (!aligned16(b->keys) || !aligned16(b->values) || !aligned16(b->key_scales) ||
@@ -675,6 +684,7 @@ int ec_kv_batch_append(const ec_kv_batch* b, const float* k, const float* v,
     a.seq_len = b->seq_len;
     a.err = b->error_word;
     a.total_slots = b->total_slots;
+    a.pages = ec::page_map_of(b);
     a.num_seqs = (int)b->num_seqs;
     a.n_new = (int)tokens_per_seq;
     cudaError_t e = ec::launch_append(a, (int)b->num_kv_heads, b->scale_mode == EC_SCALE_ROW,
@@ -717,6 +727,7 @@ int ec_kv_batch_append_rope(const ec_kv_batch* b, const float* k, const float* v
     a.seq_len = b->seq_len;
     a.err = b->error_word;
     a.total_slots = b->total_slots;
+    a.pages = ec::page_map_of(b);
     a.num_seqs = (int)b->num_seqs;
     a.n_new = (int)tokens_per_seq;
     a.k_norm_w = k_desc->norm_weight;
@@ -777,6 +788,7 @@ static int decode_common(const ec_kv_batch* b, const float* q, float* out, float
     a.seq_len = b->seq_len;
     a.err = b->error_word;
     a.total_slots = b->total_slots;
+    a.pages = ec::page_map_of(b);
     a.q = q;
     a.out = out;
     a.out_ml = out_ml;
@@ -823,6 +835,7 @@ int ec_prefill_attention(const ec_kv_batch* b, const float* q, float* out, uint3
     a.seq_len = b->seq_len;
     a.err = b->error_word;
     a.total_slots = b->total_slots;
+    a.pages = ec::page_map_of(b);
     a.q = q;
     a.out = out;
     a.num_seqs = (int)b->num_seqs;

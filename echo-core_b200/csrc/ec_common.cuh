@@ -9,6 +9,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "ec_internal.h"
 #include "ec_kv.h"
 
 namespace ec {
@@ -20,6 +21,34 @@ extern __device__ int32_t g_error_word;
 
 __device__ __forceinline__ void flag_error(int32_t* err, int32_t code) {
     atomicCAS(err ? err : &g_error_word, 0, code);
+}
+
+// Paged KV layout (PageMap in ec_internal.h).  With a page table, token t of
+// sequence s lives in slot table[s * max_pages + (t >> shift)] << shift |
+// (t & (page - 1)); without one, in slot seq_offset[s] + t (per-sequence
+// contiguous slabs).  False for a page id outside the pool or a t past the
+// table row: the caller flags the table and skips the access.
+__device__ __forceinline__ bool page_slot(const PageMap& pm, int s, int32_t off, int t,
+                                          uint64_t total_slots, int64_t& out) {
+    if (!pm.table) {
+        out = (int64_t)off + t;
+        return true;
+    }
+    const int pg = t >> pm.shift;
+    if (t < 0 || pg >= pm.max_pages) return false;
+    const int32_t id = pm.table[(size_t)s * pm.max_pages + pg];
+    const uint64_t base = (uint64_t)(int64_t)id << pm.shift;
+    if (id < 0 || base + ((uint64_t)1 << pm.shift) > total_slots) return false;
+    out = (int64_t)base + (t & ((1 << pm.shift) - 1));
+    return true;
+}
+
+// Bounds of a table entry: within its slab (contiguous) or its page row.
+__device__ __forceinline__ bool page_entry_ok(const PageMap& pm, int32_t off, int32_t cap,
+                                              int32_t len, uint64_t total_slots) {
+    if (cap < 0 || len < 0 || len > cap) return false;
+    if (pm.table) return (int64_t)cap <= ((int64_t)pm.max_pages << pm.shift);
+    return off >= 0 && (uint64_t)off + (uint64_t)cap <= total_slots;
 }
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

@@ -6,7 +6,27 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "ec_kv.h"
+
 namespace ec {
+
+// Optional paged layout of a batch (device page table; null: contiguous slabs
+// addressed by seq_offset).  Page size 1 << shift tokens, a multiple of 128.
+struct PageMap {
+    const int32_t* table;   // [num_seqs][max_pages] page ids into the slot pool
+    int shift;
+    int max_pages;
+};
+
+inline PageMap page_map_of(const ec_kv_batch* b) {
+    PageMap m{nullptr, 0, 0};
+    if (b->page_table) {
+        int sh = 0;
+        while ((1u << sh) < b->page_tokens) ++sh;
+        m = PageMap{b->page_table, sh, (int)b->max_pages};
+    }
+    return m;
+}
 
 struct AppendArgs {
     const float* k;
@@ -23,6 +43,7 @@ struct AppendArgs {
     uint64_t total_slots;
     int num_seqs;
     int n_new;
+    PageMap pages;
     // K pre-processing of echo-core-zig (src/inference/engine.zig): per-head
     // RMS norm with an fp16 weight (:521-532), then RoPE (:466-518).  Used by
     // the rope variant of the append kernel only.
@@ -54,6 +75,7 @@ struct DecodeArgs {
     int chunk_tokens;
     int row_scales;       // 1: EC_SCALE_ROW
     int mode;             // kOut or kPartial
+    PageMap pages;
 };
 
 enum { kOut = 0, kPartial = 1 };
@@ -101,6 +123,7 @@ struct PrefillArgs {
     float* out;               // same shape, fp32
     int num_seqs, num_heads, num_kv_heads, n_new, row_scales;
     float qk_mul;             // softmax scale * log2(e)
+    PageMap pages;
 };
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st);
 // Records `msg` as the calling thread's ec_last_error() text; returns status.

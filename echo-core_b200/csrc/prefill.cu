@@ -332,10 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int seq = idx / HKV;
     const int h = g + HKV * jh;
 
-    const int32_t off = a.seq_offset[seq], cap = a.seq_capacity[seq], len = a.seq_len[seq];
+    const int32_t off = a.seq_offset ? a.seq_offset[seq] : 0;
+    const int32_t cap = a.seq_capacity[seq], len = a.seq_len[seq];
     const int past = len - a.n_new;
-    if (!(off >= 0 && cap >= 0 && len <= cap && past >= 0 &&
-          (uint64_t)off + (uint64_t)cap <= a.total_slots)) {
+    if (!(page_entry_ok(a.pages, off, cap, len, a.total_slots) && past >= 0)) {
         if (threadIdx.x == 0 && qb == nqb - 1 && jh == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
         return;
     }
@@ -388,7 +388,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (j >= 2 && !wait_abortable(S.bar(B_KV_EMPTY + st), ((j >> 1) - 1) & 1, abort_flag))
                     break;
                 mbar_arrive_expect_tx(S.bar(B_KV_FULL + st), 2 * I8_TILE);
-                const int y = off + j * BN;
+                // a tile never crosses a page (pages are multiples of 128 tokens);
+                // a bad page id is flagged and slot 0 read instead
+                int64_t slot;
+                if (!page_slot(a.pages, seq, off, j * BN, a.total_slots, slot)) {
+                    flag_error(a.err, EC_DEVERR_BAD_TABLE);
+                    slot = 0;
+                }
+                const int y = (int)slot;
                 tma_load_2d(I8 + (2 * st) * I8_TILE, &tmap_k, g * D, y, S.bar(B_KV_FULL + st), pol);
                 tma_load_2d(I8 + (2 * st + 1) * I8_TILE, &tmap_v, g * D, y, S.bar(B_KV_FULL + st), pol);
                 issued = j + 1;
@@ -541,8 +548,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (raw value: the multiply waits until the next tile, when the load has
         // landed, so the in-order warp does not stall on it here)
         auto load_scale = [&](int j) -> float {
-            const int slot = off + j * BN + sc_col;
             if (j * BN + sc_col >= len) return 0.0f;
+            int64_t slot;
+            if (!page_slot(a.pages, seq, off, j * BN + sc_col, a.total_slots, slot)) return 0.0f;
             return a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g];
         };
 

@@ -75,6 +75,7 @@ struct TableView {
     const int32_t* length;
     int32_t host_offset, host_capacity, host_length;  // used when the pointers are null
     uint64_t total_slots;
+    PageMap pages;
 
     // Loads and checks one entry; false (and a flagged error) for a bad one.
     __device__ __forceinline__ bool load(int s, int32_t* err, int32_t& off, int32_t& cap,
@@ -82,9 +83,7 @@ struct TableView {
         off = offset ? offset[s] : host_offset;
         cap = capacity ? capacity[s] : host_capacity;
         len = length ? length[s] : host_length;
-        const bool ok = off >= 0 && cap >= 0 && len >= 0 && len <= cap &&
-                        (uint64_t)off + (uint64_t)cap <= total_slots;
-        return ok;
+        return page_entry_ok(pages, off, cap, len, total_slots);
     }
 };
 
@@ -97,7 +96,7 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
     const int i = warp - s * a.n_new;
     if (s >= a.num_seqs) return;
     TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, a.host_offset, a.host_capacity,
-                 a.host_length, a.total_slots};
+                 a.host_length, a.total_slots, a.pages};
     int32_t off, cap, len;
     if (!tv.load(s, a.err, off, cap, len)) {
         if (i == 0 && lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
@@ -107,7 +106,11 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
         if (i == 0 && lane == 0) flag_error(a.err, EC_DEVERR_OVERFLOW);
         return;
     }
-    const int64_t slot = (int64_t)off + len + i;
+    int64_t slot;
+    if (!page_slot(a.pages, s, off, len + i, a.total_slots, slot)) {
+        if (lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
+        return;
+    }
     const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
 
 #pragma unroll
@@ -156,7 +159,7 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
 __global__ void bump_lengths_kernel(AppendArgs a) {
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= a.num_seqs || a.seq_len == nullptr) return;
-    TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, 0, 0, 0, a.total_slots};
+    TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, 0, 0, 0, a.total_slots, a.pages};
     int32_t off, cap, len;
     if (!tv.load(s, a.err, off, cap, len)) return;  // already flagged by append_kernel
     if ((int64_t)len + a.n_new > cap) return;
@@ -220,7 +223,7 @@ __global__ void __launch_bounds__(256) append_rope_kernel(AppendArgs a) {
     const int i = warp - s * a.n_new;
     if (s >= a.num_seqs) return;
     TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, a.host_offset, a.host_capacity,
-                 a.host_length, a.total_slots};
+                 a.host_length, a.total_slots, a.pages};
     int32_t off, cap, len;
     if (!tv.load(s, a.err, off, cap, len)) {
         if (i == 0 && lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
@@ -231,7 +234,11 @@ __global__ void __launch_bounds__(256) append_rope_kernel(AppendArgs a) {
         return;
     }
     const int pos = len + i;                  // the token's position in its sequence
-    const int64_t slot = (int64_t)off + pos;
+    int64_t slot;
+    if (!page_slot(a.pages, s, off, pos, a.total_slots, slot)) {
+        if (lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
+        return;
+    }
     const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
     PairRot rot{};
     if (a.rope) rot = pair_rotation(pos, lane, a.inv_freq);

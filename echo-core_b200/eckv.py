@@ -100,7 +100,9 @@ class KVBatch(ctypes.Structure):
                 ("seq_len", ctypes.c_void_p), ("error_word", ctypes.c_void_p),
                 ("total_slots", ctypes.c_uint64), ("num_seqs", ctypes.c_uint32),
                 ("num_kv_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
-                ("scale_mode", ctypes.c_int32), ("max_seq_len", ctypes.c_uint32)]
+                ("scale_mode", ctypes.c_int32), ("max_seq_len", ctypes.c_uint32),
+                ("page_table", ctypes.c_void_p), ("page_tokens", ctypes.c_uint32),
+                ("max_pages", ctypes.c_uint32)]
 
 
 _lib = None
@@ -349,3 +351,76 @@ def lse_combine(part_o, part_ml, num_parts: int, num_seqs: int, num_heads: int, 
                 out, stream=None) -> None:
     check(lib().ec_lse_combine(_ptr(part_o), _ptr(part_ml), num_parts, num_seqs, num_heads,
                                head_dim, _ptr(out), _stream(stream)))
+
+
+# ----------------------------------------------------------- PagedBatchCache
+class PagedBatchCache(BatchCache):
+    """A batch whose sequences hold pages of ``page_tokens`` slots from one
+    pool (ec_kv_batch.page_table) instead of fixed slabs: a sequence grows by
+    ``reserve``-ing more pages, up to ``max_pages`` of them.  The host keeps
+    the free list and each sequence's page list; the device holds the page
+    table and the capacity / length table the kernels read."""
+
+    def __init__(self, num_seqs, *, num_pages, page_tokens=256, max_pages=None, num_kv_heads=4,
+                 head_dim=128, scale_mode=SCALE_PER_HEAD, device="cuda", shuffle_seed=None):
+        torch = _torch()
+        if page_tokens < 128 or page_tokens & (page_tokens - 1):
+            raise ValueError("page_tokens must be a power of two >= 128")
+        self.num_seqs = int(num_seqs)
+        self.hkv, self.d = num_kv_heads, head_dim
+        self.scale_mode = scale_mode
+        self.page_tokens = int(page_tokens)
+        self.max_pages = int(max_pages or num_pages)
+        self.total_slots = int(num_pages) * self.page_tokens
+        if self.total_slots >= 2 ** 31:
+            raise ValueError("the pool's slots must fit int32")
+        row = num_kv_heads * head_dim
+        ns = num_kv_heads if scale_mode == SCALE_PER_HEAD else 1
+        self.keys = torch.zeros((self.total_slots, row), dtype=torch.int8, device=device)
+        self.values = torch.zeros((self.total_slots, row), dtype=torch.int8, device=device)
+        self.key_scales = torch.zeros((self.total_slots * ns,), dtype=torch.float32, device=device)
+        self.val_scales = torch.zeros((self.total_slots * ns,), dtype=torch.float32, device=device)
+        self.page_table = torch.full((self.num_seqs, self.max_pages), -1, dtype=torch.int32,
+                                     device=device)
+        self.offset = None
+        self.capacity = torch.zeros(self.num_seqs, dtype=torch.int32, device=device)
+        self.length = torch.zeros(self.num_seqs, dtype=torch.int32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        order = np.arange(num_pages)
+        if shuffle_seed is not None:
+            np.random.default_rng(shuffle_seed).shuffle(order)
+        self.free = list(order[::-1])          # pop() hands out pages in `order`
+        self.pages = [[] for _ in range(self.num_seqs)]
+        self.max_seq_len = self.max_pages * self.page_tokens
+        self._ws = None
+
+    def slot(self, seq: int, t: int) -> int:
+        """Pool slot of token t of sequence seq."""
+        return int(self.pages[seq][t // self.page_tokens]) * self.page_tokens + t % self.page_tokens
+
+    def reserve(self, seq: int, tokens: int) -> None:
+        """Gives sequence seq pages for at least `tokens` tokens."""
+        torch = _torch()
+        need = -(-int(tokens) // self.page_tokens)
+        if need > self.max_pages:
+            raise ValueError(f"{tokens} tokens exceed max_pages * page_tokens")
+        grew = False
+        while len(self.pages[seq]) < need:
+            if not self.free:
+                raise MemoryError("page pool exhausted")
+            self.pages[seq].append(self.free.pop())
+            grew = True
+        if grew:
+            row = self.pages[seq] + [-1] * (self.max_pages - len(self.pages[seq]))
+            self.page_table[seq].copy_(torch.tensor(row, dtype=torch.int32))
+            self.capacity[seq] = len(self.pages[seq]) * self.page_tokens
+
+    def desc(self) -> KVBatch:
+        return KVBatch(keys=self.keys.data_ptr(), values=self.values.data_ptr(),
+                       key_scales=self.key_scales.data_ptr(), val_scales=self.val_scales.data_ptr(),
+                       seq_offset=None, seq_capacity=self.capacity.data_ptr(),
+                       seq_len=self.length.data_ptr(), error_word=self.err.data_ptr(),
+                       total_slots=self.total_slots, num_seqs=self.num_seqs,
+                       num_kv_heads=self.hkv, head_dim=self.d, scale_mode=self.scale_mode,
+                       max_seq_len=self.max_seq_len, page_table=self.page_table.data_ptr(),
+                       page_tokens=self.page_tokens, max_pages=self.max_pages)

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define EC_KV_ABI_VERSION 1
+#define EC_KV_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define EC_API __attribute__((visibility("default")))
@@ -214,6 +214,17 @@ typedef struct ec_kv_batch {
     uint32_t head_dim;
     int32_t scale_mode;          /* ec_scale_mode                                  */
     uint32_t max_seq_len;        /* host-side bound on every seq_len (sizes grids) */
+    /* Paged layout (optional; all zero = contiguous slabs).  With page_table
+     * set, seq_offset is ignored (it may be NULL) and token t of sequence s
+     * lives in slot page_table[s*max_pages + t/page_tokens]*page_tokens +
+     * t%page_tokens; seq_capacity[s] is the tokens its pages hold (at most
+     * max_pages*page_tokens).  Pages are taken from a pool of total_slots
+     * slots; a sequence grows past any initial size by receiving more pages
+     * (the reference's cache stops at max_seq_len, src/main.cpp:304).  A page
+     * id outside the pool is flagged EC_DEVERR_BAD_TABLE, never dereferenced. */
+    const int32_t* page_table;   /* [num_seqs][max_pages] device int32            */
+    uint32_t page_tokens;        /* power of two, multiple of 128                  */
+    uint32_t max_pages;          /* row stride of page_table                       */
 } ec_kv_batch;
 
 /* Batched KVCache::append: quantizes tokens_per_seq new tokens of every
