@@ -312,6 +312,9 @@ __device__ __forceinline__ float* out_row(const PrefillArgs& a, int r, bool& liv
     return a.out + (((size_t)seq * a.n_new + (live ? qpos : 0)) * H + h) * D;
 }
 
+// PAGED: slots through the batch's page table.  Compiled apart so that the
+// contiguous kernel carries none of the translation in its softmax loop.
+template <bool PAGED>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmap_k,
                    const __grid_constant__ CUtensorMap tmap_v, const PrefillArgs a) {
@@ -332,10 +335,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int seq = idx / HKV;
     const int h = g + HKV * jh;
 
-    const int32_t off = a.seq_offset ? a.seq_offset[seq] : 0;
+    const int32_t off = PAGED ? 0 : a.seq_offset[seq];
     const int32_t cap = a.seq_capacity[seq], len = a.seq_len[seq];
     const int past = len - a.n_new;
-    if (!(page_entry_ok(a.pages, off, cap, len, a.total_slots) && past >= 0)) {
+    const PageMap pm = PAGED ? a.pages : PageMap{nullptr, 0, 0};
+    if (!(page_entry_ok(pm, off, cap, len, a.total_slots) && past >= 0)) {
         if (threadIdx.x == 0 && qb == nqb - 1 && jh == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
         return;
     }
@@ -390,8 +394,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(S.bar(B_KV_FULL + st), 2 * I8_TILE);
                 // a tile never crosses a page (pages are multiples of 128 tokens);
                 // a bad page id is flagged and slot 0 read instead
-                int64_t slot;
-                if (!page_slot(a.pages, seq, off, j * BN, a.total_slots, slot)) {
+                int64_t slot = off + j * BN;
+                if (PAGED && !page_slot(pm, seq, off, j * BN, a.total_slots, slot)) {
                     flag_error(a.err, EC_DEVERR_BAD_TABLE);
                     slot = 0;
                 }
@@ -548,9 +552,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (raw value: the multiply waits until the next tile, when the load has
         // landed, so the in-order warp does not stall on it here)
         auto load_scale = [&](int j) -> float {
+            if (PAGED) {
+                if (j * BN + sc_col >= len) return 0.0f;
+                int64_t slot;
+                if (!page_slot(pm, seq, off, j * BN + sc_col, a.total_slots, slot)) return 0.0f;
+                return a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g];
+            }
+            const int slot = off + j * BN + sc_col;
             if (j * BN + sc_col >= len) return 0.0f;
-            int64_t slot;
-            if (!page_slot(a.pages, seq, off, j * BN + sc_col, a.total_slots, slot)) return 0.0f;
             return a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g];
         };
 
@@ -791,7 +800,9 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
     if (!bit || !(attr_done & bit)) {
-        e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        e = cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
         if (e != cudaSuccess) return e;
         attr_done |= bit;
     }
@@ -802,7 +813,10 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st) {
     const long long blocks = (long long)a.num_seqs * a.num_heads * nqb;
     if (blocks == 0) return cudaSuccess;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    prefill_kernel<<<(unsigned)blocks, kThreads, SMEM, st>>>(mk, mv, a);
+    if (a.pages.table)
+        prefill_kernel<true><<<(unsigned)blocks, kThreads, SMEM, st>>>(mk, mv, a);
+    else
+        prefill_kernel<false><<<(unsigned)blocks, kThreads, SMEM, st>>>(mk, mv, a);
     return cudaGetLastError();
 }
 
