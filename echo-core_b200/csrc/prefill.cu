@@ -12,11 +12,11 @@
 // reads KV head h % num_kv_heads, src/inference.cpp:335).  Warp roles:
 //   producer  (warp 12)   2-D TMA of the int8 K and V codes of 128-token
 //                         tiles (128-byte swizzle, no multicast), 2 stages;
-//   converter (warps 8-11) int8 -> bf16 K (K-major) and int8 -> f16 V
+//   converter (warps 8-11) int8 -> f16 K (K-major) and int8 -> f16 V
 //                         (MN-major), both exact, into 128B-swizzled UMMA
 //                         operand layouts (K one tile, V two tiles);
-//   MMA       (warp 13)   one thread issues tcgen05.mma: S = Q K^T (bf16 x
-//                         bf16 -> fp32) into one of three S/P buffers in TMEM,
+//   MMA       (warp 13)   one thread issues tcgen05.mma: S = Q K^T (f16 x
+//                         f16 -> fp32) into one of three S/P buffers in TMEM,
 //                         one tile ahead of the softmax, then O += P'hi V +
 //                         P'lo V with P' read from TMEM (f16 x f16 -> fp32,
 //                         accumulated in TMEM);
@@ -28,8 +28,10 @@
 //                         softmax in base 2 with lazy rescaling of O, and write
 //                         p' = p * v_scale (the fused v-scale) as an f16 hi/lo
 //                         pair over the S columns they have read.
-// Q is cast to bf16 on load (the queries are bf16-cast); the softmax scale and
-// log2(e) multiply the fp32 scores.  K and V codes are exact in bf16 / f16; p'
+// Q is cast to bf16 on load (the queries are bf16-cast), then held as f16
+// under one power-of-two scale per CTA (exact for the bf16 values); the
+// softmax scale, log2(e) and the inverse power of two multiply the fp32
+// scores.  K and V codes are exact in f16; p'
 // enters the PV product as an f16 pair hi + lo (two MMAs), about 22 bits, so
 // the only rounding of consequence is Q's bf16 cast (part of the contract).
 // Every wait is bounded; a timeout raises a CTA-wide abort flag so that every
@@ -64,8 +66,8 @@ constexpr int kMmaWarp = 13;
 constexpr int kThreads = 14 * 32;
 constexpr int kSoftmaxThreads = 256;
 constexpr int ATOM = 128 * 128;            // one [128 rows][128 B] swizzled block
-constexpr int OFF_Q = 0;                   // bf16 Q   : 2 K-blocks (dims 0-63, 64-127)
-constexpr int OFF_K = OFF_Q + 2 * ATOM;    // bf16 K   : 2 K-blocks (one tile)
+constexpr int OFF_Q = 0;                   // f16 Q    : 2 K-blocks (dims 0-63, 64-127)
+constexpr int OFF_K = OFF_Q + 2 * ATOM;    // f16 K    : 2 K-blocks (one tile)
 constexpr int OFF_V = OFF_K + 2 * ATOM;    // f16  V   : [2 buffers][2 dim halves], MN-major
 constexpr int I8_TILE = BN * 128;          // 16 KB of int8 codes
 constexpr int OFF_I8 = OFF_V + 4 * ATOM;   // [2 stages][K, V]
