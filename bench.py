@@ -11,8 +11,10 @@ sequence (quantize-on-append) and then runs split-K decode attention.  The
     python bench.py --impl reference     # the reference's CPU code on the host
 
 Config 4 (one 1,048,576-token sequence split along context) runs a partial
-(m, l, O) per rank and merges them with an NCCL all-gather plus the
-log-sum-exp combine kernel.
+(m, l, O) per rank; at N > 1 the ranks exchange and merge the partials in one
+kernel over NVLink peer memory (``--cp-nccl``: an NCCL all-gather plus the
+log-sum-exp combine kernel instead).  Config 5 is the chunked prefill,
+``--kv-fp32`` the fp32-cache decode.
 
 Prints one JSON line on rank 0.
 """
@@ -533,15 +535,16 @@ def run_prefill_arm(args, rank, world, local_rank):
 
     def step(record=False):
         bc.length.copy_(base_len)
+        if record:
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record(stream)
         bc.append(kn, vn, n_new, stream)
         if record:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+            e[1].record(stream)
         bc.prefill(q, out, n_new, H, scale, stream)
         if record:
-            e1.record(stream)
-            ev.append((e0, e1))
+            e[2].record(stream)
+            ev.append(e)
 
     for _ in range(args.warmup):
         step()
@@ -562,7 +565,8 @@ def run_prefill_arm(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
     clk = clocks.stop() if clocks else None
-    pre_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    pre_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in ev]))
+    app_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
     pairs = n_new * past + n_new * (n_new + 1) // 2
     flops_rank = 4.0 * D * pairs * H * nseq
     t = torch.tensor([ms, flops_rank], dtype=torch.float64, device=dev)
@@ -594,7 +598,11 @@ def run_prefill_arm(args, rank, world, local_rank):
                      "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_kind": "measured sustained" if pk else "fallback",
                      "note": "algorithmic FLOPs (QK^T and PV, causal); PV runs as two f16 MMAs (p' hi/lo)"},
-        "append_gbs": round(append_bytes / ((ms_max / args.steps - pre_ms) * 1e-3) / 1e9, 1),
+        "append": {"kernel": "append_kernel+bump_lengths_kernel", "ms": round(app_ms, 4),
+                   "gbs": round(append_bytes / (app_ms * 1e-3) / 1e9, 1),
+                   "frac": round(append_bytes / (app_ms * 1e-3) / 1e9 / peaks()[0], 4),
+                   "bytes": append_bytes, "bound": "hbm",
+                   "note": "fp32 K/V rows read + int8 codes and scales written, per rank"},
         "gpu_launches": 3 * args.steps, "clocks": clk}), flush=True)
 
 

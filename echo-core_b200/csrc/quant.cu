@@ -6,6 +6,8 @@
 //   scale = amax / 127.0f, or 1.0f when amax == 0       (:63)  -- IEEE division
 //   body  (first n - n%8 elements):  q = sat8(RNE(x * (1.0f/scale)))   (:70-88)
 //   tail  (last n%8 elements):       q = clamp127(round_half_away(x / scale)) (:91-96)
+// with x86's conversion of a NaN or out-of-range value to INT32_MIN, which a
+// subnormal scale (reciprocal inf) reaches for finite input.
 // Every operation uses an explicitly IEEE-rounded intrinsic; this file must
 // not be compiled with fast-math.
 #include <cstdint>
@@ -28,14 +30,20 @@ __device__ __forceinline__ float scale_of(float amax) {
     return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
 }
 
+// x86 CVTPS2DQ semantics: a value that is NaN or outside the int32 range
+// converts to INT32_MIN ("integer indefinite"), which the saturating packs
+// then turn into -128 (body) or the clamp into -127 (tail).  Finite input
+// reaches this only through a subnormal scale, whose reciprocal overflows.
 __device__ __forceinline__ int32_t q_body(float x, float inv) {
-    int32_t v = __float2int_rn(__fmul_rn(x, inv));
-    return max(-128, min(127, v));
+    const float v = __fmul_rn(x, inv);
+    if (!(fabsf(v) < 2147483648.0f)) return -128;
+    return max(-128, min(127, __float2int_rn(v)));
 }
 
 __device__ __forceinline__ int32_t q_tail(float x, float scale) {
-    int32_t v = __float2int_rz(roundf(__fdiv_rn(x, scale)));
-    return max(-127, min(127, v));
+    const float v = roundf(__fdiv_rn(x, scale));
+    if (!(fabsf(v) < 2147483648.0f)) return -127;
+    return max(-127, min(127, (int32_t)v));
 }
 
 // ---------------------------------------------------------------- generic
@@ -87,6 +95,91 @@ struct TableView {
     }
 };
 
+// Quantizes one token's K and V rows held as xs[t][g] (lane l holds float4 l
+// of head g's 128 floats) and stores codes and scales at `slot`.
+//
+// The 2 x HKV absmaxes (2 for ROW) are reduced with a butterfly
+// reduce-scatter: after it, lane l holds the full absmax of value
+// k = l >> (5 - log2(NV)), replicated over 32 / NV lanes.  That lane alone
+// computes k's scale and reciprocal (two IEEE divisions per lane instead of
+// one per value per lane); shuffles broadcast the reciprocals back.
+//
+// Codes: v = RN(x * inv) is below 127.5 in magnitude whenever the scale is a
+// normal float (|x| <= amax, and scale and inv each carry one rounding of
+// 2^-24), so sat8(RNE(v)) is the low byte of RN(v + 1.5 * 2^23): adding the
+// even integer 1.5 * 2^23 rounds v to an integer with ties to even, and the
+// sum's mantissa is 2^22 + RNE(v).  A subnormal scale (absmax below about
+// 1.5e-36) takes the exact path, uniformly across the warp.
+template <int HKV, bool ROW>
+__device__ __forceinline__ void quantize_store(const float4 (&xs)[2][HKV], const AppendArgs& a,
+                                               int64_t slot, int lane) {
+    constexpr int D = 128;
+    constexpr int NV = ROW ? 2 : 2 * HKV;           // values to reduce: (t, g) or t
+    constexpr int LB = NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : 4;   // log2(NV)
+    constexpr int SH = 5 - LB;                      // lane >> SH = the value a lane ends with
+    static_assert(NV == (1 << LB) && NV <= 16, "HKV must be 1, 2, 4 or 8");
+    float v[NV];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+#pragma unroll
+        for (int g = 0; g < HKV; ++g) {
+            const float4 x = xs[t][g];
+            const float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+            if (ROW) v[t] = g == 0 ? m : fmaxf(v[t], m);
+            else v[t * HKV + g] = m;
+        }
+    }
+    // reduce-scatter: each step halves the values a lane keeps
+#pragma unroll
+    for (int step = 0, half = NV / 2; half >= 1; ++step, half >>= 1) {
+        const int o = 16 >> step;
+        const bool upper = lane & o;
+#pragma unroll
+        for (int j = 0; j < half; ++j) {
+            const float send = upper ? v[j] : v[j + half];
+            const float keep = upper ? v[j + half] : v[j];
+            v[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, o));
+        }
+    }
+    // all-reduce across the 32 / NV lanes that share a value
+#pragma unroll
+    for (int o = (16 >> LB); o > 0; o >>= 1) v[0] = fmaxf(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
+    const float scale = scale_of(v[0]);
+    const float inv_own = __fdiv_rn(1.0f, scale);
+    const uint32_t sub = __ballot_sync(0xffffffffu, scale < 1.17549435e-38f);
+    if ((lane & ((1 << SH) - 1)) == 0) {
+        const int k = lane >> SH;
+        const int t = k / (NV / 2), g = k % (NV / 2);
+        float* sc = t == 0 ? a.key_scales : a.val_scales;
+        if (ROW) sc[slot] = scale;
+        else sc[(size_t)slot * HKV + g] = scale;
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        int8_t* dst = (t == 0 ? a.keys : a.values) + (size_t)slot * (HKV * D);
+#pragma unroll
+        for (int g = 0; g < HKV; ++g) {
+            const int src = (ROW ? t : t * HKV + g) << SH;
+            const float inv = __shfl_sync(0xffffffffu, inv_own, src);
+            const float4 x = xs[t][g];
+            uint32_t word;
+            if (!((sub >> src) & 1u)) {
+                constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
+                const uint32_t b0 = __float_as_uint(__fadd_rn(__fmul_rn(x.x, inv), kRound));
+                const uint32_t b1 = __float_as_uint(__fadd_rn(__fmul_rn(x.y, inv), kRound));
+                const uint32_t b2 = __float_as_uint(__fadd_rn(__fmul_rn(x.z, inv), kRound));
+                const uint32_t b3 = __float_as_uint(__fadd_rn(__fmul_rn(x.w, inv), kRound));
+                word = __byte_perm(__byte_perm(b0, b1, 0x0040u), __byte_perm(b2, b3, 0x0040u), 0x5410u);
+            } else {
+                word = (uint32_t)(q_body(x.x, inv) & 0xff) | ((uint32_t)(q_body(x.y, inv) & 0xff) << 8) |
+                       ((uint32_t)(q_body(x.z, inv) & 0xff) << 16) |
+                       ((uint32_t)(q_body(x.w, inv) & 0xff) << 24);
+            }
+            reinterpret_cast<uint32_t*>(dst + g * D)[lane] = word;
+        }
+    }
+}
+
 template <int HKV, bool ROW>
 __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
     constexpr int D = 128;
@@ -95,6 +188,17 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
     const int s = warp / a.n_new;
     const int i = warp - s * a.n_new;
     if (s >= a.num_seqs) return;
+    // The K and V rows do not depend on the table: all 2 x HKV float4 loads of
+    // the lane are issued first, so that they and the table load are in
+    // flight together.
+    const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
+    float4 xs[2][HKV];
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int g = 0; g < HKV; ++g)
+            xs[t][g] = __ldcs(reinterpret_cast<const float4*>((t == 0 ? a.k : a.v) + src_row) +
+                              g * 32 + lane);
     TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, a.host_offset, a.host_capacity,
                  a.host_length, a.total_slots, a.pages};
     int32_t off, cap, len;
@@ -111,49 +215,8 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
         if (lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
         return;
     }
-    const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
 
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const float* src = (t == 0 ? a.k : a.v) + src_row;
-        int8_t* dst = (t == 0 ? a.keys : a.values) + (size_t)slot * (HKV * D);
-        float* sc = t == 0 ? a.key_scales : a.val_scales;
-        float4 x[HKV];
-#pragma unroll
-        for (int g = 0; g < HKV; ++g) x[g] = __ldcs(reinterpret_cast<const float4*>(src) + g * 32 + lane);
-        float amax[HKV];
-#pragma unroll
-        for (int g = 0; g < HKV; ++g)
-            amax[g] = fmaxf(fmaxf(fabsf(x[g].x), fabsf(x[g].y)), fmaxf(fabsf(x[g].z), fabsf(x[g].w)));
-        if (ROW) {
-            float m = amax[0];
-#pragma unroll
-            for (int g = 1; g < HKV; ++g) m = fmaxf(m, amax[g]);
-            m = warp_max(m);
-#pragma unroll
-            for (int g = 0; g < HKV; ++g) amax[g] = m;
-        } else {
-#pragma unroll
-            for (int g = 0; g < HKV; ++g) amax[g] = warp_max(amax[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < HKV; ++g) {
-            const float scale = scale_of(amax[g]);
-            const float inv = __fdiv_rn(1.0f, scale);
-            const uint32_t b0 = (uint32_t)(q_body(x[g].x, inv) & 0xff);
-            const uint32_t b1 = (uint32_t)(q_body(x[g].y, inv) & 0xff);
-            const uint32_t b2 = (uint32_t)(q_body(x[g].z, inv) & 0xff);
-            const uint32_t b3 = (uint32_t)(q_body(x[g].w, inv) & 0xff);
-            reinterpret_cast<uint32_t*>(dst + g * D)[lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-            if (lane == 0) {
-                if (ROW) {
-                    if (g == 0) sc[slot] = scale;
-                } else {
-                    sc[(size_t)slot * HKV + g] = scale;
-                }
-            }
-        }
-    }
+    quantize_store<HKV, ROW>(xs, a, slot, lane);
 }
 
 __global__ void bump_lengths_kernel(AppendArgs a) {
@@ -242,53 +305,19 @@ __global__ void __launch_bounds__(256) append_rope_kernel(AppendArgs a) {
     const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
     PairRot rot{};
     if (a.rope) rot = pair_rotation(pos, lane, a.inv_freq);
+    float4 xs[2][HKV];
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const float* src = (t == 0 ? a.k : a.v) + src_row;
-        int8_t* dst = (t == 0 ? a.keys : a.values) + (size_t)slot * (HKV * D);
-        float* sc = t == 0 ? a.key_scales : a.val_scales;
-        float4 x[HKV];
+    for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int g = 0; g < HKV; ++g) {
-            x[g] = __ldcs(reinterpret_cast<const float4*>(src) + g * 32 + lane);
+            float4 x = __ldcs(reinterpret_cast<const float4*>((t == 0 ? a.k : a.v) + src_row) + g * 32 + lane);
             if (t == 0) {
-                if (a.k_norm_w) x[g] = head_rms_norm(x[g], a.k_norm_w, lane);
-                if (a.rope) x[g] = rotate(x[g], rot);
+                if (a.k_norm_w) x = head_rms_norm(x, a.k_norm_w, lane);
+                if (a.rope) x = rotate(x, rot);
             }
+            xs[t][g] = x;
         }
-        float amax[HKV];
-#pragma unroll
-        for (int g = 0; g < HKV; ++g)
-            amax[g] = fmaxf(fmaxf(fabsf(x[g].x), fabsf(x[g].y)), fmaxf(fabsf(x[g].z), fabsf(x[g].w)));
-        if (ROW) {
-            float m = amax[0];
-#pragma unroll
-            for (int g = 1; g < HKV; ++g) m = fmaxf(m, amax[g]);
-            m = warp_max(m);
-#pragma unroll
-            for (int g = 0; g < HKV; ++g) amax[g] = m;
-        } else {
-#pragma unroll
-            for (int g = 0; g < HKV; ++g) amax[g] = warp_max(amax[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < HKV; ++g) {
-            const float scale = scale_of(amax[g]);
-            const float inv = __fdiv_rn(1.0f, scale);
-            const uint32_t b0 = (uint32_t)(q_body(x[g].x, inv) & 0xff);
-            const uint32_t b1 = (uint32_t)(q_body(x[g].y, inv) & 0xff);
-            const uint32_t b2 = (uint32_t)(q_body(x[g].z, inv) & 0xff);
-            const uint32_t b3 = (uint32_t)(q_body(x[g].w, inv) & 0xff);
-            reinterpret_cast<uint32_t*>(dst + g * D)[lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-            if (lane == 0) {
-                if (ROW) {
-                    if (g == 0) sc[slot] = scale;
-                } else {
-                    sc[(size_t)slot * HKV + g] = scale;
-                }
-            }
-        }
-    }
+    quantize_store<HKV, ROW>(xs, a, slot, lane);
 }
 
 struct RopeRowsArgs {

@@ -49,6 +49,53 @@ def test_quantize_rows_random(cuda, rows, n):
     assert np.array_equal(bits(s.cpu().numpy()), bits(ws))
 
 
+@pytest.mark.parametrize("n", [7, 128, 133, 512])
+def test_quantize_rows_extreme_magnitudes(cuda, n):
+    """Subnormal absmaxes make the scale subnormal and its reciprocal inf:
+    the codes then follow x86's out-of-range conversion (-128 body, -127 tail),
+    as the reference computes them."""
+    import torch
+    import eckv
+    from test_oracle import extreme_rows
+    x = extreme_rows(np.random.default_rng(n + 5), n)
+    rows = x.shape[0]
+    wq, ws = O.quantize_per_token_symmetric(x, rows, n)
+    q = torch.empty((rows, n), dtype=torch.int8, device="cuda")
+    s = torch.empty(rows, dtype=torch.float32, device="cuda")
+    eckv.quantize_per_token_symmetric(_dev(torch, x), q, s, rows, n)
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy().reshape(-1), wq)
+    assert np.array_equal(bits(s.cpu().numpy()), bits(ws))
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("hkv", [1, 2, 4, 8])
+def test_batch_append_extreme_magnitudes(cuda, mode, hkv):
+    """Append of tokens whose heads span zero, subnormal and huge absmaxes
+    (each head of each token drawn at its own magnitude), bit-exact."""
+    import torch
+    import eckv
+    from test_oracle import EXTREME_ROW_SCALES
+    rng = np.random.default_rng(100 + 10 * hkv + mode)
+    n_tok = 24
+    mags = rng.choice(EXTREME_ROW_SCALES, (2, n_tok, hkv, 1))
+    kv = (rng.standard_normal((2, n_tok, hkv, 128)) * mags).astype(np.float32)
+    kv[:, 0] = 0.0
+    k = kv[0].reshape(1, n_tok, hkv * 128)
+    v = kv[1].reshape(1, n_tok, hkv * 128)
+    bc = eckv.BatchCache([n_tok], num_kv_heads=hkv, head_dim=128, scale_mode=mode)
+    bc.append(_dev(torch, k), _dev(torch, v), n_tok)
+    torch.cuda.synchronize()
+    assert bc.device_error() == 0
+    off = bc.offsets_host[0]
+    for t, (src, codes, scales) in enumerate(((k, bc.keys, bc.key_scales), (v, bc.values, bc.val_scales))):
+        wq, ws = O.quantize_kv(src[0], hkv, 128, mode)
+        ns = hkv if mode == 0 else 1
+        assert np.array_equal(codes.cpu().numpy()[off:off + n_tok], wq), ("kv"[t], hkv, mode)
+        assert np.array_equal(bits(scales.cpu().numpy()[off * ns:(off + n_tok) * ns]),
+                              bits(ws.reshape(-1)))
+
+
 def _batch_case(torch, eckv, mode, hkv, caps, lens, n_new, seed):
     rng = np.random.default_rng(seed)
     bc = eckv.BatchCache(caps, num_kv_heads=hkv, head_dim=128, scale_mode=mode)

@@ -134,6 +134,32 @@ def test_quantize_matches_reference_build(n):
     assert np.array_equal(a[0], b[0]) and np.array_equal(bits(a[1]), bits(b[1]))
 
 
+# row magnitudes from an all-zero row through subnormal absmaxes (whose scale
+# is subnormal and whose reciprocal overflows to inf) to near FLT_MAX / 127
+EXTREME_ROW_SCALES = [0.0, 1e-45, 1e-44, 1e-41, 1e-39, 1e-37, 2e-37, 5e-37, 1.5e-36, 3e-36, 1e-30, 1.0,
+                      1e30, 1e37]
+
+
+def extreme_rows(rng, n, reps=2):
+    rows = []
+    for s in EXTREME_ROW_SCALES:
+        for _ in range(reps):
+            rows.append(rng.standard_normal(n) * s)
+    x = np.array(rows, dtype=np.float64).astype(np.float32)
+    x[1, : n // 2] = 0.0
+    return x
+
+
+@needs_ref
+@pytest.mark.parametrize("n", [7, 128, 133, 512])
+def test_quantize_extreme_magnitudes_match_reference_build(n):
+    x = extreme_rows(np.random.default_rng(n + 5), n)
+    rows = x.shape[0]
+    a = O.quantize_per_token_symmetric(x, rows, n)
+    b = O.ref_quantize_per_token_symmetric(x, rows, n)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(bits(a[1]), bits(b[1]))
+
+
 @needs_ref
 @pytest.mark.parametrize("dim", [4, 16, 33, 128])
 def test_fused_dot_matches_reference_build(dim):
