@@ -267,6 +267,20 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// pv - float(h) per half, each a mixed-precision fma (f16 x f16 + f32 -> f32,
+// one rounding): h * -1 + pv.  pv - h is exact in f32 when h = f16(pv).
+__device__ __forceinline__ float2 minus_f16x2_from_f32x2(__half2 h, float2 pv) {
+    float2 d;
+    asm("{\n\t.reg .f16 a0, a1, m;\n\t"
+        "mov.b32 {a0, a1}, %2;\n\t"
+        "mov.b16 m, 0xBC00;\n\t"
+        "fma.rn.f32.f16 %0, a0, m, %3;\n\t"
+        "fma.rn.f32.f16 %1, a1, m, %4;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "r"(*reinterpret_cast<const uint32_t*>(&h)), "f"(pv.x), "f"(pv.y));
+    return d;
+}
+
 // max of three (one sm_100 instruction)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
@@ -583,9 +597,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
 
         float sc_next = load_scale(0);
-        float m_run[4], l_run[4];                  // l_run: this thread's columns only
+        float m_run[4];
+        float2 l_run[4];                           // this thread's even / odd columns
 #pragma unroll
-        for (int k = 0; k < 4; ++k) { m_run[k] = -INFINITY; l_run[k] = 0.0f; }
+        for (int k = 0; k < 4; ++k) { m_run[k] = -INFINITY; l_run[k] = make_float2(0.0f, 0.0f); }
         bool bad = false;                          // a bounded wait of this warp gave up
 
         int j = 0;
@@ -598,13 +613,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // tile j's scales are visible to all, and all agree whether to go on
             if (bar_any(1, kSoftmaxThreads, bad)) break;
             tc_fence_after();
-            float ks[16], vs[16];                  // scales of this thread's columns
+            float2 ks[8], vs[8];                   // scales of this thread's column pairs
 #pragma unroll
             for (int n = 0; n < 8; ++n) {
-                const float2 k2 = *reinterpret_cast<const float2*>(sck + c0 + 8 * n + 2 * qq);
-                const float2 v2 = *reinterpret_cast<const float2*>(sck + BN + c0 + 8 * n + 2 * qq);
-                ks[2 * n] = k2.x; ks[2 * n + 1] = k2.y;
-                vs[2 * n] = v2.x; vs[2 * n + 1] = v2.y;
+                ks[n] = *reinterpret_cast<const float2*>(sck + c0 + 8 * n + 2 * qq);
+                vs[n] = *reinterpret_cast<const float2*>(sck + BN + c0 + 8 * n + 2 * qq);
             }
             const uint32_t s_col = tmem + sb * BN + c0;
             const int kv0 = j * BN + c0 + 2 * qq;  // kv slot of column c0 + 2q
@@ -621,8 +634,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
                 for (int n = 0; n < 8; ++n) {
-                    float a0 = v[4 * n] * ks[2 * n], a1 = v[4 * n + 1] * ks[2 * n + 1];
-                    float b0 = v[4 * n + 2] * ks[2 * n], b1 = v[4 * n + 3] * ks[2 * n + 1];
+                    // packed f32x2 multiplies: one instruction per column pair
+                    const float2 pa = __fmul2_rn(make_float2(v[4 * n], v[4 * n + 1]), ks[n]);
+                    const float2 pb = __fmul2_rn(make_float2(v[4 * n + 2], v[4 * n + 3]), ks[n]);
+                    float a0 = pa.x, a1 = pa.y, b0 = pb.x, b1 = pb.y;
                     if (masked_tile) {
                         const int c = kv0 + 8 * n;
                         if (c > rlim[2 * blk]) a0 = -INFINITY;
@@ -663,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     m_run[k] = t;
                     any_corr = true;
                 }
-                l_run[k] *= corr[k];
+                l_run[k] = __fmul2_rn(l_run[k], make_float2(corr[k], corr[k]));
                 neg_m[k] = m_run[k] == -INFINITY ? 0.0f : -m_run[k];
             }
 
@@ -712,19 +727,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int rr = 0; rr < 2; ++rr) {      // row g or g + 8
                             const int k = 2 * blk + rr;
-                            float e0 = fmaf(v[4 * h4 + 2 * rr], ks[2 * n], neg_m[k]);
-                            float e1 = fmaf(v[4 * h4 + 2 * rr + 1], ks[2 * n + 1], neg_m[k]);
+                            // packed f32x2 arithmetic on the column pair
+                            const float2 e = __ffma2_rn(
+                                make_float2(v[4 * h4 + 2 * rr], v[4 * h4 + 2 * rr + 1]), ks[n],
+                                make_float2(neg_m[k], neg_m[k]));
+                            float e0 = e.x, e1 = e.y;
                             if (masked_tile) {
                                 const int c = kv0 + 8 * n;
                                 if (c > rlim[k]) e0 = -INFINITY;
                                 if (c + 1 > rlim[k]) e1 = -INFINITY;
                             }
-                            const float p0 = fast_exp2(e0), p1 = fast_exp2(e1);
-                            l_run[k] += p0 + p1;
-                            const float pv0 = p0 * vs[2 * n], pv1 = p1 * vs[2 * n + 1];
-                            const __half2 hh = __floats2half2_rn(pv0, pv1);
-                            const float2 hf = __half22float2(hh);
-                            const __half2 ll = __floats2half2_rn(pv0 - hf.x, pv1 - hf.y);
+                            const float2 pp = make_float2(fast_exp2(e0), fast_exp2(e1));
+                            l_run[k] = __fadd2_rn(l_run[k], pp);
+                            const float2 pv = __fmul2_rn(pp, vs[n]);
+                            const __half2 hh = __floats2half2_rn(pv.x, pv.y);
+                            const float2 lo = minus_f16x2_from_f32x2(hh, pv);
+                            const __half2 ll = __floats2half2_rn(lo.x, lo.y);
                             w[G][2 * h2 + rr] = *reinterpret_cast<const uint32_t*>(&hh);
                             w[G][4 + 2 * h2 + rr] = *reinterpret_cast<const uint32_t*>(&ll);
                         }
@@ -740,19 +758,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // ---- epilogue: O / l for live rows, l summed over the quad and both halves
         const bool ran = j == ntiles;
+        float l_sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         if (ran) {
             const int lj = ntiles - 1;
             bad |= !warp_wait_abortable(S.bar(B_PV_BUF + lj % NSP), (lj / NSP) & 1, abort_flag);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                l_run[k] += __shfl_xor_sync(kFull, l_run[k], 1);
-                l_run[k] += __shfl_xor_sync(kFull, l_run[k], 2);
+                l_sum[k] = l_run[k].x + l_run[k].y;
+                l_sum[k] += __shfl_xor_sync(kFull, l_sum[k], 1);
+                l_sum[k] += __shfl_xor_sync(kFull, l_sum[k], 2);
             }
             if (qq == 0) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
                     red[((ntiles & 1) * 2 + half) * BM + (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)] =
-                        l_run[k];
+                        l_sum[k];
             }
         }
         // every softmax thread reaches this barrier exactly once
@@ -767,7 +787,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int rr = 0; rr < 2; ++rr) {
                     const int k = 2 * blk + rr;
                     const int rw = (warp & 3) * 32 + 16 * blk + gq + 8 * rr;
-                    const float l = l_run[k] + red[((ntiles & 1) * 2 + (half ^ 1)) * BM + rw];
+                    const float l = l_sum[k] + red[((ntiles & 1) * 2 + (half ^ 1)) * BM + rw];
                     bool row_live;
                     float* op = out_row(a, rw, row_live) + c0 + 2 * qq;
                     const float inv = (row_live && l > 0.0f) ? __fdiv_rn(1.0f, l) : 0.0f;
