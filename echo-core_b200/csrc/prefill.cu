@@ -657,30 +657,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmax[k] = fmaxf(tmax[k], __shfl_xor_sync(kFull, tmax[k], 2));
             }
             // row maximum over both halves (every thread of a row computes the
-            // same m_run, corr and p scale from it)
-            if (qq == 0) {
+            // same m_run, corr and p scale from it).  The running maximum only
+            // moves when some half-row exceeds it by the lazy threshold, which
+            // after the first tiles is rare: one barrier that ORs that
+            // condition decides whether the halves need to exchange at all.
+            bool need = false;
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    red[(par * 2 + half) * BM + (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)] =
-                        tmax[k];
-            }
-            named_bar(1, kSoftmaxThreads);
-            float corr[4], neg_m[4];
+            for (int k = 0; k < 4; ++k) need |= tmax[k] > m_run[k] + kLazyRescale;
+            float corr[4] = {1.0f, 1.0f, 1.0f, 1.0f};
             bool any_corr = false;
+            if (bar_any(1, kSoftmaxThreads, need)) {
+                if (qq == 0) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float t = fmaxf(
-                    tmax[k],
-                    red[(par * 2 + (half ^ 1)) * BM + (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)]);
-                corr[k] = 1.0f;
-                if (t > m_run[k] + kLazyRescale) {
-                    corr[k] = fast_exp2(m_run[k] - t);
-                    m_run[k] = t;
-                    any_corr = true;
+                    for (int k = 0; k < 4; ++k)
+                        red[(par * 2 + half) * BM + (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)] =
+                            tmax[k];
                 }
-                l_run[k] = __fmul2_rn(l_run[k], make_float2(corr[k], corr[k]));
-                neg_m[k] = m_run[k] == -INFINITY ? 0.0f : -m_run[k];
+                named_bar(1, kSoftmaxThreads);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float t = fmaxf(
+                        tmax[k],
+                        red[(par * 2 + (half ^ 1)) * BM + (warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)]);
+                    if (t > m_run[k] + kLazyRescale) {
+                        corr[k] = fast_exp2(m_run[k] - t);
+                        m_run[k] = t;
+                        any_corr = true;
+                    }
+                    l_run[k] = __fmul2_rn(l_run[k], make_float2(corr[k], corr[k]));
+                }
             }
+            float neg_m[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) neg_m[k] = m_run[k] == -INFINITY ? 0.0f : -m_run[k];
 
             // rescale this half of the O rows only when some row's maximum
             // jumped (rare): O must first hold every earlier tile
