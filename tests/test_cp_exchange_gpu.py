@@ -60,7 +60,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _two_rank_worker(rank, port, L, result, same_gpu_timeout):
+def _rank_worker(rank, world, port, L, result, same_gpu_timeout):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     for sub in ("oracle", "echo-core_b200", "tests"):
@@ -74,10 +74,10 @@ def _two_rank_worker(rank, port, L, result, same_gpu_timeout):
     os.environ["MASTER_PORT"] = str(port)
     dev = torch.device("cuda", 0 if same_gpu_timeout else rank)
     torch.cuda.set_device(dev)
-    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         kq, vq, ks, vs, q = _seq(L, 7)
-        lo, hi = ranks.shard(L, rank, 2)
+        lo, hi = ranks.shard(L, rank, world)
         bc, po, pml = _partial(torch, eckv, kq[lo:hi], vq[lo:hi], ks[lo:hi], vs[lo:hi], q, dev)
         cx = ranks.CPExchange(1, H)
         out = torch.full((1, H, D), 9.0, device=dev)
@@ -105,13 +105,13 @@ def _two_rank_worker(rank, port, L, result, same_gpu_timeout):
         dist.destroy_process_group()
 
 
-def _spawn(tmp_path, same_gpu_timeout, L=20000):
+def _spawn(tmp_path, same_gpu_timeout, L=20000, world=2):
     import torch.multiprocessing as mp
     out = str(tmp_path / "r.npy")
     ctx = mp.get_context("spawn")
     port = _free_port()
-    ps = [ctx.Process(target=_two_rank_worker, args=(r, port, L, out, same_gpu_timeout))
-          for r in range(2)]
+    ps = [ctx.Process(target=_rank_worker, args=(r, world, port, L, out, same_gpu_timeout))
+          for r in range(world)]
     for p in ps:
         p.start()
     for p in ps:
@@ -120,7 +120,7 @@ def _spawn(tmp_path, same_gpu_timeout, L=20000):
     for p in ps:
         if p.is_alive():
             p.kill()
-    assert codes == [0, 0], codes
+    assert codes == [0] * world, codes
     return np.load(out)
 
 
@@ -129,6 +129,17 @@ def test_two_ranks_on_two_gpus(cuda, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     code, err, ok = _spawn(tmp_path, False)
+    assert code == 0 and ok == 1.0, (code, err)
+
+
+def test_all_ranks_on_all_gpus(cuda, tmp_path):
+    """One rank per visible GPU (3 to 8): every rank stores into every
+    other rank's buffer; the merged output matches the oracle."""
+    import torch
+    world = min(torch.cuda.device_count(), 8)
+    if world < 3:
+        pytest.skip("needs 3 or more GPUs")
+    code, err, ok = _spawn(tmp_path, False, L=50000, world=world)
     assert code == 0 and ok == 1.0, (code, err)
 
 
