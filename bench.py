@@ -385,15 +385,39 @@ def run_gpu_arm(args, rank, world, local_rank):
         sync_all()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        # Copies overlap the kernels on two copy streams: layer l's inputs go
+        # up while earlier layers attend, and its output comes down while
+        # later layers attend.  Events order each buffer's reuse.
+        up, down = torch.cuda.Stream(), torch.cuda.Stream()
+        consumed = [None] * layers    # decode of layer l done with q/kn/vn[l]
+        read = [None] * layers        # out[l] copied down
         e0.record(stream)
+        up.wait_event(e0)
         for k in range(args.steps):
             for l, bc in enumerate(caches):
-                q[l].copy_(q_h[l], non_blocking=True)
-                kn[l].copy_(kn_h[l], non_blocking=True)
-                vn[l].copy_(vn_h[l], non_blocking=True)
+                if consumed[l] is not None:
+                    up.wait_event(consumed[l])
+                with torch.cuda.stream(up):
+                    q[l].copy_(q_h[l], non_blocking=True)
+                    kn[l].copy_(kn_h[l], non_blocking=True)
+                    vn[l].copy_(vn_h[l], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(up)
+                stream.wait_event(ready)
+                if read[l] is not None:
+                    stream.wait_event(read[l])
                 bc.append(kn[l], vn[l], 1, stream)
                 bc.decode(q[l], out[l], H, scale, stream)
-                out_h[l].copy_(out[l], non_blocking=True)
+                done = torch.cuda.Event()
+                done.record(stream)
+                consumed[l] = done
+                down.wait_event(done)
+                with torch.cuda.stream(down):
+                    out_h[l].copy_(out[l], non_blocking=True)
+                read[l] = torch.cuda.Event()
+                read[l].record(down)
+        for l in range(layers):
+            stream.wait_event(read[l])
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1)
