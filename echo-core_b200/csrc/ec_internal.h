@@ -149,7 +149,7 @@ cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st);
 // keys / values [len][num_kv_heads][128] fp32, q [num_heads][128] unscaled,
 // out [num_heads][128].  Split-K over chunks of at least kF32ChunkTokens
 // tokens; the workspace holds (m, l, O) per (chunk, head).
-constexpr int kF32ChunkTokens = 512;   // minimum tokens per CTA
+constexpr int kF32ChunkTokens = 256;   // minimum tokens per CTA
 int f32_decode_chunks(int len, int num_kv_heads);
 size_t f32_decode_workspace_bytes(int max_len, int num_kv_heads, int num_heads);
 cudaError_t launch_decode_f32(const float* keys, const float* values, int num_kv_heads,
