@@ -461,7 +461,9 @@ def run_gpu_arm(args, rank, world, local_rank):
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "alg_bytes_per_launch": alg_bytes,
-                     "traffic": (tr or {}).get("bytes_per_launch")},
+                     # measured DRAM bytes per cached token (ncu) x this launch's tokens
+                     "traffic": (int(int(lens_mid.sum()) * tr["bytes_per_token_measured"])
+                                 if tr and "bytes_per_token_measured" in tr else None)},
         "gpu_launches": launches_per_layer * layers * args.steps,
         "clocks": clk,
     }
