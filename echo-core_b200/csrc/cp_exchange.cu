@@ -37,7 +37,20 @@ __global__ void __launch_bounds__(D) cp_exchange_kernel(CpExchangeArgs a) {
     const int s = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
     const int S = a.num_seqs, H = a.num_heads, W = a.world;
     const size_t sh = (size_t)s * H + h;
-    const int par = a.epoch & 1;
+    // device epochs: one counter per (sequence, head), advanced by the only
+    // CTA that uses it, so every call of a replayed graph runs the next epoch
+    __shared__ uint32_t s_epoch;
+    if (d == 0) {
+        uint32_t e = a.epoch;
+        if (a.epoch_dev) {
+            e = a.epoch_dev[sh] + 1;
+            a.epoch_dev[sh] = e;
+        }
+        s_epoch = e;
+    }
+    __syncthreads();
+    const uint32_t epoch = s_epoch;
+    const int par = epoch & 1;
     // per rank buffer: [2 parities][W ranks][S][H] of O (D floats), ml (2), flag (1)
     const size_t n_sh = (size_t)S * H;
     auto o_at = [&](float* base, int p, int r) { return base + ((size_t)(p * W + r) * n_sh + sh) * D; };
@@ -60,7 +73,7 @@ __global__ void __launch_bounds__(D) cp_exchange_kernel(CpExchangeArgs a) {
     __threadfence_system();
     __syncthreads();
     if (d == 0)
-        for (int r = 0; r < W; ++r) st_release_sys(flag_at(a.peer_base[r], par, a.rank), a.epoch);
+        for (int r = 0; r < W; ++r) st_release_sys(flag_at(a.peer_base[r], par, a.rank), epoch);
 
     // ---- wait for every rank's flag of this step in the local buffer
     __shared__ int s_bad;
@@ -69,9 +82,9 @@ __global__ void __launch_bounds__(D) cp_exchange_kernel(CpExchangeArgs a) {
         float* mine = a.peer_base[a.rank];
         for (int r = 0; r < W && !bad; ++r) {
             const uint32_t* f = flag_at(mine, par, r);
-            if (ld_acquire_sys(f) == a.epoch) continue;
+            if (ld_acquire_sys(f) == epoch) continue;
             const long long t0 = clock64();
-            while (ld_acquire_sys(f) != a.epoch) {
+            while (ld_acquire_sys(f) != epoch) {
                 if (clock64() - t0 > kWaitBudgetCycles) { bad = 1; break; }
                 __nanosleep(64);
             }

@@ -533,6 +533,8 @@ struct ec_cp_comm {
     int world, rank, num_seqs, num_heads, device;
     float* local;                        // this rank's receive buffer
     float* peers[ec::kCpMaxWorld];       // opened IPC mappings (own slot = local)
+    uint32_t* epoch_dev;                 // device epochs per (sequence, head) (calls with epoch 0)
+    int epoch_mode;                      // 0 none yet, 1 caller epochs, 2 device epochs
     bool opened;
 };
 
@@ -551,14 +553,21 @@ int ec_cp_comm_create(uint32_t world, uint32_t rank, uint32_t num_seqs, uint32_t
     c->num_seqs = (int)num_seqs;
     c->num_heads = (int)num_heads;
     c->opened = false;
+    c->epoch_mode = 0;
+    c->local = nullptr;
+    c->epoch_dev = nullptr;
     cudaGetDevice(&c->device);
     const size_t bytes = ec::cp_exchange_buffer_bytes(c->world, c->num_seqs, c->num_heads);
     cudaError_t e = cudaMalloc(&c->local, bytes);
     if (e == cudaSuccess) e = cudaMemset(c->local, 0, bytes);   // flags start below epoch 1
+    const size_t ebytes = (size_t)num_seqs * num_heads * sizeof(uint32_t);
+    if (e == cudaSuccess) e = cudaMalloc(&c->epoch_dev, ebytes);
+    if (e == cudaSuccess) e = cudaMemset(c->epoch_dev, 0, ebytes);
     cudaIpcMemHandle_t h;
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->local);
     if (e != cudaSuccess) {
         cudaFree(c->local);
+        cudaFree(c->epoch_dev);
         delete c;
         return cuda_fail(e, "cp_comm_create: receive buffer");
     }
@@ -607,6 +616,7 @@ void ec_cp_comm_destroy(ec_cp_comm* c) {
     for (int r = 0; r < c->world; ++r)
         if (r != c->rank && c->peers[r]) cudaIpcCloseMemHandle(c->peers[r]);
     cudaFree(c->local);
+    cudaFree(c->epoch_dev);
     cudaSetDevice(prev);
     delete c;
 }
@@ -617,7 +627,11 @@ int ec_cp_exchange_combine(ec_cp_comm* c, const float* part_o, const float* part
         return fail(EC_ERR_INVALID_ARGUMENT, "cp_exchange_combine: null argument");
     if (!c->opened && c->world > 1)
         return fail(EC_ERR_INVALID_ARGUMENT, "cp_exchange_combine: comm not opened");
-    if (epoch == 0) return fail(EC_ERR_INVALID_ARGUMENT, "cp_exchange_combine: epoch must start at 1");
+    const int mode = epoch == 0 ? 2 : 1;
+    if (c->epoch_mode != 0 && c->epoch_mode != mode)
+        return fail(EC_ERR_INVALID_ARGUMENT,
+                    "cp_exchange_combine: a comm uses caller epochs or device epochs (0), not both");
+    c->epoch_mode = mode;
     ec::CpExchangeArgs a{};
     for (int r = 0; r < c->world; ++r) a.peer_base[r] = c->peers[r];
     a.part_o = part_o;
@@ -629,6 +643,7 @@ int ec_cp_exchange_combine(ec_cp_comm* c, const float* part_o, const float* part
     a.num_seqs = c->num_seqs;
     a.num_heads = c->num_heads;
     a.epoch = epoch;
+    a.epoch_dev = mode == 2 ? c->epoch_dev : nullptr;
     cudaError_t e = ec::launch_cp_exchange(a, as_stream(stream));
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "cp_exchange_combine launch");
 }

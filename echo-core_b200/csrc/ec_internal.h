@@ -141,6 +141,7 @@ struct CpExchangeArgs {
     int32_t* err;
     int world, rank, num_seqs, num_heads;
     uint32_t epoch;
+    uint32_t* epoch_dev;             // non-null: [num_seqs][num_heads] epochs kept on the device
 };
 size_t cp_exchange_buffer_bytes(int world, int num_seqs, int num_heads);
 cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st);

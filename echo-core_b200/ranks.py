@@ -71,7 +71,7 @@ class CPExchange:
     once per step, in the same order; ``close`` is collective too, so that no
     rank frees its buffer while a peer may still store into it."""
 
-    def __init__(self, num_seqs: int, num_heads: int, group=None):
+    def __init__(self, num_seqs: int, num_heads: int, group=None, device_epoch: bool = False):
         import ctypes
         import torch.distributed as dist
         import eckv
@@ -90,14 +90,18 @@ class CPExchange:
             blob = b"".join(got)
             eckv.check(self._lib.ec_cp_comm_open(self._h, ctypes.create_string_buffer(blob, len(blob))))
         self.epoch = 0
+        # device_epoch: the epoch lives on the GPU and advances in stream
+        # order, so combine() can be captured into a CUDA graph and replayed
+        self.device_epoch = device_epoch
 
     def combine(self, part_o, part_ml, out, stream=None) -> None:
         import ctypes
         import eckv
         self.epoch += 1
-        eckv.check(self._lib.ec_cp_exchange_combine(self._h, eckv._ptr(part_o), eckv._ptr(part_ml),
-                                                    ctypes.c_uint32(self.epoch), eckv._ptr(out),
-                                                    eckv._stream(stream)))
+        eckv.check(self._lib.ec_cp_exchange_combine(
+            self._h, eckv._ptr(part_o), eckv._ptr(part_ml),
+            ctypes.c_uint32(0 if self.device_epoch else self.epoch), eckv._ptr(out),
+            eckv._stream(stream)))
 
     def close(self) -> None:
         if not getattr(self, "_h", None) or not self._h.value:

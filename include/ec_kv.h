@@ -300,6 +300,11 @@ EC_API int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t nu
  * order, as ec_lse_combine) is written once every rank's partial for that
  * epoch has arrived.  Waits are bounded (about 1 s); a rank that never
  * arrives makes the others flag EC_DEVERR_TIMEOUT and write zeros.
+ * epoch 0 instead keeps the epochs in device memory (one per sequence and
+ * head) and advances them inside the kernel, so the call can be captured into
+ * a CUDA graph and replayed; a comm uses caller epochs or device epochs, not
+ * both
+ * (EC_ERR_INVALID_ARGUMENT on a switch).
  * world <= 8; num_seqs * num_heads <= 2368 (one CTA each, all resident). */
 #define EC_CP_HANDLE_BYTES 64
 typedef struct ec_cp_comm ec_cp_comm;

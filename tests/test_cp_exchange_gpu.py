@@ -54,13 +54,46 @@ def test_single_rank_exchange_is_the_normalised_output(cuda):
     cx.close()
 
 
+def test_single_rank_device_epoch_replays_as_a_graph(cuda):
+    """epoch 0: the epoch advances on the device, so the call captured once
+    in a CUDA graph is correct on every replay (both parities); a comm then
+    refuses a caller epoch."""
+    import torch
+    import eckv
+    import ranks
+    kq, vq, ks, vs, q = _seq(3000, 2)
+    bc, po, pml = _partial(torch, eckv, kq, vq, ks, vs, q, "cuda")
+    cx = ranks.CPExchange(1, H, device_epoch=True)
+    out = torch.zeros((1, H, D), device="cuda")
+    cx.combine(po, pml, out)                            # device epoch 1, eager
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(g, stream=side):
+        cx.combine(po, pml, out, torch.cuda.current_stream())
+    want = O.decode_attention(kq, vq, ks, vs, 3000, q[0], H, HKV, D, W.softmax_scale(D))
+    for _ in range(3):                                  # device epochs 2..4
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert eckv.device_error() == 0
+        assert_attn_close(out.cpu().numpy()[0], want, "cp x1 graph")
+    del g
+    import ctypes
+    rc = cx._lib.ec_cp_exchange_combine(cx._h, eckv._ptr(po), eckv._ptr(pml), ctypes.c_uint32(7),
+                                        eckv._ptr(out), None)
+    assert rc == eckv.EC_ERR_INVALID_ARGUMENT
+    cx.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _rank_worker(rank, world, port, L, result, same_gpu_timeout):
+def _rank_worker(rank, world, port, L, result, same_gpu_timeout, graph=False):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     for sub in ("oracle", "echo-core_b200", "tests"):
@@ -79,7 +112,7 @@ def _rank_worker(rank, world, port, L, result, same_gpu_timeout):
         kq, vq, ks, vs, q = _seq(L, 7)
         lo, hi = ranks.shard(L, rank, world)
         bc, po, pml = _partial(torch, eckv, kq[lo:hi], vq[lo:hi], ks[lo:hi], vs[lo:hi], q, dev)
-        cx = ranks.CPExchange(1, H)
+        cx = ranks.CPExchange(1, H, device_epoch=graph)
         out = torch.full((1, H, D), 9.0, device=dev)
         eckv.device_error()                              # clear
         if same_gpu_timeout:
@@ -90,10 +123,25 @@ def _rank_worker(rank, world, port, L, result, same_gpu_timeout):
                 code = eckv.device_error()
                 np.save(result, np.array([code, float(np.abs(out.cpu().numpy()).max())]))
             dist.barrier()
+        elif graph:
+            # every rank captures its step once and replays it: device epochs
+            cx.combine(po, pml, out)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.graph(g, stream=side):
+                cx.combine(po, pml, out, torch.cuda.current_stream())
+            dist.barrier()
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            del g
         else:
             for _ in range(3):
                 cx.combine(po, pml, out)
             torch.cuda.synchronize()
+        if not same_gpu_timeout:
             if rank == 0:
                 want = O.decode_attention(kq, vq, ks, vs, L, q[0], H, HKV, D, W.softmax_scale(D))
                 got = out.cpu().numpy()[0]
@@ -105,12 +153,12 @@ def _rank_worker(rank, world, port, L, result, same_gpu_timeout):
         dist.destroy_process_group()
 
 
-def _spawn(tmp_path, same_gpu_timeout, L=20000, world=2):
+def _spawn(tmp_path, same_gpu_timeout, L=20000, world=2, graph=False):
     import torch.multiprocessing as mp
     out = str(tmp_path / "r.npy")
     ctx = mp.get_context("spawn")
     port = _free_port()
-    ps = [ctx.Process(target=_rank_worker, args=(r, world, port, L, out, same_gpu_timeout))
+    ps = [ctx.Process(target=_rank_worker, args=(r, world, port, L, out, same_gpu_timeout, graph))
           for r in range(world)]
     for p in ps:
         p.start()
@@ -140,6 +188,17 @@ def test_all_ranks_on_all_gpus(cuda, tmp_path):
     if world < 3:
         pytest.skip("needs 3 or more GPUs")
     code, err, ok = _spawn(tmp_path, False, L=50000, world=world)
+    assert code == 0 and ok == 1.0, (code, err)
+
+
+def test_ranks_replay_captured_exchange(cuda, tmp_path):
+    """Device epochs across ranks: each rank replays its captured exchange;
+    one rank per visible GPU (2 to 8)."""
+    import torch
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    code, err, ok = _spawn(tmp_path, False, L=30000, world=world, graph=True)
     assert code == 0 and ok == 1.0, (code, err)
 
 
