@@ -628,17 +628,10 @@ __global__ void __launch_bounds__(D) lse_merge_kernel(const float* __restrict__ 
 template <int HKV, int GROUP>
 cudaError_t launch_decode_t(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t st) {
     using G = Geo<HKV>;
-    static unsigned long long attr_done = 0;  // one bit per device ordinal
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static std::atomic<unsigned long long> attr_done{0};
+    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(decode_kernel<HKV, GROUP>),
+                                      G::SMEM, attr_done);
     if (e != cudaSuccess) return e;
-    const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
-    if (!bit || !(attr_done & bit)) {
-        e = cudaFuncSetAttribute(decode_kernel<HKV, GROUP>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
-        if (e != cudaSuccess) return e;
-        attr_done |= bit;
-    }
     CUtensorMap mk, mv;
     if ((e = make_code_map(&mk, a.keys, HKV, a.total_slots, T)) != cudaSuccess) return e;
     if ((e = make_code_map(&mv, a.values, HKV, a.total_slots, T)) != cudaSuccess) return e;

@@ -235,13 +235,12 @@ __global__ void __launch_bounds__((kWarps + 1) * 32)
 // resident CTAs per SM across the KV heads, so that long contexts run in
 // long-lived CTAs and the log-sum-exp merge sees at most a few hundred parts.
 static int f32_target_chunks(int num_kv_heads) {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
-            sms = 148;
-    }
+    // the current device's SM count (queried each call: cheap, and right for
+    // whichever device the caller has made current)
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        sms = 148;
     const int t = 3 * sms / (num_kv_heads > 0 ? num_kv_heads : 1);
     return t > 0 ? t : 1;
 }
@@ -284,17 +283,10 @@ cudaError_t launch_decode_f32(const float* keys, const float* values, int num_kv
     if ((e = make_f32_row_map(&mv, values, num_kv_heads, (uint64_t)len, box)) != cudaSuccess) return e;
 #define EC_F32_CASE(GR)                                                                        \
     case GR: {                                                                                 \
-        static unsigned long long done = 0;                                                    \
-        int dev = 0;                                                                           \
-        cudaGetDevice(&dev);                                                                   \
-        const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;                        \
-        if (!bit || !(done & bit)) {                                                           \
-            e = cudaFuncSetAttribute(decode_f32_kernel<GR>,                                    \
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,              \
-                                     F32Geo<GR>::SMEM);                                        \
-            if (e != cudaSuccess) return e;                                                    \
-            done |= bit;                                                                       \
-        }                                                                                      \
+        static std::atomic<unsigned long long> done{0};                                       \
+        e = ensure_smem_limit(reinterpret_cast<const void*>(decode_f32_kernel<GR>),            \
+                              F32Geo<GR>::SMEM, done);                                         \
+        if (e != cudaSuccess) return e;                                                        \
         decode_f32_kernel<GR><<<grid, (kWarps + 1) * 32, F32Geo<GR>::SMEM, st>>>(             \
             mk, mv, num_kv_heads, len, chunk_tokens, q, q_mul, part_o, part_ml);              \
         break;                                                                                 \

@@ -1,6 +1,7 @@
 // ec_internal.h -- launch arguments and launchers shared by the .cu files.
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
@@ -9,6 +10,21 @@
 #include "ec_kv.h"
 
 namespace ec {
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device
+// ordinal (one bit each in `done`; devices past 63 set it on every call).
+// Safe to call from several host threads: a repeated set is harmless.
+inline cudaError_t ensure_smem_limit(const void* kernel, int bytes,
+                                     std::atomic<unsigned long long>& done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
+    return e;
+}
 
 // Optional paged layout of a batch (device page table; null: contiguous slabs
 // addressed by seq_offset).  Page size 1 << shift tokens, a multiple of 128.

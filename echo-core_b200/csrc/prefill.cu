@@ -825,18 +825,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st) {
-    static unsigned long long attr_done = 0;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static std::atomic<unsigned long long> done_contig{0}, done_paged{0};
+    cudaError_t e = a.pages.table
+        ? ensure_smem_limit(reinterpret_cast<const void*>(prefill_kernel<true>), SMEM, done_paged)
+        : ensure_smem_limit(reinterpret_cast<const void*>(prefill_kernel<false>), SMEM, done_contig);
     if (e != cudaSuccess) return e;
-    const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
-    if (!bit || !(attr_done & bit)) {
-        e = cudaFuncSetAttribute(prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-        if (e != cudaSuccess) return e;
-        attr_done |= bit;
-    }
     CUtensorMap mk, mv;
     if ((e = make_code_map(&mk, a.keys, a.num_kv_heads, a.total_slots, BN)) != cudaSuccess) return e;
     if ((e = make_code_map(&mv, a.values, a.num_kv_heads, a.total_slots, BN)) != cudaSuccess) return e;
