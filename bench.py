@@ -258,7 +258,8 @@ def run_gpu_arm(args, rank, world, local_rank):
         return run_prefill_arm(args, rank, world, local_rank)
     # ---- shard sequences
     nseq_total = cfg.num_seqs
-    lo, hi = ranks.shard(nseq_total, rank, world)
+    # contiguous blocks balanced by cached tokens (equal blocks for equal lengths)
+    lo, hi = ranks.shard_weighted(cfg.ctx[:nseq_total], rank, world)
     lens0 = cfg.ctx[lo:hi]
     nseq = hi - lo
     layers = cfg.num_layers

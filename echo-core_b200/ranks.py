@@ -35,6 +35,43 @@ def shard(n: int, rank: int, world: int) -> tuple[int, int]:
     return rank * n // world, (rank + 1) * n // world
 
 
+def shard_weighted(weights, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous [lo, hi) block of units for `rank`, balanced by weight.
+
+    For ragged batches the weight of a sequence is its cached-token count, so
+    every rank streams about the same KV bytes.  Boundary r is the last unit
+    index whose prefix sum does not exceed r/world of the total; blocks are rank-ordered,
+    cover every unit exactly once, and a rank's sum exceeds total/world by at
+    most one unit's weight.  Equal weights give the same blocks as `shard`.
+    """
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    w = [float(x) for x in weights]
+    if any(x < 0 for x in w):
+        raise ValueError("negative weight")
+    n = len(w)
+    total = sum(w)
+    if total <= 0:
+        return shard(n, rank, world)
+
+    def boundary(r):
+        if r <= 0:
+            return 0
+        if r >= world:
+            return n
+        target = total * r / world
+        acc, best = 0.0, 0
+        for i in range(n):
+            acc += w[i]
+            if acc > target * (1 + 1e-12):
+                break
+            best = i + 1
+        return best
+
+    lo, hi = boundary(rank), boundary(rank + 1)
+    return lo, max(lo, hi)
+
+
 def gather_partials(part_o, part_ml, group=None):
     """All-gathers this rank's partial decode state.
 

@@ -31,6 +31,26 @@ def test_shard_covers_every_unit_once_in_rank_order(n, world):
     assert max(sizes) - min(sizes) <= 1
 
 
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_shard_weighted_balances_ragged_lengths(world):
+    """Config 2's ragged batch (lengths uniform in [512, 8192]): contiguous,
+    rank-ordered blocks covering every sequence once, each rank's cached tokens
+    within one sequence of the even share; equal lengths give `shard`'s blocks."""
+    import random
+    rng = random.Random(world)
+    for n in (0, 1, 7, 64, 129):
+        lens = [rng.randint(512, 8192) for _ in range(n)]
+        blocks = [ranks.shard_weighted(lens, r, world) for r in range(world)]
+        assert blocks[0][0] == 0 and blocks[-1][1] == n
+        for (lo, hi), (lo2, _) in zip(blocks, blocks[1:]):
+            assert lo <= hi == lo2
+        if n:
+            for lo, hi in blocks:
+                assert sum(lens[lo:hi]) <= sum(lens) / world + max(lens)
+        assert [ranks.shard_weighted([5] * n, r, world) for r in range(world)] == \
+            [ranks.shard(n, r, world) for r in range(world)]
+
+
 def test_shard_rejects_bad_rank():
     with pytest.raises(ValueError):
         ranks.shard(10, 2, 2)

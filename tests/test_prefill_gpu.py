@@ -25,9 +25,10 @@ def _bf16_round(x):
     return torch.from_numpy(np.ascontiguousarray(x)).bfloat16().float().numpy()
 
 
-def _case(torch, eckv, pasts, n_new, H, hkv, seed, mode=0, rows=None, qmul=None):
+def _case(torch, eckv, pasts, n_new, H, hkv, seed, mode=0, rows=None, qmul=None, raw_q=False):
     """Builds caches of `pasts` tokens, appends n_new tokens per sequence on
-    the GPU, runs prefill; returns GPU output and the oracle check rows."""
+    the GPU, runs prefill; returns GPU output and the oracle check rows
+    (oracle fed the bf16-cast queries, or the raw fp32 ones with raw_q)."""
     rng = np.random.default_rng(seed)
     seqs, k_new, v_new = [], [], []
     for p in pasts:
@@ -57,7 +58,7 @@ def _case(torch, eckv, pasts, n_new, H, hkv, seed, mode=0, rows=None, qmul=None)
     torch.cuda.synchronize()
     assert bc.device_error() == 0
     got = out.cpu().numpy()
-    qb = _bf16_round(q)
+    qb = q if raw_q else _bf16_round(q)
     checks = []
     for s, ((kf, vf), p) in enumerate(zip(seqs, pasts)):
         kq, ks = O.quantize_kv(kf, hkv, D, mode)
@@ -135,3 +136,20 @@ def test_prefill_mixed_row_magnitudes(cuda):
     qmul = np.where(np.arange(128) % 3 == 0, 30.0, 3e-4)
     for got, want, what in _case(torch, eckv, [300], 128, 8, 2, 12, qmul=qmul):
         assert_attn_close(got, want, what)
+
+
+def test_prefill_error_against_raw_fp32_queries(cuda):
+    """The contract casts queries to bf16 on load; against an oracle fed the
+    raw fp32 queries the difference is that cast's (about 2^-9 relative per
+    query element), reported here beside the bf16-query error."""
+    import torch
+    import eckv
+    rows = [0, 5, 63, 64, 500, 1023]
+    cb = _case(torch, eckv, [1024, 64], 1024, 16, 4, 21, rows=rows)
+    cr = _case(torch, eckv, [1024, 64], 1024, 16, 4, 21, rows=rows, raw_q=True)
+    eb = max(float(np.abs(g - w).max()) for g, w, _ in cb)
+    er = max(float(np.abs(g - w).max()) for g, w, _ in cr)
+    print(f"prefill max-abs error: {eb:.2e} vs bf16-cast queries, {er:.2e} vs raw fp32 queries")
+    for got, want, what in cb:
+        assert_attn_close(got, want, what)
+    assert er < 0.1, er
