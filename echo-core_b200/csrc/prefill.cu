@@ -597,6 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
 
         float sc_next = load_scale(0);
+        float sc_next2 = ntiles > 1 ? load_scale(1) : 0.0f;   // two tiles ahead
         float m_run[4];
         float2 l_run[4];                           // this thread's even / odd columns
 #pragma unroll
@@ -608,7 +609,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int sb = j % NSP, par = j & 1;
             float* sck = scb + par * 2 * BN;
             sck[st] = sc_next * sc_mul;
-            if (j + 1 < ntiles) sc_next = load_scale(j + 1);
+            sc_next = sc_next2;
+            if (j + 2 < ntiles) sc_next2 = load_scale(j + 2);
             bad |= !warp_wait_abortable(S.bar(B_S_FULL + sb), (j / NSP) & 1, abort_flag);
             // tile j's scales are visible to all, and all agree whether to go on
             if (bar_any(1, kSoftmaxThreads, bad)) break;
