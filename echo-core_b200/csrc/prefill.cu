@@ -561,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 
         // per-token scales of a tile: thread st loads k-scale * qk_mul of column
-        // st (st < 128) or v-scale of column st - 128, one tile ahead
+        // st (st < 128) or v-scale of column st - 128, two tiles ahead
         const int sc_col = st & (BN - 1);
         const float* sc_src = st < BN ? a.key_scales : a.val_scales;
         const float sc_mul = st < BN ? a.qk_mul * q_inv : 1.0f;
