@@ -283,7 +283,8 @@ def run_gpu_arm(args, rank, world, local_rank):
     scale = W.softmax_scale(D)
     stream = torch.cuda.current_stream()
     plan_chunks = eckv.lib().ec_decode_workspace_size(nseq, H, D, caches[0].max_seq_len)
-    launches_per_layer = 2 + 1 + (1 if plan_chunks > 0 else 0)  # append+bump, decode, combine
+    # append (its length bump folded in for one new token), decode, split-K merge
+    launches_per_layer = (1 if new_tok == 1 else 2) + 1 + (1 if plan_chunks > 0 else 0)
 
     def step(ev=None, st=None):
         st = st or stream

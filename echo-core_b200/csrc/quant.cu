@@ -180,6 +180,15 @@ __device__ __forceinline__ void quantize_store(const float4 (&xs)[2][HKV], const
     }
 }
 
+// With one new token per sequence, the sequence's only warp advances its
+// length itself once every lane has read the old one; with more, a separate
+// launch does it after all of a sequence's warps have read it.
+__device__ __forceinline__ void bump_own_length(const AppendArgs& a, int s, int32_t len, int lane) {
+    if (a.n_new != 1 || a.seq_len == nullptr) return;
+    __syncwarp();
+    if (lane == 0) a.seq_len[s] = len + 1;
+}
+
 template <int HKV, bool ROW>
 __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
     constexpr int D = 128;
@@ -217,6 +226,7 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
     }
 
     quantize_store<HKV, ROW>(xs, a, slot, lane);
+    bump_own_length(a, s, len, lane);
 }
 
 __global__ void bump_lengths_kernel(AppendArgs a) {
@@ -318,6 +328,7 @@ __global__ void __launch_bounds__(256) append_rope_kernel(AppendArgs a) {
             xs[t][g] = x;
         }
     quantize_store<HKV, ROW>(xs, a, slot, lane);
+    bump_own_length(a, s, len, lane);
 }
 
 struct RopeRowsArgs {
@@ -364,7 +375,7 @@ cudaError_t launch_append_rope(const AppendArgs& a, int num_kv_heads, bool row_m
 #undef EC_APPEND_CASE
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (a.seq_len != nullptr) {
+    if (a.seq_len != nullptr && a.n_new > 1) {
         bump_lengths_kernel<<<(a.num_seqs + 127) / 128, 128, 0, st>>>(a);
         e = cudaGetLastError();
     }
@@ -421,7 +432,7 @@ cudaError_t launch_append(const AppendArgs& a, int num_kv_heads, bool row_mode, 
 #undef EC_APPEND_CASE
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (a.seq_len != nullptr) {
+    if (a.seq_len != nullptr && a.n_new > 1) {
         bump_lengths_kernel<<<(a.num_seqs + 127) / 128, 128, 0, st>>>(a);
         e = cudaGetLastError();
     }
