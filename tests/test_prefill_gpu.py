@@ -88,7 +88,16 @@ def test_prefill_config5_shape_rows(cuda):
         assert_attn_close(got, want, what)
 
 
-@pytest.mark.parametrize("H,hkv", [(8, 8), (32, 8), (4, 1), (16, 2)])
+@pytest.mark.parametrize("n_new", [1, 2, 127, 129])
+def test_prefill_chunk_lengths(cuda, n_new):
+    """Degenerate and block-edge chunk lengths (one token is a decode step)."""
+    import torch
+    import eckv
+    for got, want, what in _case(torch, eckv, [0, 130, 511], n_new, 16, 4, 40 + n_new):
+        assert_attn_close(got, want, what)
+
+
+@pytest.mark.parametrize("H,hkv", [(8, 8), (32, 8), (4, 1), (16, 2), (12, 4), (6, 2)])
 def test_prefill_gqa_groupings(cuda, H, hkv):
     import torch
     import eckv
