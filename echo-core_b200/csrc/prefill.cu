@@ -609,6 +609,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int sb = j % NSP, par = j & 1;
             float* sck = scb + par * 2 * BN;
             sck[st] = sc_next * sc_mul;
+            // p' = p * v_scale is carried in f16 with p < 2^8: v-scales of 255
+            // or more could overflow it, so they are flagged
+            if (st >= BN && sc_next >= 255.0f) flag_error(a.err, EC_DEVERR_RANGE);
             sc_next = sc_next2;
             if (j + 2 < ntiles) sc_next2 = load_scale(j + 2);
             bad |= !warp_wait_abortable(S.bar(B_S_FULL + sb), (j / NSP) & 1, abort_flag);

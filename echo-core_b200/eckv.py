@@ -40,6 +40,7 @@ DEVERR_NONE = 0
 DEVERR_BAD_TABLE = 1
 DEVERR_OVERFLOW = 2
 DEVERR_TIMEOUT = 3
+DEVERR_RANGE = 4
 
 # Every symbol include/ec_kv.h declares.
 EXPORTS = (

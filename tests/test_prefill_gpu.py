@@ -162,3 +162,21 @@ def test_prefill_error_against_raw_fp32_queries(cuda):
     for got, want, what in cb:
         assert_attn_close(got, want, what)
     assert er < 0.1, er
+
+
+def test_prefill_flags_v_scales_out_of_range(cuda):
+    """v-scales of 255 or more (|v| near 32,000 and above) are outside the
+    f16 range of p' = p * v_scale: the kernel flags EC_DEVERR_RANGE."""
+    import torch
+    import eckv
+    n_new = 64
+    bc = eckv.BatchCache([n_new], num_kv_heads=4)
+    k = torch.randn(1, n_new, 4 * D, device="cuda")
+    v = torch.randn(1, n_new, 4 * D, device="cuda")
+    v[0, 10] *= 20000.0                               # one token's v-scale near 600
+    bc.append(k, v, n_new)
+    q = torch.randn(1, n_new, 16, D, device="cuda")
+    out = torch.empty(1, n_new, 16, D, device="cuda")
+    bc.prefill(q, out, n_new, 16, W.softmax_scale(D))
+    torch.cuda.synchronize()
+    assert bc.device_error() == eckv.DEVERR_RANGE
