@@ -416,6 +416,17 @@ class PagedBatchCache(BatchCache):
             self.page_table[seq].copy_(torch.tensor(row, dtype=torch.int32))
             self.capacity[seq] = len(self.pages[seq]) * self.page_tokens
 
+    def release(self, seq: int) -> None:
+        """Returns sequence seq's pages to the pool (a finished sequence) and
+        empties its row, capacity and length.  Call it only once no launch
+        that reads the sequence is still in flight."""
+        torch = _torch()
+        self.free.extend(reversed(self.pages[seq]))
+        self.pages[seq] = []
+        self.page_table[seq].copy_(torch.full((self.max_pages,), -1, dtype=torch.int32))
+        self.capacity[seq] = 0
+        self.length[seq] = 0
+
     def desc(self) -> KVBatch:
         return KVBatch(keys=self.keys.data_ptr(), values=self.values.data_ptr(),
                        key_scales=self.key_scales.data_ptr(), val_scales=self.val_scales.data_ptr(),
