@@ -124,3 +124,43 @@ def test_paged_bad_page_is_flagged(cuda):
     bc.decode(torch.randn(2, H, D, device="cuda"), out, H, 0.1)
     torch.cuda.synchronize()
     assert bc.device_error() == eckv.DEVERR_BAD_TABLE
+
+
+def test_released_pages_serve_a_new_sequence(cuda):
+    """A finished sequence's pages go back to the pool and the sequence that
+    takes its slot appends into them; attention sees only its own tokens,
+    while the other sequence keeps growing past the reuse."""
+    import torch
+    import eckv
+    rng = np.random.default_rng(34)
+    bc = eckv.PagedBatchCache(2, num_pages=8, page_tokens=128, shuffle_seed=4)
+
+    def rows(n):
+        return W.kv_rows(rng, n, HKV, D)
+
+    k1 = np.stack([rows(256), rows(256)])
+    v1 = np.stack([rows(256), rows(256)])
+    bc.reserve(0, 256)
+    bc.reserve(1, 256)
+    bc.append(torch.from_numpy(k1).cuda(), torch.from_numpy(v1).cuda(), 256)
+    torch.cuda.synchronize()
+    old0 = list(bc.pages[0])
+    bc.release(0)
+    k2 = np.stack([rows(384), rows(384)])
+    v2 = np.stack([rows(384), rows(384)])
+    bc.reserve(0, 384)
+    bc.reserve(1, 256 + 384)
+    assert set(bc.pages[0]) & set(old0)             # the released pages are reused
+    bc.append(torch.from_numpy(k2).cuda(), torch.from_numpy(v2).cuda(), 384)
+    q = W.queries(rng, 2, H, D)
+    out = torch.empty((2, H, D), device="cuda")
+    bc.decode(torch.from_numpy(q).cuda(), out, H, W.softmax_scale(D))
+    torch.cuda.synchronize()
+    assert bc.device_error() == 0
+    assert bc.length.cpu().tolist() == [384, 640]
+    for s, (kf, vf) in enumerate([(k2[0], v2[0]), (np.concatenate([k1[1], k2[1]]),
+                                                   np.concatenate([v1[1], v2[1]]))]):
+        kq, ks = O.quantize_kv(kf, HKV, D)
+        vq, vs = O.quantize_kv(vf, HKV, D)
+        want = O.decode_attention(kq, vq, ks, vs, len(kf), q[s], H, HKV, D, W.softmax_scale(D))
+        assert_attn_close(out.cpu().numpy()[s], want, f"sequence {s} after the reuse")
