@@ -548,6 +548,7 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, 1)
 // each of kCombineSplit thread groups sums a quarter of the chunks for every
 // dim (independent loads, so a long chunk list is not one serial chain).
 constexpr int kCombineSplit = 4;
+static_assert(D * kCombineSplit >= 256, "one thread per chunk: the plan allows 256 chunks");
 __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const DecodeArgs a) {
     const int seq = blockIdx.x, h = blockIdx.y;
     const int d = threadIdx.x % D, part = threadIdx.x / D;
@@ -558,9 +559,12 @@ __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const Decode
     const size_t base = (size_t)seq * a.max_chunks * H + h;
     __shared__ float s_f[256], s_l[256], s_red[D * kCombineSplit];
     __shared__ float s_M;
-    // chunk maxima -> M (the plan keeps nch <= 256)
-    float m = -INFINITY;
-    for (int c = threadIdx.x; c < nch; c += D * kCombineSplit) m = fmaxf(m, a.part_ml[(base + (size_t)c * H) * 2]);
+    // chunk maxima -> M (the plan keeps nch <= 256 < the block's threads, so
+    // thread c holds chunk c's (m, l) from the one load)
+    const bool has_c = threadIdx.x < nch;
+    float2 mlc = make_float2(-INFINITY, 0.0f);
+    if (has_c) mlc = *reinterpret_cast<const float2*>(a.part_ml + (base + (size_t)threadIdx.x * H) * 2);
+    float m = mlc.x;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
@@ -572,12 +576,10 @@ __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const Decode
     }
     __syncthreads();
     const float M = s_M;
-    for (int c = threadIdx.x; c < nch; c += D * kCombineSplit) {
-        const size_t p = base + (size_t)c * H;
-        const float mc = a.part_ml[p * 2];
-        const float f = mc == -INFINITY ? 0.0f : exp2f(mc - M);
-        s_f[c] = f;
-        s_l[c] = f * a.part_ml[p * 2 + 1];
+    if (has_c) {
+        const float f = mlc.x == -INFINITY ? 0.0f : exp2f(mlc.x - M);
+        s_f[threadIdx.x] = f;
+        s_l[threadIdx.x] = f * mlc.y;
     }
     __syncthreads();
     float so = 0.0f;
