@@ -21,6 +21,7 @@ Prints one JSON line on rank 0.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -278,11 +279,15 @@ def run_gpu_arm(args, rank, world, local_rank):
     vn = torch.randn((layers, nseq, HKV * D), generator=gen, device=dev)
     out = torch.empty((layers, nseq, H, D), device=dev)
     for bc in caches:
+        # host estimate of the cached tokens at the timed decodes: sizes the
+        # split-K plan for ragged batches (config 2)
+        bc.tokens_hint = int(sum(lens0)) + nseq * (args.warmup + 1 + args.steps // 2) * new_tok
         bc.workspace(H)
     torch.cuda.synchronize()
     scale = W.softmax_scale(D)
     stream = torch.cuda.current_stream()
-    plan_chunks = eckv.lib().ec_decode_workspace_size(nseq, H, D, caches[0].max_seq_len)
+    d0 = caches[0].desc()
+    plan_chunks = eckv.lib().ec_decode_workspace_size_batch(ctypes.byref(d0), H)
     # append (its length bump folded in for one new token), decode, split-K merge
     launches_per_layer = (1 if new_tok == 1 else 2) + 1 + (1 if plan_chunks > 0 else 0)
 

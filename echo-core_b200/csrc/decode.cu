@@ -695,20 +695,30 @@ cudaError_t make_f32_row_map(CUtensorMap* m, const float* base, int hkv, uint64_
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms) {
+DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens) {
     DecodePlan best{T, 1};
     if (max_seq_len <= 0 || num_seqs <= 0) return best;
     const int tiles = (max_seq_len + T - 1) / T;
     double best_cost = 1e300;
     const int kmax = tiles < 256 ? tiles : 256;
+    // with a token count below the all-full batch, the CTAs that find work
+    // are about total / chunk plus half a chunk per sequence; the others exit
+    // at once (about 16 tokens' worth of time each)
+    const bool ragged = total_tokens > 0 && total_tokens < (uint64_t)num_seqs * max_seq_len;
     for (int k = 1; k <= kmax; ++k) {
         const int chunk = ((tiles + k - 1) / k) * T;
         const int kk = (max_seq_len + chunk - 1) / chunk;
         const long long ctas = (long long)num_seqs * kk;
-        const long long waves = (ctas + num_sms - 1) / num_sms;
+        long long busy = ctas;
+        if (ragged) {
+            const double est = (double)total_tokens / chunk + 0.5 * num_seqs;
+            busy = est < (double)ctas ? (long long)est + 1 : ctas;
+        }
+        const long long waves = (busy + num_sms - 1) / num_sms;
         // per-CTA time ~ its tokens plus a fixed prologue; a combine pass when
         // split, growing with the number of chunks it merges
-        const double cost = (double)waves * (chunk + 48) + (kk > 1 ? 64.0 + 0.5 * kk : 0.0);
+        const double cost = (double)waves * (chunk + 48) + 16.0 * (double)(ctas - busy) / num_sms +
+                            (kk > 1 ? 64.0 + 0.5 * kk : 0.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
             best = DecodePlan{chunk, kk};

@@ -85,7 +85,8 @@ int ec_decode_attention_noalloc(const ec_kv_batch* b, const float* q, float* out
     if (e != cudaSuccess) return reject(EC_ERR_CUDA, cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return reject(EC_ERR_UNSUPPORTED, "device ordinal >= 64");
 
-    const ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, sms);
+    const ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, sms,
+                                                b->total_tokens_hint);
     const size_t need = ec::decode_workspace_bytes(plan, (int)b->num_seqs, (int)num_heads);
     if (need > kNoAllocScratchBytes) {
         char msg[200];

@@ -777,6 +777,13 @@ size_t ec_decode_workspace_size(uint32_t num_seqs, uint32_t num_heads, uint32_t 
     return ec::decode_workspace_bytes(p, (int)num_seqs, (int)num_heads);
 }
 
+size_t ec_decode_workspace_size_batch(const ec_kv_batch* b, uint32_t num_heads) {
+    if (!b) return 0;
+    ec::DecodePlan p = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, num_sms_current(),
+                                       b->total_tokens_hint);
+    return ec::decode_workspace_bytes(p, (int)b->num_seqs, (int)num_heads);
+}
+
 static int decode_common(const ec_kv_batch* b, const float* q, float* out, float* out_ml,
                          uint32_t num_heads, float softmax_scale, void* ws, size_t ws_bytes,
                          int mode, ec_stream_t stream, const char* who) {
@@ -788,7 +795,8 @@ static int decode_common(const ec_kv_batch* b, const float* q, float* out, float
     if (!decode_shape_supported(num_heads, b->num_kv_heads, b->head_dim))
         return fail(EC_ERR_UNSUPPORTED, "%s: needs head_dim 128, num_kv_heads 4|8, num_heads/num_kv_heads 1|2|4", who);
     if (!aligned16(q) || !aligned16(out)) return fail(EC_ERR_MISALIGNED, "%s: q/out not 16-byte aligned", who);
-    ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, num_sms_current());
+    ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, num_sms_current(),
+                                          b->total_tokens_hint);
     const size_t need = ec::decode_workspace_bytes(plan, (int)b->num_seqs, (int)num_heads);
     if (need > 0 && (!ws || ws_bytes < need))
         return fail(EC_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", who, need, ws_bytes);

@@ -113,7 +113,9 @@ struct DecodePlan {
     int chunk_tokens;
     int max_chunks;
 };
-DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms);
+// total_tokens: host estimate of the batch's cached tokens (0: unknown, every
+// sequence is assumed to be max_seq_len long)
+DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens = 0);
 size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads);
 // Returns cudaErrorInvalidValue for a shape outside the envelope.
 cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan, void* ws,

@@ -48,7 +48,8 @@ EXPORTS = (
     "ec_quantize_per_token_symmetric", "ec_fused_dequant_dot_int8",
     "ec_kv_cache_create", "ec_kv_cache_destroy", "ec_kv_cache_layer", "ec_kv_cache_append",
     "ec_kv_cache_seq_len", "ec_kv_cache_reset", "ec_kv_cache_attention",
-    "ec_kv_batch_append", "ec_decode_workspace_size", "ec_decode_attention",
+    "ec_kv_batch_append", "ec_decode_workspace_size", "ec_decode_workspace_size_batch",
+    "ec_decode_attention",
     "ec_decode_attention_partial", "ec_lse_combine", "ec_prefill_attention",
     "ec_decode_attention_noalloc", "ec_kv_cache_step", "ec_kv_cache_step_host",
     "ec_kv_cache_snapshot_size", "ec_kv_cache_snapshot", "ec_kv_cache_restore",
@@ -103,7 +104,7 @@ class KVBatch(ctypes.Structure):
                 ("num_kv_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
                 ("scale_mode", ctypes.c_int32), ("max_seq_len", ctypes.c_uint32),
                 ("page_table", ctypes.c_void_p), ("page_tokens", ctypes.c_uint32),
-                ("max_pages", ctypes.c_uint32)]
+                ("max_pages", ctypes.c_uint32), ("total_tokens_hint", ctypes.c_uint64)]
 
 
 _lib = None
@@ -135,6 +136,7 @@ def lib() -> ctypes.CDLL:
             "ec_kv_cache_attention": ([vp, u32, vp, vp, f, vp], i32),
             "ec_kv_batch_append": ([ctypes.POINTER(KVBatch), vp, vp, u32, vp], i32),
             "ec_decode_workspace_size": ([u32, u32, u32, u32], ctypes.c_size_t),
+            "ec_decode_workspace_size_batch": ([ctypes.POINTER(KVBatch), u32], ctypes.c_size_t),
             "ec_decode_attention": ([ctypes.POINTER(KVBatch), vp, vp, u32, f, vp, ctypes.c_size_t,
                                      vp], i32),
             "ec_decode_attention_partial": ([ctypes.POINTER(KVBatch), vp, vp, vp, u32, f, vp,
@@ -289,6 +291,8 @@ class BatchCache:
         self.capacities_host = caps
         self.max_seq_len = int(caps.max()) if max_seq_len is None else int(max_seq_len)
         self._ws = None
+        # host estimate of the cached tokens at decode (0: unknown); steers the split-K plan
+        self.tokens_hint = 0
 
     def desc(self) -> KVBatch:
         return KVBatch(keys=self.keys.data_ptr(), values=self.values.data_ptr(),
@@ -297,11 +301,12 @@ class BatchCache:
                        seq_len=self.length.data_ptr(), error_word=self.err.data_ptr(),
                        total_slots=self.total_slots, num_seqs=self.num_seqs,
                        num_kv_heads=self.hkv, head_dim=self.d, scale_mode=self.scale_mode,
-                       max_seq_len=self.max_seq_len)
+                       max_seq_len=self.max_seq_len, total_tokens_hint=self.tokens_hint)
 
     def workspace(self, num_heads: int):
         torch = _torch()
-        need = lib().ec_decode_workspace_size(self.num_seqs, num_heads, self.d, self.max_seq_len)
+        d = self.desc()
+        need = lib().ec_decode_workspace_size_batch(ctypes.byref(d), num_heads)
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(max(need, 16), dtype=torch.uint8, device=self.keys.device)
         return self._ws, need
@@ -394,6 +399,8 @@ class PagedBatchCache(BatchCache):
         self.pages = [[] for _ in range(self.num_seqs)]
         self.max_seq_len = self.max_pages * self.page_tokens
         self._ws = None
+        # host estimate of the cached tokens at decode (0: unknown); steers the split-K plan
+        self.tokens_hint = 0
 
     def slot(self, seq: int, t: int) -> int:
         """Pool slot of token t of sequence seq."""
@@ -435,4 +442,5 @@ class PagedBatchCache(BatchCache):
                        total_slots=self.total_slots, num_seqs=self.num_seqs,
                        num_kv_heads=self.hkv, head_dim=self.d, scale_mode=self.scale_mode,
                        max_seq_len=self.max_seq_len, page_table=self.page_table.data_ptr(),
-                       page_tokens=self.page_tokens, max_pages=self.max_pages)
+                       page_tokens=self.page_tokens, max_pages=self.max_pages,
+                       total_tokens_hint=self.tokens_hint)

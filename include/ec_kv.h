@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define EC_KV_ABI_VERSION 2
+#define EC_KV_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define EC_API __attribute__((visibility("default")))
@@ -227,6 +227,12 @@ typedef struct ec_kv_batch {
     const int32_t* page_table;   /* [num_seqs][max_pages] device int32            */
     uint32_t page_tokens;        /* power of two, multiple of 128                  */
     uint32_t max_pages;          /* row stride of page_table                       */
+    /* Optional host-side estimate of the batch's cached tokens (the sum of
+     * seq_len) at the decode, 0 if unknown.  A ragged batch whose sequences
+     * are mostly shorter than max_seq_len gets a split-K plan sized for its
+     * actual tokens; size the workspace with ec_decode_workspace_size_batch.
+     * The estimate only steers the plan: results do not depend on it. */
+    uint64_t total_tokens_hint;
 } ec_kv_batch;
 
 /* Batched KVCache::append: quantizes tokens_per_seq new tokens of every
@@ -265,6 +271,9 @@ EC_API int ec_rope_rows(float* x, uint32_t rows, uint32_t num_heads, uint32_t he
  * the current device. */
 EC_API size_t ec_decode_workspace_size(uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim,
                                 uint32_t max_seq_len);
+/* The same for a batch descriptor, taking its total_tokens_hint into account
+ * (equals ec_decode_workspace_size when the hint is 0). */
+EC_API size_t ec_decode_workspace_size_batch(const ec_kv_batch* batch, uint32_t num_heads);
 
 /* Decode attention for every sequence of the batch (the loop of
  * src/inference.cpp:321-392 per sequence):

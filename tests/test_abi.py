@@ -44,7 +44,7 @@ def test_every_declared_symbol_is_exported(L):
 
 def test_version_and_status_strings(L):
     import eckv
-    assert L.ec_abi_version() == 2
+    assert L.ec_abi_version() == 3
     assert L.ec_status_string(eckv.EC_ERR_CAPACITY) == b"cache capacity exceeded"
     assert L.ec_status_string(12345) == b"unknown status"
 

@@ -228,3 +228,33 @@ def test_repeated_calls_are_deterministic(cuda):
         bc.decode(_dev(torch, q), out, 16, W.softmax_scale(D))
         torch.cuda.synchronize()
         assert np.array_equal(out.cpu().numpy(), a)
+
+
+def test_ragged_batch_plan_from_token_hint(cuda):
+    """A host estimate of the batch's cached tokens (ec_kv_batch.total_tokens_hint)
+    changes only the split-K plan: the ragged batch of config 2 decodes to
+    the oracle's results with and without it."""
+    import ctypes
+    import torch
+    import eckv
+    rng = np.random.default_rng(12)
+    lens = [int(x) for x in rng.integers(512, 8193, 64)]
+    seqs = [_make_seq(rng, L, 4) for L in lens]
+    q = _dev(torch, W.queries(rng, 64, 16, D))
+    bc = eckv.BatchCache(lens, num_kv_heads=4)
+    fill_batch(bc, seqs)
+    sc = W.softmax_scale(D)
+    outs = []
+    for hint in (0, sum(lens)):
+        bc.tokens_hint = hint
+        d = bc.desc()
+        outs.append((eckv.lib().ec_decode_workspace_size_batch(ctypes.byref(d), 16), torch.empty((64, 16, D), device="cuda")))
+        bc.decode(q, outs[-1][1], 16, sc)
+        torch.cuda.synchronize()
+        assert bc.device_error() == 0
+    assert outs[1][0] > outs[0][0]                   # the hinted plan splits finer
+    qn = q.cpu().numpy()
+    for s in range(0, 64, 7):
+        want = O.decode_attention(*seqs[s], lens[s], qn[s], 16, 4, D, sc)
+        for _, out in outs:
+            assert_attn_close(out.cpu().numpy()[s], want, f"seq {s}")
