@@ -43,6 +43,7 @@ namespace {
 constexpr int D = 128;
 constexpr int T = 32;                              // tokens per tile
 constexpr int kPBufs = 2;                          // p' tiles in flight per head
+constexpr int kDecodeCtasPerSm = 2;                // decode_kernel residency, HKV <= 4
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyRescale = 8.0f;
 constexpr unsigned kFull = 0xffffffffu;
@@ -56,13 +57,17 @@ struct Geo {
     static constexpr int KV_TILE = HKV * HEAD_TILE;
     static constexpr int SC_TILE = T * HKV * 4;
     static constexpr int STAGE = 2 * KV_TILE + 2 * SC_TILE; // multiple of 1024
-    static constexpr int kStages = HKV <= 4 ? 6 : 3;
+    // Two CTAs per SM for HKV <= 4 (three stages each, ~105 KB): one CTA's
+    // prologue, pipeline fill and epilogue overlap the other's streaming.
+    static constexpr int kCtasPerSm = HKV <= 4 ? kDecodeCtasPerSm : 1;
+    static constexpr int kStages = 3;
     static constexpr int PSLOT = 4 * T + 4;                 // p'[4 heads][32 tokens], corr[4]
     static constexpr int PBUF = HKV * kPBufs * PSLOT * 4;
     static constexpr int NBARS = 2 * kStages + 2 * HKV * kPBufs;
     static constexpr int SMEM = 1024 /*alignment slack*/ + kStages * STAGE + PBUF + NBARS * 8;
     static_assert(STAGE % 1024 == 0, "swizzled boxes need 1024-byte aligned stages");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(kCtasPerSm * (SMEM + 1024) <= 228 * 1024, "resident CTAs per SM");
 };
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -211,7 +216,7 @@ __device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMa
 }
 
 template <int HKV, int GROUP>
-__global__ void __launch_bounds__(Geo<HKV>::kThreads, 1)
+__global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const DecodeArgs a) {
     using G = Geo<HKV>;
@@ -230,6 +235,8 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, 1)
     const int seq = blockIdx.y;
     const int chunk = blockIdx.x;
     const bool direct = a.max_chunks == 1;
+    pdl_wait();  // the append before this kernel writes the lengths and the codes
+    pdl_trigger();
     int32_t off, cap, len;
     if (!load_entry(a, seq, off, cap, len)) {
         if (chunk == 0 && threadIdx.x == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
@@ -553,6 +560,8 @@ __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const Decode
     const int seq = blockIdx.x, h = blockIdx.y;
     const int d = threadIdx.x % D, part = threadIdx.x / D;
     const int H = a.num_heads;
+    pdl_wait();  // the partials of decode_kernel
+    pdl_trigger();
     int32_t off, cap, len;
     if (!load_entry(a, seq, off, cap, len)) return;  // flagged by decode_kernel
     const int nch = (len + a.chunk_tokens - 1) / a.chunk_tokens;
@@ -638,8 +647,7 @@ cudaError_t launch_decode_t(const DecodeArgs& a, const DecodePlan& plan, cudaStr
     if ((e = make_code_map(&mk, a.keys, HKV, a.total_slots, T)) != cudaSuccess) return e;
     if ((e = make_code_map(&mv, a.values, HKV, a.total_slots, T)) != cudaSuccess) return e;
     dim3 grid(plan.max_chunks, a.num_seqs);
-    decode_kernel<HKV, GROUP><<<grid, G::kThreads, G::SMEM, st>>>(mk, mv, a);
-    return cudaGetLastError();
+    return launch_pdl(decode_kernel<HKV, GROUP>, grid, dim3(G::kThreads), G::SMEM, st, mk, mv, a);
 }
 
 }  // namespace
@@ -696,6 +704,7 @@ cudaError_t make_f32_row_map(CUtensorMap* m, const float* base, int hkv, uint64_
 }
 
 DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens) {
+    const int slots = num_sms * kDecodeCtasPerSm;  // resident CTAs (exact for HKV <= 4)
     DecodePlan best{T, 1};
     if (max_seq_len <= 0 || num_seqs <= 0) return best;
     const int tiles = (max_seq_len + T - 1) / T;
@@ -714,10 +723,10 @@ DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t tota
             const double est = (double)total_tokens / chunk + 0.5 * num_seqs;
             busy = est < (double)ctas ? (long long)est + 1 : ctas;
         }
-        const long long waves = (busy + num_sms - 1) / num_sms;
+        const long long waves = (busy + slots - 1) / slots;
         // per-CTA time ~ its tokens plus a fixed prologue; a combine pass when
         // split, growing with the number of chunks it merges
-        const double cost = (double)waves * (chunk + 48) + 16.0 * (double)(ctas - busy) / num_sms +
+        const double cost = (double)waves * (chunk + 48) + 16.0 * (double)(ctas - busy) / slots +
                             (kk > 1 ? 64.0 + 0.5 * kk : 0.0);
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
@@ -747,8 +756,7 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
     EC_DEC(4, 4) EC_DEC(4, 2) EC_DEC(4, 1) EC_DEC(8, 4) EC_DEC(8, 2) EC_DEC(8, 1)
 #undef EC_DEC
     if (e != cudaSuccess || plan.max_chunks <= 1) return e;
-    combine_kernel<<<dim3(a.num_seqs, a.num_heads), D * kCombineSplit, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(combine_kernel, dim3(a.num_seqs, a.num_heads), dim3(D * kCombineSplit), 0, st, a);
 }
 
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,

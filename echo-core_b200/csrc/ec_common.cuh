@@ -23,6 +23,18 @@ __device__ __forceinline__ void flag_error(int32_t* err, int32_t code) {
     atomicCAS(err ? err : &g_error_word, 0, code);
 }
 
+// Programmatic dependent launch.  A kernel launched by launch_pdl may become
+// resident while the previous kernel on its stream is still running.  Every
+// thread calls pdl_wait() before its first global memory access (read or
+// write) and before any exit, so the kernel sees all of the predecessor's
+// writes and never completes ahead of it; pdl_trigger() then lets the next
+// kernel's CTAs be scheduled.  Both are no-ops in a kernel launched without
+// the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Paged KV layout (PageMap in ec_internal.h).  With a page table, token t of
 // sequence s lives in slot table[s * max_pages + (t >> shift)] << shift |
 // (t & (page - 1)); without one, in slot seq_offset[s] + t (per-sequence

@@ -26,6 +26,25 @@ inline cudaError_t ensure_smem_limit(const void* kernel, int bytes,
     return e;
 }
 
+// Launch with programmatic stream serialization: the kernel's CTAs may be
+// scheduled while the previous kernel on the stream drains; the kernel itself
+// waits for it (pdl_wait) before touching global memory.
+template <typename... P, typename... A>
+inline cudaError_t launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, A&&... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
+
 // Optional paged layout of a batch (device page table; null: contiguous slabs
 // addressed by seq_offset).  Page size 1 << shift tokens, a multiple of 128.
 struct PageMap {

@@ -192,6 +192,8 @@ __device__ __forceinline__ void bump_own_length(const AppendArgs& a, int s, int3
 template <int HKV, bool ROW>
 __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
     constexpr int D = 128;
+    pdl_wait();  // k / v and the table may come from the previous kernel
+    pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int s = warp / a.n_new;
@@ -230,6 +232,8 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
 }
 
 __global__ void bump_lengths_kernel(AppendArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= a.num_seqs || a.seq_len == nullptr) return;
     TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, 0, 0, 0, a.total_slots, a.pages};
@@ -290,6 +294,8 @@ __device__ __forceinline__ float4 head_rms_norm(float4 x, const uint16_t* w, int
 template <int HKV, bool ROW>
 __global__ void __launch_bounds__(256) append_rope_kernel(AppendArgs a) {
     constexpr int D = 128;
+    pdl_wait();  // k / v and the table may come from the previous kernel
+    pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int s = warp / a.n_new;
@@ -354,32 +360,39 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(RopeRowsArgs a) {
 }
 
 // ---------------------------------------------------------------- launchers
-cudaError_t launch_append_rope(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st) {
+using AppendFn = void (*)(AppendArgs);
+
+// One warp per (sequence, new token); lengths bumped in place for n_new == 1,
+// by a second kernel otherwise.
+static cudaError_t launch_append_with(AppendFn fn, const AppendArgs& a, cudaStream_t st) {
     const int64_t warps = (int64_t)a.num_seqs * a.n_new;
     if (warps == 0) return cudaSuccess;
+    if (fn == nullptr) return cudaErrorInvalidValue;
     const int threads = 256;
     const int64_t blocks = (warps * 32 + threads - 1) / threads;
     if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-#define EC_APPEND_CASE(H)                                                                      \
-    case H:                                                                                    \
-        if (row_mode) append_rope_kernel<H, true><<<(unsigned)blocks, threads, 0, st>>>(a);   \
-        else append_rope_kernel<H, false><<<(unsigned)blocks, threads, 0, st>>>(a);           \
-        break;
-    switch (num_kv_heads) {
-        EC_APPEND_CASE(1)
-        EC_APPEND_CASE(2)
-        EC_APPEND_CASE(4)
-        EC_APPEND_CASE(8)
-        default: return cudaErrorInvalidValue;
-    }
-#undef EC_APPEND_CASE
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    if (a.seq_len != nullptr && a.n_new > 1) {
-        bump_lengths_kernel<<<(a.num_seqs + 127) / 128, 128, 0, st>>>(a);
-        e = cudaGetLastError();
-    }
+    cudaError_t e = launch_pdl(fn, dim3((unsigned)blocks), dim3(threads), 0, st, a);
+    if (e == cudaSuccess && a.seq_len != nullptr && a.n_new > 1)
+        e = launch_pdl(bump_lengths_kernel, dim3((a.num_seqs + 127) / 128), dim3(128), 0, st, a);
     return e;
+}
+
+#define EC_PICK_APPEND(K)                                      \
+    switch (num_kv_heads) {                                    \
+        case 1: return row_mode ? K<1, true> : K<1, false>;    \
+        case 2: return row_mode ? K<2, true> : K<2, false>;    \
+        case 4: return row_mode ? K<4, true> : K<4, false>;    \
+        case 8: return row_mode ? K<8, true> : K<8, false>;    \
+        default: return nullptr;                               \
+    }
+static AppendFn pick_append(int num_kv_heads, bool row_mode) { EC_PICK_APPEND(append_kernel) }
+static AppendFn pick_append_rope(int num_kv_heads, bool row_mode) {
+    EC_PICK_APPEND(append_rope_kernel)
+}
+#undef EC_PICK_APPEND
+
+cudaError_t launch_append_rope(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st) {
+    return launch_append_with(pick_append_rope(num_kv_heads, row_mode), a, st);
 }
 
 cudaError_t launch_rope_rows(float* x, uint32_t rows, uint32_t num_heads, const int32_t* positions,
@@ -412,31 +425,7 @@ cudaError_t launch_quantize_rows(const float* in, int8_t* out, float* scales, ui
 }
 
 cudaError_t launch_append(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st) {
-    const int64_t warps = (int64_t)a.num_seqs * a.n_new;
-    if (warps == 0) return cudaSuccess;
-    const int threads = 256;
-    const int64_t blocks = (warps * 32 + threads - 1) / threads;
-    if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-#define EC_APPEND_CASE(H)                                                                 \
-    case H:                                                                               \
-        if (row_mode) append_kernel<H, true><<<(unsigned)blocks, threads, 0, st>>>(a);   \
-        else append_kernel<H, false><<<(unsigned)blocks, threads, 0, st>>>(a);           \
-        break;
-    switch (num_kv_heads) {
-        EC_APPEND_CASE(1)
-        EC_APPEND_CASE(2)
-        EC_APPEND_CASE(4)
-        EC_APPEND_CASE(8)
-        default: return cudaErrorInvalidValue;
-    }
-#undef EC_APPEND_CASE
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    if (a.seq_len != nullptr && a.n_new > 1) {
-        bump_lengths_kernel<<<(a.num_seqs + 127) / 128, 128, 0, st>>>(a);
-        e = cudaGetLastError();
-    }
-    return e;
+    return launch_append_with(pick_append(num_kv_heads, row_mode), a, st);
 }
 
 // ------------------------------------------------------ fused dequant dot

