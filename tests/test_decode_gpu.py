@@ -258,3 +258,58 @@ def test_ragged_batch_plan_from_token_hint(cuda):
         want = O.decode_attention(*seqs[s], lens[s], qn[s], 16, 4, D, sc)
         for _, out in outs:
             assert_attn_close(out.cpu().numpy()[s], want, f"seq {s}")
+
+
+def test_layer_steps_replayed_as_a_graph(cuda):
+    """Append-then-decode over two layers captured once in a CUDA graph and
+    replayed: the append, decode and split-K merge kernels follow each other
+    with programmatic dependent launch, and every replay must see the token
+    the previous kernel appended and the partials it wrote."""
+    import torch
+    import eckv
+    rng = np.random.default_rng(21)
+    lens = [int(x) for x in rng.integers(300, 3001, 12)]
+    sc = W.softmax_scale(D)
+    layers = []
+    for _ in range(2):
+        seqs = [list(_make_seq(rng, L, 4)) for L in lens]
+        bc = eckv.BatchCache([L + 4 for L in lens], num_kv_heads=4)
+        fill_batch(bc, [tuple(s) for s in seqs])
+        layers.append((bc, seqs))
+    k_buf = [torch.empty((12, 4 * D), device="cuda") for _ in layers]
+    v_buf = [torch.empty((12, 4 * D), device="cuda") for _ in layers]
+    q_buf = [torch.empty((12, 16, D), device="cuda") for _ in layers]
+    o_buf = [torch.empty((12, 16, D), device="cuda") for _ in layers]
+    for (bc, _), q, o in zip(layers, q_buf, o_buf):
+        q.zero_()
+        bc.decode(q, o, 16, sc)      # workspace and one-time set-up outside the capture
+    torch.cuda.synchronize()
+    assert any(bc.workspace(16)[1] > 0 for bc, _ in layers)   # the plan splits
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for (bc, _), k, v, q, o in zip(layers, k_buf, v_buf, q_buf, o_buf):
+            bc.append(k, v, 1)
+            bc.decode(q, o, 16, sc)
+    for step in range(3):
+        news = []
+        for l in range(2):
+            kn, vn = W.kv_rows(rng, 12, 4, D), W.kv_rows(rng, 12, 4, D)
+            qn = W.queries(rng, 12, 16, D)
+            k_buf[l].copy_(_dev(torch, kn)); v_buf[l].copy_(_dev(torch, vn))
+            q_buf[l].copy_(_dev(torch, qn))
+            news.append((kn, vn, qn))
+        g.replay()
+        torch.cuda.synchronize()
+        for l, ((bc, seqs), (kn, vn, qn)) in enumerate(zip(layers, news)):
+            assert bc.device_error() == 0
+            got = o_buf[l].cpu().numpy()
+            for s in range(12):
+                nk, nks = O.quantize_kv(kn[s:s + 1], 4, D)
+                nv, nvs = O.quantize_kv(vn[s:s + 1], 4, D)
+                kq, vq, ks, vs = seqs[s]
+                seqs[s] = [np.concatenate([kq, nk]), np.concatenate([vq, nv]),
+                           np.concatenate([ks, nks]), np.concatenate([vs, nvs])]
+                L = lens[s] + step + 1
+                want = O.decode_attention(*seqs[s], L, qn[s], 16, 4, D, sc)
+                assert_attn_close(got[s], want, f"replay {step} layer {l} seq {s}")
+    del g
