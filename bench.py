@@ -117,7 +117,9 @@ class CpuDecode:
     """Single-sequence decode steps at `ctx` on the host (setup once, time steps).
 
     use_ref: the reference's own InferenceEngine::attention (oracle/_ref), one
-    engine per thread, each holding one copy of the cache; else the C
+    engine per thread, each holding one copy of the cache, run through the
+    reference's weight-absent branch so that the Q/K/V/O matvecs around the
+    loop are not timed (src/inference.cpp:313-319,410-411); else the C
     restatement (oracle/liboracle.so) on one thread."""
 
     def __init__(self, ctx, threads, use_ref):
@@ -131,7 +133,7 @@ class CpuDecode:
         self.engines = []
         if use_ref:
             for _ in range(threads):
-                e = O.RefAttention(H, HKV, D, ctx + 1)
+                e = O.RefAttention(H, HKV, D, ctx + 1, projections=False)
                 e.load(self.kq, self.vq, self.ks, self.vs, ctx)
                 self.engines.append(e)
 
@@ -204,8 +206,9 @@ def run_reference_arm(args, rank):
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": f"{per_step_units} (sequence, layer) decode steps of config 3 "
                                    f"per step on {threads} host threads, "
-                                   + ("the reference's InferenceEngine::attention (oracle/_ref; "
-                                      "includes its identity Q/K/V/O projections)"
+                                   + ("the reference's InferenceEngine::attention (oracle/_ref), "
+                                      "projections excluded: its weight-absent branch skips the "
+                                      "Q/K/V/O matvecs; the attention loop and the append are timed"
                                       if use_ref else "C restatement (oracle)")},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -265,13 +268,14 @@ def run_gpu_arm(args, rank, world, local_rank):
     nseq = hi - lo
     layers = cfg.num_layers
     new_tok = 1
-    cap_extra = (args.warmup + args.steps + 1) * new_tok + 1
+    # capacities, grid bound and split-K token hint (shared with the parity
+    # test at this size, so that both run the same plan)
+    caps, max_len, hint = W.decode_bench_batch(lens0, args.warmup, args.steps, new_tok)
     gen = torch.Generator(device=dev)
     gen.manual_seed(cfg.seed * 1000 + rank)
     caches = []
     for _ in range(layers):
-        bc = eckv.BatchCache([L + cap_extra for L in lens0], num_kv_heads=HKV, device=dev,
-                             max_seq_len=max(lens0) + cap_extra)
+        bc = eckv.BatchCache(caps, num_kv_heads=HKV, device=dev, max_seq_len=max_len)
         fill_layer(torch, eckv, bc, lens0, gen)
         caches.append(bc)
     q = torch.randn((layers, nseq, H, D), generator=gen, device=dev)
@@ -281,7 +285,7 @@ def run_gpu_arm(args, rank, world, local_rank):
     for bc in caches:
         # host estimate of the cached tokens at the timed decodes: sizes the
         # split-K plan for ragged batches (config 2)
-        bc.tokens_hint = int(sum(lens0)) + nseq * (args.warmup + 1 + args.steps // 2) * new_tok
+        bc.tokens_hint = hint
         bc.workspace(H)
     torch.cuda.synchronize()
     scale = W.softmax_scale(D)

@@ -70,3 +70,16 @@ def config(idx: int) -> Config:
 # bytes of one cached token of one layer: K and V codes plus their fp32 scales
 def kv_bytes_per_token(num_kv_heads: int = 4, head_dim: int = 128) -> int:
     return 2 * num_kv_heads * head_dim + 2 * num_kv_heads * 4
+
+
+def decode_bench_batch(lens, warmup: int = 3, steps: int = 20, new_tokens: int = 1):
+    """Capacities, max_seq_len and split-K token hint of the per-layer batch the
+    decode bench builds over cached lengths `lens` for `warmup` untimed and
+    `steps` timed steps of `new_tokens` appended tokens each.  The parity test
+    at the headline size builds its batch from the same numbers, so it runs the
+    bench's own split-K plan."""
+    cap_extra = (warmup + steps + 1) * new_tokens + 1
+    caps = [int(L) + cap_extra for L in lens]
+    max_seq_len = max(int(L) for L in lens) + cap_extra
+    hint = int(sum(int(L) for L in lens)) + len(lens) * (warmup + 1 + steps // 2) * new_tokens
+    return caps, max_seq_len, hint
