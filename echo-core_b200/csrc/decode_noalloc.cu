@@ -13,11 +13,19 @@
 // The array is kNoAllocScratchBytes (16 MiB) of device memory that every GPU
 // which loads this library keeps until the process exits.  The first call on
 // each device looks up the array's device address with cudaGetSymbolAddress
-// (with that device current) and remembers it; make that first call before
-// any stream capture.  All calls share the one array and nothing in it needs
-// to start at zero: every partial the combine step reads is written earlier
-// by the same call.  Two calls whose kernels overlap on the GPU (different
-// streams, no ordering) race on the array and corrupt each other's results.
+// (with that device current) and remembers it together with the device's
+// current CUDA context; make that first call before any stream capture.  A
+// later call that finds a different context current on the device (after
+// cudaDeviceReset, the module is loaded again and the array may move) looks
+// the address up again instead of using the stale one.  All calls share the
+// one array and nothing in it needs to start at zero: every partial the
+// combine step reads is written earlier by the same call.  Two calls whose
+// kernels overlap on the GPU (different streams, no ordering) race on the
+// array and corrupt each other's results.
+//
+// Argument checking is the main entry point's own (ec::check_batch and
+// ec::decode_shape_supported), so the two accept and refuse the same batches,
+// paged ones included.
 #include <cstdio>
 #include <mutex>
 
@@ -32,16 +40,41 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch for each device ordinal, looked up once.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry point (no libcuda link).
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    });
+    return fn;
+}
+
+// Device address of g_noalloc_scratch for each device ordinal, looked up once
+// per CUDA context of that device (the caller has made the device current).
 void* scratch_address(int device, cudaError_t* err) {
     static std::mutex mu;
     static void* addr[kMaxDevices] = {};
+    static CUcontext ctx_of[kMaxDevices] = {};
+    CtxGetCurrentFn get_ctx = ctx_get_current();
+    CUcontext ctx = nullptr;
+    if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS || !ctx) {
+        *err = cudaErrorInvalidDeviceFunction;
+        return nullptr;
+    }
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[device]) {
+    if (!addr[device] || ctx_of[device] != ctx) {
         void* p = nullptr;
         *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (*err != cudaSuccess) return nullptr;
         addr[device] = p;
+        ctx_of[device] = ctx;
     }
     *err = cudaSuccess;
     return addr[device];
@@ -61,23 +94,15 @@ extern "C" {
 
 int ec_decode_attention_noalloc(const ec_kv_batch* b, const float* q, float* out,
                                 uint32_t num_heads, float softmax_scale, ec_stream_t stream) {
-    if (!b || !q || !out) return reject(EC_ERR_INVALID_ARGUMENT, "null argument");
-    if (!b->keys || !b->values || !b->key_scales || !b->val_scales || !b->seq_offset ||
-        !b->seq_capacity || !b->seq_len)
-        return reject(EC_ERR_INVALID_ARGUMENT, "null buffer in batch");
-    if (b->scale_mode != EC_SCALE_PER_HEAD && b->scale_mode != EC_SCALE_ROW)
-        return reject(EC_ERR_INVALID_ARGUMENT, "bad scale_mode");
-    if (!aligned16(b->keys) || !aligned16(b->values) || !aligned16(b->key_scales) ||
-        !aligned16(b->val_scales) || !aligned16(q) || !aligned16(out))
-        return reject(EC_ERR_MISALIGNED, "buffers must be 16-byte aligned");
+    // the same checks, in the same order, as ec_decode_attention
+    const int rc = ec::check_batch(b, "decode_attention_noalloc");
+    if (rc != EC_OK) return rc;
     if (b->num_seqs == 0) return EC_OK;
-    if (b->num_seqs > 65535u || b->total_slots >= (1ull << 31) || b->max_seq_len > 0x7fffffffu)
-        return reject(EC_ERR_UNSUPPORTED, "batch too large (num_seqs <= 65535, total_slots < 2^31)");
+    if (!q || !out) return reject(EC_ERR_INVALID_ARGUMENT, "q/out NULL");
     const uint32_t hkv = b->num_kv_heads;
-    if (b->head_dim != 128 || (hkv != 4 && hkv != 8) || num_heads == 0 || num_heads % hkv ||
-        (num_heads / hkv != 1 && num_heads / hkv != 2 && num_heads / hkv != 4))
-        return reject(EC_ERR_UNSUPPORTED,
-                      "needs head_dim 128, num_kv_heads 4|8, num_heads/num_kv_heads 1|2|4");
+    if (!ec::decode_shape_supported(num_heads, hkv, b->head_dim))
+        return reject(EC_ERR_UNSUPPORTED, "shape outside the decode kernel's envelope");
+    if (!aligned16(q) || !aligned16(out)) return reject(EC_ERR_MISALIGNED, "q/out not 16-byte aligned");
 
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);

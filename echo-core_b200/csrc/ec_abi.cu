@@ -40,14 +40,6 @@ int num_sms_current() {
     return sms > 0 ? sms : 148;
 }
 
-bool decode_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim) {
-    if (head_dim != 128) return false;
-    if (num_kv_heads != 4 && num_kv_heads != 8) return false;
-    if (num_heads == 0 || num_heads % num_kv_heads) return false;
-    const uint32_t g = num_heads / num_kv_heads;
-    return g == 1 || g == 2 || g == 4;
-}
-
 // The fp32-cache kernel: any num_kv_heads, query groups of 1, 2, 4 or 8.
 bool f32_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim) {
     if (head_dim != 128 || num_kv_heads == 0 || num_heads == 0 || num_heads % num_kv_heads)
@@ -61,6 +53,16 @@ cudaStream_t as_stream(ec_stream_t s) { return reinterpret_cast<cudaStream_t>(s)
 }  // namespace
 
 int ec::set_last_error(int status, const char* msg) { return fail(status, "%s", msg); }
+
+bool ec::decode_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim) {
+    if (head_dim != 128) return false;
+    if (num_kv_heads != 4 && num_kv_heads != 8) return false;
+    if (num_heads == 0 || num_heads % num_kv_heads) return false;
+    const uint32_t g = num_heads / num_kv_heads;
+    return g == 1 || g == 2 || g == 4;
+}
+
+using ec::decode_shape_supported;
 
 struct ec_kv_cache {
     ec_model_config cfg;
@@ -649,7 +651,9 @@ int ec_cp_exchange_combine(ec_cp_comm* c, const float* part_o, const float* part
 }
 
 // ------------------------------------------------------------ batched cache
-static int check_batch(const ec_kv_batch* b, const char* who) {
+}  // extern "C"
+
+int ec::check_batch(const ec_kv_batch* b, const char* who) {
     if (!b) return fail(EC_ERR_INVALID_ARGUMENT, "%s: batch is NULL", who);
     if (!b->keys || !b->values || !b->key_scales || !b->val_scales ||
         (!b->seq_offset && !b->page_table) || !b->seq_capacity || !b->seq_len)
@@ -674,6 +678,10 @@ static int check_batch(const ec_kv_batch* b, const char* who) {
     if (b->max_seq_len > 0x7fffffffu) return fail(EC_ERR_INVALID_ARGUMENT, "%s: max_seq_len too large", who);
     return EC_OK;
 }
+
+using ec::check_batch;
+
+extern "C" {
 
 int ec_kv_batch_append(const ec_kv_batch* b, const float* k, const float* v,
                        uint32_t tokens_per_seq, ec_stream_t stream) {

@@ -165,6 +165,14 @@ struct PrefillArgs {
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st);
 // Records `msg` as the calling thread's ec_last_error() text; returns status.
 int set_last_error(int status, const char* msg);
+// Host-side validation of a batch descriptor shared by every entry point that
+// takes one: null buffers, the paged-layout fields (page_tokens a power of two
+// >= 128, max_pages > 0, total_slots a multiple of page_tokens), scale mode,
+// 16-byte alignment and the int32 index limits.  EC_OK, or a status with
+// ec_last_error() set to "<who>: <reason>".
+int check_batch(const ec_kv_batch* b, const char* who);
+// The (num_heads, num_kv_heads, head_dim) shapes the int8 decode kernel covers.
+bool decode_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim);
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
                                int num_seqs, int num_heads, float* out, cudaStream_t st);
 
