@@ -78,7 +78,8 @@ class KVLayer(ctypes.Structure):
     _fields_ = [("keys_int8", ctypes.c_void_p), ("values_int8", ctypes.c_void_p),
                 ("key_scales", ctypes.c_void_p), ("val_scales", ctypes.c_void_p),
                 ("keys_fp32", ctypes.c_void_p), ("values_fp32", ctypes.c_void_p),
-                ("seq_len", ctypes.c_uint32)]
+                ("seq_len", ctypes.c_uint32),
+                ("_align64", ctypes.c_uint8 * 8)]   # KVCacheLayer is alignas(64): 64 bytes
 
 
 class RopeDesc(ctypes.Structure):

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define EC_KV_ABI_VERSION 3
+#define EC_KV_ABI_VERSION 4  /* 4: ec_kv_layer is 64-byte aligned (64 bytes), as KVCacheLayer */
 
 #if defined(__GNUC__)
 #define EC_API __attribute__((visibility("default")))
@@ -124,9 +124,17 @@ typedef struct ec_model_config {
     bool use_kv_quantization;
 } ec_model_config;
 
-/* Mirror of KVCacheLayer (include/kv_cache.h:7-18); pointers are device
- * pointers into the cache's HBM slab. */
-typedef struct ec_kv_layer {
+/* Mirror of KVCacheLayer (include/kv_cache.h:7-18), including its 64-byte
+ * alignment (64 bytes in all); pointers are device pointers into the cache's
+ * HBM slab. */
+#if defined(__cplusplus)
+#define EC_ALIGN64 alignas(64)
+#elif defined(__GNUC__)
+#define EC_ALIGN64 __attribute__((aligned(64)))
+#else
+#define EC_ALIGN64 _Alignas(64)
+#endif
+typedef struct EC_ALIGN64 ec_kv_layer {
     int8_t* keys_int8;
     int8_t* values_int8;
     float* key_scales;

@@ -7,7 +7,10 @@
 // and argument meanings with the storage in HBM:
 //   - the constructor takes the reference's ModelConfig unchanged (layout is
 //     checked at compile time against ec_model_config);
-//   - layer(i) returns the KVCacheLayer view with device pointers;
+//   - layer(i) returns a KVCacheLayer view with device pointers, as a
+//     reference that binds to the reference's own `KVCacheLayer&` (so
+//     `KVCacheLayer& cache_layer = kv_cache_->layer(layer_idx);` of
+//     src/inference.cpp:331 compiles unchanged) or to ec_kv_layer&;
 //   - append(i, k, v) takes device pointers to the token's fp32 K/V
 //     projections and quantizes them on the GPU;
 //   - attention(i, q, out) is the KV half of InferenceEngine::attention;
@@ -20,6 +23,7 @@
 #include <cstddef>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "ec_kv.h"
 
@@ -32,6 +36,29 @@ inline void check(int status) {
                                  ec_last_error());
 }
 
+// One layer's view: ec_kv_layer plus a conversion to any struct laid out like
+// it, the reference's KVCacheLayer (include/kv_cache.h:7-18) included.  The
+// view is refreshed from the cache by every KVCache::layer() call; writing to
+// it does not change the cache (append() and reset() do).
+struct LayerView : ec_kv_layer {
+    template <class KVCacheLayerT>
+    operator KVCacheLayerT&() {
+        static_assert(sizeof(KVCacheLayerT) == sizeof(ec_kv_layer) &&
+                          alignof(KVCacheLayerT) == alignof(ec_kv_layer),
+                      "KVCacheLayer layout differs from ec_kv_layer");
+        return *reinterpret_cast<KVCacheLayerT*>(static_cast<ec_kv_layer*>(this));
+    }
+    template <class KVCacheLayerT>
+    operator const KVCacheLayerT&() const {
+        static_assert(sizeof(KVCacheLayerT) == sizeof(ec_kv_layer) &&
+                          alignof(KVCacheLayerT) == alignof(ec_kv_layer),
+                      "KVCacheLayer layout differs from ec_kv_layer");
+        return *reinterpret_cast<const KVCacheLayerT*>(static_cast<const ec_kv_layer*>(this));
+    }
+};
+static_assert(sizeof(LayerView) == 64 && alignof(LayerView) == 64,
+              "KVCacheLayer is 64 bytes, 64-byte aligned");
+
 class KVCache {
 public:
     // Any struct laid out like ModelConfig (include/config.h:6-24) is accepted,
@@ -41,15 +68,20 @@ public:
         static_assert(sizeof(ModelConfigT) == sizeof(ec_model_config),
                       "ModelConfig layout differs from ec_model_config");
         check(ec_kv_cache_create(reinterpret_cast<const ec_model_config*>(&config), mode, &h_));
+        views_.resize(config.num_layers);
     }
     ~KVCache() { ec_kv_cache_destroy(h_); }
     KVCache(const KVCache&) = delete;
     KVCache& operator=(const KVCache&) = delete;
 
-    ec_kv_layer layer(uint32_t layer_idx) const {
-        ec_kv_layer l;
-        check(ec_kv_cache_layer(h_, layer_idx, &l));
-        return l;
+    // KVCache::layer (src/kv_cache.cpp:79-87): the layer's buffers and length.
+    LayerView& layer(uint32_t layer_idx) {
+        refresh(layer_idx);
+        return views_[layer_idx];
+    }
+    const LayerView& layer(uint32_t layer_idx) const {
+        refresh(layer_idx);
+        return views_[layer_idx];
     }
     void append(uint32_t layer_idx, const float* k_proj, const float* v_proj,
                 ec_stream_t stream = nullptr) {
@@ -79,7 +111,11 @@ public:
     ec_kv_cache* handle() const { return h_; }
 
 private:
+    void refresh(uint32_t layer_idx) const {
+        check(ec_kv_cache_layer(h_, layer_idx, static_cast<ec_kv_layer*>(&views_.at(layer_idx))));
+    }
     ec_kv_cache* h_ = nullptr;
+    mutable std::vector<LayerView> views_;
 };
 
 }  // namespace gpu

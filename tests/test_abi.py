@@ -44,7 +44,7 @@ def test_every_declared_symbol_is_exported(L):
 
 def test_version_and_status_strings(L):
     import eckv
-    assert L.ec_abi_version() == 3
+    assert L.ec_abi_version() == 4
     assert L.ec_status_string(eckv.EC_ERR_CAPACITY) == b"cache capacity exceeded"
     assert L.ec_status_string(12345) == b"unknown status"
 
@@ -84,7 +84,7 @@ def test_struct_layouts_match_the_c_header(tmp_path):
     src = tmp_path / "probe.c"
     fields = {
         "ec_model_config": [f[0] for f in eckv.ModelConfig._fields_],
-        "ec_kv_layer": [f[0] for f in eckv.KVLayer._fields_],
+        "ec_kv_layer": [f[0] for f in eckv.KVLayer._fields_ if not f[0].startswith("_")],
         "ec_kv_batch": [f[0] for f in eckv.KVBatch._fields_],
     }
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "ec_kv.h"', "int main(void){"]
@@ -115,3 +115,90 @@ def test_model_config_mirrors_reference_layout():
     import eckv
     assert ctypes.sizeof(eckv.ModelConfig) == 48
     assert eckv.ModelConfig.use_kv_quantization.offset == 44
+
+
+@pytest.mark.parametrize("page_tokens,max_pages,total_slots", [
+    (96, 4, 96 * 4),       # not a power of two
+    (16, 4, 64),           # below 128: a 32-token decode tile would cross pages
+    (256, 0, 1024),        # no page-table row
+    (256, 4, 1000),        # pool not a whole number of pages
+    (1 << 25, 4, 1 << 25),  # beyond the page-size limit
+])
+def test_noalloc_refuses_bad_paged_batches_like_the_main_entry_point(L, page_tokens, max_pages,
+                                                                     total_slots):
+    """ec_decode_attention_noalloc validates a batch with the same code as
+    ec_decode_attention: a paged descriptor whose page_tokens / max_pages /
+    total_slots the kernels cannot address is refused on the host, before
+    any device call, by both entry points.  A valid paged descriptor (with
+    seq_offset NULL, as the header allows) passes the batch check and only
+    then meets the device."""
+    import eckv
+    null = ctypes.c_void_p(0)
+    b = eckv.KVBatch(keys=256, values=256, key_scales=256, val_scales=256, seq_offset=None,
+                     seq_capacity=256, seq_len=256, total_slots=total_slots, num_seqs=1,
+                     num_kv_heads=4, head_dim=128, scale_mode=0, max_seq_len=page_tokens,
+                     page_table=256, page_tokens=page_tokens, max_pages=max_pages)
+    q = ctypes.c_void_p(256)
+    rc_main = L.ec_decode_attention(ctypes.byref(b), q, q, 16, ctypes.c_float(0.1), q, 1 << 20, null)
+    msg_main = L.ec_last_error()
+    rc = L.ec_decode_attention_noalloc(ctypes.byref(b), q, q, 16, ctypes.c_float(0.1), null)
+    assert rc == rc_main == eckv.EC_ERR_INVALID_ARGUMENT, (rc, rc_main)
+    assert L.ec_last_error().split(b":", 1)[1] == msg_main.split(b":", 1)[1]
+
+
+def test_noalloc_takes_the_main_entry_points_null_argument_checks(L):
+    import eckv
+    null = ctypes.c_void_p(0)
+    assert L.ec_decode_attention_noalloc(None, null, null, 16, ctypes.c_float(0.1),
+                                         null) == eckv.EC_ERR_INVALID_ARGUMENT
+    b = eckv.KVBatch(keys=256, values=256, key_scales=256, val_scales=256, seq_offset=None,
+                     seq_capacity=256, seq_len=256, total_slots=1024, num_seqs=1,
+                     num_kv_heads=4, head_dim=128, scale_mode=0, max_seq_len=512)
+    # neither seq_offset nor a page table
+    assert L.ec_decode_attention_noalloc(ctypes.byref(b), ctypes.c_void_p(256), ctypes.c_void_p(256),
+                                         16, ctypes.c_float(0.1), null) == eckv.EC_ERR_INVALID_ARGUMENT
+    b.seq_offset = 256
+    b.head_dim = 64
+    assert L.ec_decode_attention_noalloc(ctypes.byref(b), ctypes.c_void_p(256), ctypes.c_void_p(256),
+                                         16, ctypes.c_float(0.1), null) == eckv.EC_ERR_UNSUPPORTED
+
+
+def test_kv_layer_has_the_reference_alignment(tmp_path):
+    """KVCacheLayer is alignas(64) (include/kv_cache.h:7): ec_kv_layer keeps
+    that size and alignment in C and C++, and the binding's struct is 64 bytes."""
+    import eckv
+    assert ctypes.sizeof(eckv.KVLayer) == 64
+    src = tmp_path / "align.c"
+    src.write_text('#include "ec_kv.h"\n'
+                   '_Static_assert(sizeof(ec_kv_layer) == 64, "size");\n'
+                   '_Static_assert(_Alignof(ec_kv_layer) == 64, "align");\n'
+                   'int main(void) { return 0; }\n')
+    subprocess.run(["gcc", "-std=c11", "-fsyntax-only", "-I", os.path.join(ROOT, "include"),
+                    str(src)], check=True)
+
+
+def test_reference_layer_call_site_compiles_against_the_wrapper(tmp_path):
+    """The reference engine's own call site, `KVCacheLayer& cache_layer =
+    kv_cache_->layer(layer_idx);` (src/inference.cpp:331), and its
+    `layer(0).seq_len` read (src/kv_cache.cpp:115-118) compile unchanged
+    against ec::gpu::KVCache, with a KVCacheLayer laid out as the
+    reference declares it (include/kv_cache.h:7-18)."""
+    src = tmp_path / "site.cpp"
+    src.write_text(r"""
+#include <cstdint>
+#include <memory>
+#include "ec_kv_cache.hpp"
+struct alignas(64) KVCacheLayer {
+    int8_t* keys_int8; int8_t* values_int8; float* key_scales; float* val_scales;
+    float* keys_fp32; float* values_fp32; uint32_t seq_len;
+};
+using KVCache = ec::gpu::KVCache;
+uint32_t site(std::unique_ptr<KVCache>& kv_cache_, uint32_t layer_idx) {
+    KVCacheLayer& cache_layer = kv_cache_->layer(layer_idx);
+    const KVCache& c = *kv_cache_;
+    const KVCacheLayer& l0 = c.layer(0);
+    return cache_layer.seq_len + l0.seq_len + kv_cache_->layer(0).seq_len;
+}
+""")
+    subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-Wall", "-I",
+                    os.path.join(ROOT, "include"), str(src)], check=True)
