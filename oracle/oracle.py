@@ -94,6 +94,10 @@ def ref():
         L.ref_attn_load.restype = ctypes.c_int
         L.ref_attn_step.argtypes = [vp, _u32, _f32p, _f32p]
         L.ref_attn_step.restype = ctypes.c_int
+        L.ref_attn_create_noproj.argtypes = [_u32, _u32, _u32, _u32]
+        L.ref_attn_create_noproj.restype = vp
+        L.ref_attn_step_noproj.argtypes = [vp, _u32, _f32p, _f32p]
+        L.ref_attn_step_noproj.restype = ctypes.c_int
         L.ref_attn_f32_create.argtypes = [_u32, _u32, _u32, _u32]
         L.ref_attn_f32_create.restype = vp
         L.ref_attn_f32_run.argtypes = [vp, _u32, _f32p, _f32p, _f32p, _f32p]
@@ -336,10 +340,17 @@ class RefAttentionF32:
 
 
 class RefAttention:
-    """The reference's InferenceEngine::attention loop (src/inference.cpp:321-406)."""
+    """The reference's InferenceEngine::attention loop (src/inference.cpp:321-406).
 
-    def __init__(self, num_heads, num_kv_heads, head_dim, max_seq_len):
-        self.h = ref().ref_attn_create(num_heads, num_kv_heads, head_dim, max_seq_len)
+    projections=True runs it as the reference does, with fp16 identity Q and O
+    weight matvecs around the loop (:313-319, :410-411); projections=False
+    takes the reference's weight-absent branch, so step() times the attention
+    loop and the append alone (run() needs the projections)."""
+
+    def __init__(self, num_heads, num_kv_heads, head_dim, max_seq_len, projections=True):
+        create = ref().ref_attn_create if projections else ref().ref_attn_create_noproj
+        self.h = create(num_heads, num_kv_heads, head_dim, max_seq_len)
+        self.projections = projections
         self.H, self.hkv, self.d = num_heads, num_kv_heads, head_dim
 
     def close(self):
@@ -378,5 +389,6 @@ class RefAttention:
         q = np.ascontiguousarray(q, np.float32).reshape(-1)
         if out is None:
             out = np.zeros(self.H * self.d, np.float32)
-        ref().ref_attn_step(self.h, self.kv_len, _p(q, _f32p), _p(out, _f32p))
+        fn = ref().ref_attn_step if self.projections else ref().ref_attn_step_noproj
+        fn(self.h, self.kv_len, _p(q, _f32p), _p(out, _f32p))
         return out

@@ -18,6 +18,7 @@
 #include <cstdint>
 #include <cstring>
 #include <memory>
+#include <unordered_map>
 #include <vector>
 
 #include "inference.h"
@@ -58,6 +59,17 @@ struct VProjTag {
     friend type get(VProjTag);
 };
 template struct Expose<VProjTag, &InferenceEngine::v_proj_>;
+
+struct AttnOutTag {
+    typedef float* InferenceEngine::*type;
+    friend type get(AttnOutTag);
+};
+template struct Expose<AttnOutTag, &InferenceEngine::attn_out_>;
+struct GgufMapTag {
+    typedef std::unordered_map<size_t, size_t> InferenceEngine::*type;
+    friend type get(GgufMapTag);
+};
+template struct Expose<GgufMapTag, &InferenceEngine::gguf_offset_map_>;
 
 ModelConfig make_config(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
                         uint32_t num_layers, uint32_t max_seq_len, bool quant) {
@@ -217,6 +229,46 @@ int ref_attn_step(void* h, uint32_t kv_len, const float* q, float* out) {
     l.seq_len = kv_len;
     clear_projections(r);
     (r->eng.get()->*get(AttentionTag()))(0, q, out);
+    return 0;
+}
+
+// ---- InferenceEngine::attention without its weight matvecs ----
+// The timed reference arm measures the attention loop of src/inference.cpp:
+// 321-414 (q prescale, scores over the int8 cache, softmax, P.V, the append),
+// not the Q/K/V/O projections around it (:313-319, :410-411).  The engine takes
+// the reference's own "weight absent" branch for them: has_weight() is true for
+// every offset while gguf_offset_map_ is empty (include/inference.h:67-70), so
+// one entry under a key that is no layout offset (SIZE_MAX) makes it false for
+// the projection weights, and attention() then skips the four matvecs.  No
+// weights are loaded.  The caller's q goes straight into q_proj_, and the
+// result is read from attn_out_ (the O projection's input).
+void* ref_attn_create_noproj(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                             uint32_t max_seq_len) {
+    ModelConfig c = make_config(num_heads, num_kv_heads, head_dim, 1, max_seq_len, true);
+    auto* r = new RefAttn{std::make_unique<InferenceEngine>(c), num_heads, num_kv_heads, head_dim,
+                          max_seq_len};
+    (r->eng.get()->*get(GgufMapTag()))[SIZE_MAX] = 0;
+    return r;
+}
+
+// One decode step over the cache ref_attn_load installed, projections
+// excluded: q [num_heads*head_dim] unscaled, out the attention output.
+int ref_attn_step_noproj(void* h, uint32_t kv_len, const float* q, float* out) {
+    RefAttn* r = static_cast<RefAttn*>(h);
+    if (kv_len >= r->max_seq_len) return -1;
+    InferenceEngine* e = r->eng.get();
+    KVCache& cache = *(e->*get(CacheTag()));
+    KVCacheLayer& l = cache.layer(0);
+    l.key_scales[kv_len] = r->saved_k_scale;   // see ref_attn_step
+    l.val_scales[kv_len] = r->saved_v_scale;
+    l.seq_len = kv_len;
+    const size_t hidden = static_cast<size_t>(r->num_heads) * r->head_dim;
+    std::memcpy(e->*get(QProjTag()), q, sizeof(float) * hidden);
+    std::memset(e->*get(KProjTag()), 0, sizeof(float) * r->num_kv_heads * r->head_dim);
+    std::memset(e->*get(VProjTag()), 0, sizeof(float) * r->num_kv_heads * r->head_dim);
+    std::vector<float> sink(hidden);
+    (e->*get(AttentionTag()))(0, q, sink.data());
+    std::memcpy(out, e->*get(AttnOutTag()), sizeof(float) * hidden);
     return 0;
 }
 

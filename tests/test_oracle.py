@@ -203,6 +203,27 @@ def test_decode_attention_matches_reference_build(L, H):
     assert np.array_equal(bits(got), bits(want))
 
 
+@needs_ref
+@pytest.mark.parametrize("L,H", [(1, 16), (700, 16), (4096, 16), (50, 8)])
+def test_reference_attention_without_projections_is_the_same_loop(L, H):
+    """The reference arm of the bench times InferenceEngine::attention through
+    the reference's own weight-absent branch (no Q/K/V/O matvecs).  Step after
+    step over the same loaded cache it gives the restatement's output bit for
+    bit, as the identity-projection path does."""
+    hkv, d = 4, 128
+    rng = np.random.default_rng(L + 3 * H)
+    kq, ks = O.quantize_kv(W.kv_rows(rng, L, hkv, d), hkv, d)
+    vq, vs = O.quantize_kv(W.kv_rows(rng, L, hkv, d), hkv, d)
+    r = O.RefAttention(H, hkv, d, L + 1, projections=False)
+    r.load(kq, vq, ks, vs, L)
+    for _ in range(3):
+        q = W.queries(rng, 1, H, d)[0]
+        got = r.step(q).reshape(H, d)
+        want = O.decode_attention(kq, vq, ks, vs, L, q, H, hkv, d, W.softmax_scale(d))
+        assert np.array_equal(bits(got), bits(want))
+    r.close()
+
+
 @pytest.mark.parametrize("tag", ["a", "b", "c"])
 def test_decode_attention_f32_matches_golden(golden, tag):
     """FP32 cache mode (src/inference.cpp:346-358, 386-393): the restatement
