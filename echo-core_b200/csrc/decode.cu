@@ -8,14 +8,19 @@
 // sum_t p_t * (code * v_scale) (:383-392).  The softmax runs online in base 2
 // (log2(e) folded into q), with the maximum carried per split.
 //
-// Work decomposition.  One CTA owns one (sequence, chunk of tokens) and all
-// KV heads of it.  Tiles of 32 tokens stream through a shared-memory ring:
-// per KV head one 2-D TMA copy of the K codes and one of the V codes (a
-// [32 tokens x 128 B] box of the [slot][head][128] cache, 128-byte swizzled),
-// plus one 1-D bulk copy per scale array.  No multicast.  Each KV head has
-// one QK warp and one PV warp; they hand tiles of p' = p * v_scale to each
-// other through a double-buffered slot guarded by mbarriers.  Every K and V
-// byte is read from HBM exactly once per step.
+// Work decomposition.  One CTA owns one (head block, chunk of tokens,
+// sequence): HC consecutive KV heads of the sequence (all of them unless a
+// large query group or head_dim 256 splits the heads over several CTAs).  The
+// unit of work is a (KV head, quad of up to 4 of its query heads); a CTA
+// holds HC * QW units, QW = ceil(group / 4).  Tiles of 32 tokens stream
+// through a shared-memory ring: per KV head and 128-dim block one 2-D TMA copy
+// of the K codes and one of the V codes (a [32 tokens x 128 B] box of the
+// [slot][head][head_dim] cache, 128-byte swizzled), plus the tile's per-token
+// scales (one 1-D bulk copy per scale array, or 4-byte cp.async copies when a
+// token's scale row is not 16-byte sized).  No multicast.  Each unit has one
+// QK warp and one PV warp; they hand tiles of p' = p * v_scale to each other
+// through a double-buffered slot guarded by mbarriers.  Every K and V byte is
+// read from HBM once per step by the CTA that owns its KV head.
 //
 // Both contractions run on the tensor cores as int8 mma.sync m16n8k32 with
 // exact integer accumulation:
@@ -40,34 +45,55 @@
 namespace ec {
 namespace {
 
-constexpr int D = 128;
+constexpr int D = 128;                             // dims per 128-byte box (one block)
 constexpr int T = 32;                              // tokens per tile
 constexpr int kPBufs = 2;                          // p' tiles in flight per head
-constexpr int kDecodeCtasPerSm = 2;                // decode_kernel residency, HKV <= 4
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyRescale = 8.0f;
 constexpr unsigned kFull = 0xffffffffu;
 
-template <int HKV>
+constexpr int kResidentSmem = 228 * 1024;   // shared memory per SM
+constexpr int kCtaReservedSmem = 1024;      // reserved by the system per resident CTA
+
+// HC KV heads per CTA, QW query-head quads per KV head, SCW scale words per
+// token in a tile's scale arrays (the cache's num_kv_heads), DV 128-dim
+// blocks per head (head_dim = 128 * DV).
+template <int HC, int QW, int SCW, int DV>
 struct Geo {
-    static constexpr int kWarps = 2 * HKV;                  // QK warps 0..HKV-1, PV warps HKV..
+    static constexpr int DH = D * DV;                       // head_dim
+    static constexpr int kUnits = HC * QW;                  // (KV head, query quad)
+    static constexpr int kWarps = 2 * kUnits;               // QK warps 0..U-1, PV warps U..
     static constexpr int kConsumerThreads = kWarps * 32;
     static constexpr int kThreads = kConsumerThreads + 32;   // + one producer warp
-    static constexpr int HEAD_TILE = T * D;                 // 4 KB: one head's [32][128] box
-    static constexpr int KV_TILE = HKV * HEAD_TILE;
-    static constexpr int SC_TILE = T * HKV * 4;
+    static constexpr int BOX = T * D;                       // 4 KB: one [32][128 B] box
+    static constexpr int HEAD_TILE = DV * BOX;              // one head's DV boxes
+    static constexpr int KV_TILE = HC * HEAD_TILE;
+    static constexpr int SC_TILE = ((T * SCW * 4 + 511) / 512) * 512;
     static constexpr int STAGE = 2 * KV_TILE + 2 * SC_TILE; // multiple of 1024
-    // Two CTAs per SM for HKV <= 4 (three stages each, ~105 KB): one CTA's
-    // prologue, pipeline fill and epilogue overlap the other's streaming.
-    static constexpr int kCtasPerSm = HKV <= 4 ? kDecodeCtasPerSm : 1;
-    static constexpr int kStages = 3;
+    // Ring depth: three stages when a stage carries 4+ KV heads; a deeper
+    // ring for the narrow stages of one or two KV heads, whose few resident
+    // CTAs must still keep ~60 KB or more in flight per SM.
+    static constexpr int kStages =
+        HC >= 4 ? 3 : HC == 2 ? (QW >= 2 ? 4 : 3) : (QW >= 8 ? 8 : QW >= 4 ? 6 : 3);
     static constexpr int PSLOT = 4 * T + 4;                 // p'[4 heads][32 tokens], corr[4]
-    static constexpr int PBUF = HKV * kPBufs * PSLOT * 4;
-    static constexpr int NBARS = 2 * kStages + 2 * HKV * kPBufs;
+    static constexpr int PBUF = kUnits * kPBufs * PSLOT * 4;
+    static constexpr int NBARS = 2 * kStages + 2 * kUnits * kPBufs;
     static constexpr int SMEM = 1024 /*alignment slack*/ + kStages * STAGE + PBUF + NBARS * 8;
+    // Resident CTAs per SM: as many as shared memory and registers allow, at
+    // most 8.  With several CTAs per SM one CTA's prologue, pipeline fill and
+    // epilogue overlap another's streaming (two for 4 KV heads, ~105 KB each).
+    // Registers: the QK and PV warps need about 96 a thread without spilling
+    // at head_dim 128, about 112 at 256.
+    static constexpr int kBySmem = kResidentSmem / (SMEM + kCtaReservedSmem);
+    static constexpr int kByRegs = 65536 / (kThreads * (DV == 1 ? 96 : 112));
+    static constexpr int kByRes = kBySmem < kByRegs ? kBySmem : kByRegs;
+    static constexpr int kCtasPerSm = kByRes < 8 ? kByRes : 8;
+    // SCW >= 4 scale rows are whole multiples of 16 bytes: one bulk copy each
+    static constexpr bool kBulkScales = SCW % 4 == 0;
     static_assert(STAGE % 1024 == 0, "swizzled boxes need 1024-byte aligned stages");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
-    static_assert(kCtasPerSm * (SMEM + 1024) <= 228 * 1024, "resident CTAs per SM");
+    static_assert(kCtasPerSm >= 1, "resident CTAs per SM");
+    static_assert(kUnits * 4 * (DH + 2) * 4 <= kStages * STAGE, "merge area fits the ring");
 };
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -84,6 +110,19 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
+}
+
+// 4-byte asynchronous copy global -> shared, and an arrive on `bar` that fires
+// once every cp.async this thread issued before it has landed (the pending
+// count is raised when this executes and lowered on completion, so the
+// barrier's expected count is unchanged).
+__device__ __forceinline__ void cp_async_4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
 }
 
 // Byte offset of 16-byte chunk `c` of row `r` inside a 128-byte-swizzled box.
@@ -129,10 +168,11 @@ __device__ __forceinline__ bool load_entry(const DecodeArgs& a, int s, int32_t& 
 // Writes the result of a sequence with no cached token: zeros (kOut, as the
 // reference's memset at src/inference.cpp:328) or an empty partial state.
 __device__ void write_empty(const DecodeArgs& a, int seq) {
-    for (int o = threadIdx.x; o < a.num_heads * D; o += blockDim.x) {
-        a.out[(size_t)seq * a.num_heads * D + o] = 0.0f;
-        if (a.mode == kPartial && (o % D) == 0) {
-            const int h = o / D;
+    const int dh = a.head_dim;
+    for (int o = threadIdx.x; o < a.num_heads * dh; o += blockDim.x) {
+        a.out[(size_t)seq * a.num_heads * dh + o] = 0.0f;
+        if (a.mode == kPartial && (o % dh) == 0) {
+            const int h = o / dh;
             a.out_ml[((size_t)seq * a.num_heads + h) * 2] = -INFINITY;
             a.out_ml[((size_t)seq * a.num_heads + h) * 2 + 1] = 0.0f;
         }
@@ -150,19 +190,38 @@ __device__ __forceinline__ void consumer_barrier(int threads) {
 
 // Issues tile j of the chunk into stage j % kStages (warp-collective; lane 0
 // drives the copies).  Waits, bounded, until every consumer warp has released
-// the stage's previous tile.  Returns false on a timeout.
-template <int HKV>
+// the stage's previous tile.  Returns false on a timeout.  The stage holds the
+// K and V boxes of KV heads g0 .. g0 + HC - 1 and every KV head's scales of
+// the tile's tokens, [token][num_kv_heads].
+template <int HC, int QW, int SCW, int DV>
+__device__ __forceinline__ void issue_boxes(const CUtensorMap* tk, const CUtensorMap* tv,
+                                            uint8_t* st, int g0, int64_t slot, uint64_t* bar,
+                                            uint64_t pol) {
+    using G = Geo<HC, QW, SCW, DV>;
+#pragma unroll
+    for (int g = 0; g < HC; ++g)
+#pragma unroll
+        for (int dv = 0; dv < DV; ++dv) {
+            const int x = ((g0 + g) * DV + dv) * D;
+            tma_load_2d(st + g * G::HEAD_TILE + dv * G::BOX, tk, x, (int)slot, bar, pol);
+            tma_load_2d(st + G::KV_TILE + g * G::HEAD_TILE + dv * G::BOX, tv, x, (int)slot, bar,
+                        pol);
+        }
+}
+
+template <int HC, int QW, int SCW, int DV>
 __device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMap* tk,
                                            const CUtensorMap* tv, uint8_t* stages, uint64_t* full,
                                            uint64_t* empty, int j, int n, int seq, int32_t off,
-                                           int t0, uint64_t pol, int lane) {
-    using G = Geo<HKV>;
+                                           int t0, int g0, uint64_t pol, int lane) {
+    using G = Geo<HC, QW, SCW, DV>;
     const int s = j % G::kStages;
     bool ok = true;
     if (lane == 0 && j >= G::kStages) ok = mbar_wait(&empty[s], ((j / G::kStages) - 1) & 1);
     ok = __shfl_sync(kFull, ok, 0);
     if (!ok) return false;
     const int ntok = min(T, n - j * T);
+    const int hkv = a.num_kv_heads;
     // a tile never crosses a page (pages are multiples of 128 tokens); a bad
     // page id is flagged and slot 0 read instead, so that the pipeline still
     // completes and nothing outside the pool is touched
@@ -172,41 +231,46 @@ __device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMa
         slot = 0;
     }
     uint8_t* st = stages + s * G::STAGE;
+    float* ks = reinterpret_cast<float*>(st + 2 * G::KV_TILE);
+    float* vs = reinterpret_cast<float*>(st + 2 * G::KV_TILE + G::SC_TILE);
     // the boxes always land whole (rows past the tensor are zero-filled)
     const uint32_t kvb = 2u * G::KV_TILE;
-    if (!a.row_scales) {
+    if (!a.row_scales && G::kBulkScales) {
         if (lane == 0) {
-            const uint32_t scb = (uint32_t)ntok * HKV * 4;
+            const uint32_t scb = (uint32_t)ntok * hkv * 4;
             mbar_arrive_expect_tx(&full[s], kvb + 2 * scb);
-#pragma unroll
-            for (int g = 0; g < HKV; ++g) {
-                tma_load_2d(st + g * G::HEAD_TILE, tk, g * D, (int)slot, &full[s], pol);
-                tma_load_2d(st + G::KV_TILE + g * G::HEAD_TILE, tv, g * D, (int)slot, &full[s], pol);
-            }
-            bulk_g2s_hint(st + 2 * G::KV_TILE, a.key_scales + slot * HKV, scb, &full[s], pol);
-            bulk_g2s_hint(st + 2 * G::KV_TILE + G::SC_TILE, a.val_scales + slot * HKV, scb, &full[s],
-                          pol);
+            issue_boxes<HC, QW, SCW, DV>(tk, tv, st, g0, slot, &full[s], pol);
+            bulk_g2s_hint(ks, a.key_scales + slot * hkv, scb, &full[s], pol);
+            bulk_g2s_hint(vs, a.val_scales + slot * hkv, scb, &full[s], pol);
+        }
+    } else if (!a.row_scales) {
+        // scale rows of 1 or 2 floats: no 16-byte alignment to rely on, so
+        // 4-byte cp.async copies, each lane's tracked by the stage barrier
+        // (registered before lane 0's arrive, which the __syncwarp orders)
+        const int nsc = ntok * hkv;
+        for (int i = lane; i < nsc; i += 32) {
+            cp_async_4(ks + i, a.key_scales + slot * hkv + i);
+            cp_async_4(vs + i, a.val_scales + slot * hkv + i);
+        }
+        cp_async_mbar_arrive(&full[s]);
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&full[s], kvb);
+            issue_boxes<HC, QW, SCW, DV>(tk, tv, st, g0, slot, &full[s], pol);
         }
     } else {
         // ROW scales: one fp32 per token, broadcast into the per-head tile
         // layout with plain loads; the arrive releases them to the consumers.
         if (lane == 0) {
             mbar_expect_tx(&full[s], kvb);
-#pragma unroll
-            for (int g = 0; g < HKV; ++g) {
-                tma_load_2d(st + g * G::HEAD_TILE, tk, g * D, (int)slot, &full[s], pol);
-                tma_load_2d(st + G::KV_TILE + g * G::HEAD_TILE, tv, g * D, (int)slot, &full[s], pol);
-            }
+            issue_boxes<HC, QW, SCW, DV>(tk, tv, st, g0, slot, &full[s], pol);
         }
-        float* ks = reinterpret_cast<float*>(st + 2 * G::KV_TILE);
-        float* vs = ks + T * HKV;
         for (int t = lane; t < ntok; t += 32) {
             const float kv = a.key_scales[slot + t];
             const float vv = a.val_scales[slot + t];
-#pragma unroll
-            for (int g = 0; g < HKV; ++g) {
-                ks[t * HKV + g] = kv;
-                vs[t * HKV + g] = vv;
+            for (int g = 0; g < hkv; ++g) {
+                ks[t * hkv + g] = kv;
+                vs[t * hkv + g] = vv;
             }
         }
         __syncwarp();
@@ -215,12 +279,14 @@ __device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMa
     return true;
 }
 
-template <int HKV, int GROUP>
-__global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
+template <int HC, int QW, int SCW, int DV>
+__global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SCW, DV>::kCtasPerSm)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const DecodeArgs a) {
-    using G = Geo<HKV>;
+    using G = Geo<HC, QW, SCW, DV>;
+    constexpr int DH = G::DH;
     constexpr int S = G::kStages;
+    constexpr int U = G::kUnits;
     extern __shared__ uint8_t smem_raw[];
     __shared__ int fail_flag;
     uint8_t* stages = reinterpret_cast<uint8_t*>(
@@ -229,35 +295,38 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
     uint64_t* bars = reinterpret_cast<uint64_t*>(stages + S * G::STAGE + G::PBUF);
     uint64_t* full = bars;                           // [S]        TMA -> warps
     uint64_t* empty = full + S;                      // [S]        warps -> producer
-    uint64_t* p_full = empty + S;                    // [HKV][kPBufs]  QK -> PV
-    uint64_t* p_empty = p_full + HKV * kPBufs;       // [HKV][kPBufs]  PV -> QK
+    uint64_t* p_full = empty + S;                    // [U][kPBufs]  QK -> PV
+    uint64_t* p_empty = p_full + U * kPBufs;         // [U][kPBufs]  PV -> QK
 
-    const int seq = blockIdx.y;
-    const int chunk = blockIdx.x;
+    const int g0 = blockIdx.x * HC;                  // first KV head of this CTA
+    const int chunk = blockIdx.y;
+    const int seq = blockIdx.z;
     const bool direct = a.max_chunks == 1;
     pdl_wait();  // the append before this kernel writes the lengths and the codes
     pdl_trigger();
     int32_t off, cap, len;
     if (!load_entry(a, seq, off, cap, len)) {
-        if (chunk == 0 && threadIdx.x == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
+        if (chunk == 0 && blockIdx.x == 0 && threadIdx.x == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
         return;
     }
     const int t0 = chunk * a.chunk_tokens;
     if (t0 >= len) {
-        if (direct && chunk == 0) write_empty(a, seq);
+        if (direct && chunk == 0 && blockIdx.x == 0) write_empty(a, seq);
         return;
     }
     const int n = min(a.chunk_tokens, len - t0);
     const int ntiles = (n + T - 1) / T;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int hkv = a.num_kv_heads;
+    const int group = a.num_heads / hkv;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], G::kWarps);
         }
-        for (int i = 0; i < HKV * kPBufs; ++i) {
+        for (int i = 0; i < U * kPBufs; ++i) {
             mbar_init(&p_full[i], 1);
             mbar_init(&p_empty[i], 1);
         }
@@ -272,7 +341,8 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
         // has released it, independent of the consumers' own progress.
         const uint64_t pol = l2_policy_evict_first();
         for (int j = 0; j < ntiles; ++j) {
-            if (!issue_tile<HKV>(a, &tmap_k, &tmap_v, stages, full, empty, j, n, seq, off, t0, pol, lane)) {
+            if (!issue_tile<HC, QW, SCW, DV>(a, &tmap_k, &tmap_v, stages, full, empty, j, n, seq,
+                                             off, t0, g0, pol, lane)) {
                 if (lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
                 break;
             }
@@ -280,41 +350,47 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
         return;
     }
 
-    const bool is_qk = warp < HKV;
-    const int g = is_qk ? warp : warp - HKV;        // KV head of this warp
+    const bool is_qk = warp < U;
+    const int u = is_qk ? warp : warp - U;           // unit of this warp
+    const int gl = u / QW;                           // KV head within the CTA
+    const int gkv = g0 + gl;                         // KV head in the cache row
+    const int jb = 4 * (u % QW);                     // first query head of the quad in the group
     const int gid = lane >> 2;
     const int t4 = lane & 3;
-    const bool head_live = t4 < GROUP;              // accumulator columns belong to head t4
-    float* pslots = pbuf + g * kPBufs * G::PSLOT;
+    const bool head_live = jb + t4 < group;          // accumulator columns belong to head jb + t4
+    float* pslots = pbuf + u * kPBufs * G::PSLOT;
     bool failed = false;
-    // merge area (reused stage memory) for the final (m, l, O) per head
-    float* mo = reinterpret_cast<float*>(stages);    // [HKV][GROUP][128]
-    float* mm = mo + HKV * GROUP * D;                // [HKV][GROUP]
-    float* ml = mm + HKV * GROUP;                    // [HKV][GROUP]
+    // merge area (reused stage memory) for the final (m, l, O) per head slot
+    float* mo = reinterpret_cast<float*>(stages);    // [U][4][head_dim]
+    float* mm = mo + U * 4 * DH;                     // [U][4]
+    float* ml = mm + U * 4;                          // [U][4]
 
     if (is_qk) {
         // ================================================================ QK
-        // q as B fragments: column n = gid <-> (head gid >> 1, digit), thread
-        // t4 holds dims [32*t4, 32*t4 + 32), k-step j covers 8 of them.
-        uint32_t b_hi[4][2], b_lo[4][2];
+        // q as B fragments: column n = gid <-> (head jb + (gid >> 1), digit),
+        // thread t4 holds dims [32*t4, 32*t4 + 32) of every 128-dim block,
+        // k-step j covers 8 of them (block j / 4).
+        uint32_t b_hi[4 * DV][2], b_lo[4 * DV][2];
         float sq_own;
         {
             const int hq = gid >> 1;
-            const bool live = hq < GROUP;
+            const bool live = jb + hq < group;
+            // a quad past the group's end (groups that are not a multiple of
+            // 4) reads query head 0 of the group and keeps no column live
             const float* qp =
-                a.q + ((size_t)seq * a.num_heads + g + HKV * (live ? hq : 0)) * D + 32 * t4;
-            float qv[32];
+                a.q + ((size_t)seq * a.num_heads + gkv + hkv * (live ? jb + hq : 0)) * DH + 32 * t4;
+            auto scaled = [&](float v) { return __fmul_rn(__fmul_rn(v, a.q_mul), kLog2e); };
+            // the head's absmax over all its blocks (first pass), then the
+            // digits block by block (second pass, the loads hit L1)
             float amax = 0.0f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float4 v = reinterpret_cast<const float4*>(qp)[e];
-                qv[4 * e + 0] = __fmul_rn(__fmul_rn(v.x, a.q_mul), kLog2e);
-                qv[4 * e + 1] = __fmul_rn(__fmul_rn(v.y, a.q_mul), kLog2e);
-                qv[4 * e + 2] = __fmul_rn(__fmul_rn(v.z, a.q_mul), kLog2e);
-                qv[4 * e + 3] = __fmul_rn(__fmul_rn(v.w, a.q_mul), kLog2e);
-            }
+            for (int dv = 0; dv < DV; ++dv)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(qv[e]));
+                for (int e = 0; e < 8; ++e) {
+                    const float4 v = reinterpret_cast<const float4*>(qp + dv * D)[e];
+                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(scaled(v.x)), fabsf(scaled(v.y))),
+                                             fmaxf(fabsf(scaled(v.z)), fabsf(scaled(v.w)))));
+                }
             amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
             amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
             const float kQMax = 8323072.0f;  // 2^23 - 2^16 keeps d0 in [-128, 127]
@@ -322,62 +398,80 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
             sq_own = amax > 0.0f ? __fdiv_rn(amax, kQMax) : 0.0f;
             const bool odd = gid & 1;
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int dv = 0; dv < DV; ++dv) {
+                float qv[32];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-                    for (int x = 0; x < 4; ++x) {
-                        const int qi = __float2int_rn(qv[8 * j + 4 * half + x] * inv);
-                        const uint32_t d0 = (uint32_t)(qi >> 16) & 0xffu;
-                        const uint32_t r = (uint32_t)qi & 0xffffu;
-                        const uint32_t dl = odd ? (r & 0xffu) : (r >> 8);
-                        w0 |= (live && !odd ? d0 : 0u) << (8 * x);
-                        w1 |= (live ? dl : 0u) << (8 * x);
-                    }
-                    b_hi[j][half] = w0;
-                    b_lo[j][half] = w1;
+                for (int e = 0; e < 8; ++e) {
+                    const float4 v = reinterpret_cast<const float4*>(qp + dv * D)[e];
+                    qv[4 * e + 0] = scaled(v.x);
+                    qv[4 * e + 1] = scaled(v.y);
+                    qv[4 * e + 2] = scaled(v.z);
+                    qv[4 * e + 3] = scaled(v.w);
                 }
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+                        for (int x = 0; x < 4; ++x) {
+                            const int qi = __float2int_rn(qv[8 * j + 4 * half + x] * inv);
+                            const uint32_t d0 = (uint32_t)(qi >> 16) & 0xffu;
+                            const uint32_t r = (uint32_t)qi & 0xffffu;
+                            const uint32_t dl = odd ? (r & 0xffu) : (r >> 8);
+                            w0 |= (live && !odd ? d0 : 0u) << (8 * x);
+                            w1 |= (live ? dl : 0u) << (8 * x);
+                        }
+                        b_hi[4 * dv + j][half] = w0;
+                        b_lo[4 * dv + j][half] = w1;
+                    }
+            }
         }
         const float sq = __shfl_sync(kFull, sq_own, (2 * t4) << 2);
         const float c16 = 65536.0f * sq, c8 = 256.0f * sq;
-        float m_run = -INFINITY;      // running max of head t4 (log2 units)
-        float l_part = 0.0f;          // this thread's share of head t4's sum
+        float m_run = -INFINITY;      // running max of head jb + t4 (log2 units)
+        float l_part = 0.0f;          // this thread's share of that head's sum
 
         for (int i = 0; i < ntiles; ++i) {
             const int s = i % S;
             const int b = i % kPBufs;
             if (!warp_wait(&full[s], (i / S) & 1)) { failed = true; break; }
             const uint8_t* st = stages + s * G::STAGE;
-            const uint8_t* kt = st + g * G::HEAD_TILE;
+            const uint8_t* kt = st + gl * G::HEAD_TILE;
             const float* kst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE);
-            const float* vst = kst + T * HKV;
+            const float* vst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE + G::SC_TILE);
             const int valid = n - i * T;
 
-            float sc[4];   // tokens gid, gid+8, 16+gid, 24+gid of head t4
+            float sc[4];   // tokens gid, gid+8, 16+gid, 24+gid of head jb + t4
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
                 const int ra = mt * 16 + gid, rb = ra + 8;
-                const uint4 a00 = *reinterpret_cast<const uint4*>(kt + swz(ra, 2 * t4));
-                const uint4 a01 = *reinterpret_cast<const uint4*>(kt + swz(ra, 2 * t4 + 1));
-                const uint4 a10 = *reinterpret_cast<const uint4*>(kt + swz(rb, 2 * t4));
-                const uint4 a11 = *reinterpret_cast<const uint4*>(kt + swz(rb, 2 * t4 + 1));
-                const uint32_t w0[8] = {a00.x, a00.y, a00.z, a00.w, a01.x, a01.y, a01.z, a01.w};
-                const uint32_t w1[8] = {a10.x, a10.y, a10.z, a10.w, a11.x, a11.y, a11.z, a11.w};
                 int hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    mma_s8s8(hi, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1], b_hi[j][0], b_hi[j][1]);
-                    mma_s8u8(lo, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1], b_lo[j][0], b_lo[j][1]);
+                for (int dv = 0; dv < DV; ++dv) {
+                    const uint8_t* kb = kt + dv * G::BOX;
+                    const uint4 a00 = *reinterpret_cast<const uint4*>(kb + swz(ra, 2 * t4));
+                    const uint4 a01 = *reinterpret_cast<const uint4*>(kb + swz(ra, 2 * t4 + 1));
+                    const uint4 a10 = *reinterpret_cast<const uint4*>(kb + swz(rb, 2 * t4));
+                    const uint4 a11 = *reinterpret_cast<const uint4*>(kb + swz(rb, 2 * t4 + 1));
+                    const uint32_t w0[8] = {a00.x, a00.y, a00.z, a00.w, a01.x, a01.y, a01.z, a01.w};
+                    const uint32_t w1[8] = {a10.x, a10.y, a10.z, a10.w, a11.x, a11.y, a11.z, a11.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        mma_s8s8(hi, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1],
+                                 b_hi[4 * dv + j][0], b_hi[4 * dv + j][1]);
+                        mma_s8u8(lo, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1],
+                                 b_lo[4 * dv + j][0], b_lo[4 * dv + j][1]);
+                    }
                 }
                 // accumulator (row, col): [0] (ra, 2*t4) [1] (ra, 2*t4+1) [2]/[3] row rb
                 const float sa = fmaf((float)hi[0], c16, fmaf((float)lo[0], c8, (float)lo[1] * sq));
                 const float sb = fmaf((float)hi[2], c16, fmaf((float)lo[2], c8, (float)lo[3] * sq));
-                sc[2 * mt] = (head_live && ra < valid) ? sa * kst[ra * HKV + g] : -INFINITY;
-                sc[2 * mt + 1] = (head_live && rb < valid) ? sb * kst[rb * HKV + g] : -INFINITY;
+                sc[2 * mt] = (head_live && ra < valid) ? sa * kst[ra * hkv + gkv] : -INFINITY;
+                sc[2 * mt + 1] = (head_live && rb < valid) ? sb * kst[rb * hkv + gkv] : -INFINITY;
             }
 
-            // online softmax of head t4, base 2, lazy rescale
+            // online softmax of head jb + t4, base 2, lazy rescale
             float tm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
             tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 4));
             tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 8));
@@ -395,7 +489,7 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
                 l_part += p[e];
             }
 
-            if (i >= kPBufs && !warp_wait(&p_empty[g * kPBufs + b], ((i / kPBufs) - 1) & 1)) {
+            if (i >= kPBufs && !warp_wait(&p_empty[u * kPBufs + b], ((i / kPBufs) - 1) & 1)) {
                 failed = true;
                 break;
             }
@@ -404,13 +498,13 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int tok = (e >> 1) * 16 + (e & 1) * 8 + gid;
-                    pw[t4 * T + tok] = p[e] == 0.0f ? 0.0f : p[e] * vst[tok * HKV + g];
+                    pw[t4 * T + tok] = p[e] == 0.0f ? 0.0f : p[e] * vst[tok * hkv + gkv];
                 }
                 if (gid == 0) pw[4 * T + t4] = corr;
             }
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&p_full[g * kPBufs + b]);
+                mbar_arrive(&p_full[u * kPBufs + b]);
                 mbar_arrive(&empty[s]);
             }
         }
@@ -421,25 +515,25 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
         if (failed) {
             if (lane == 0) fail_flag = 1;
         } else if (gid == 0 && head_live) {
-            mm[g * GROUP + t4] = m_run;
-            ml[g * GROUP + t4] = l_part;
+            mm[u * 4 + t4] = m_run;
+            ml[u * 4 + t4] = l_part;
         }
     } else {
         // ================================================================ PV
         // O^T[dim][col] += V^T[dim][token] . P[token][col], col = (head, digit)
-        float acc[8][2];   // head t4, dims 16*mt + gid (+8)
+        float acc[8 * DV][2];   // head jb + t4, dims 16*mt + gid (+8)
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = 0.0f;
-        const int hp = gid >> 1;           // head whose p' digits this thread supplies
-        const bool p_live = hp < GROUP;
+        for (int mt = 0; mt < 8 * DV; ++mt) acc[mt][0] = acc[mt][1] = 0.0f;
+        const int hp = gid >> 1;           // head (in the quad) whose p' digits this thread supplies
+        const bool p_live = jb + hp < group;
         const bool lo_digit = gid & 1;
 
         for (int i = 0; i < ntiles; ++i) {
             const int s = i % S;
             const int b = i % kPBufs;
-            if (!warp_wait(&p_full[g * kPBufs + b], (i / kPBufs) & 1)) { failed = true; break; }
+            if (!warp_wait(&p_full[u * kPBufs + b], (i / kPBufs) & 1)) { failed = true; break; }
             if (!warp_wait(&full[s], (i / S) & 1)) { failed = true; break; }
-            const uint8_t* vt = stages + s * G::STAGE + G::KV_TILE + g * G::HEAD_TILE;
+            const uint8_t* vt = stages + s * G::STAGE + G::KV_TILE + gl * G::HEAD_TILE;
             const float* pw = pslots + b * G::PSLOT;
 
             // p' digits as B fragments: tokens 4*t4.. (b0) and 16 + 4*t4.. (b1)
@@ -480,18 +574,19 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
             if (head_live) corr = pw[4 * T + t4];
             if (__any_sync(kFull, corr != 1.0f)) {
 #pragma unroll
-                for (int mt = 0; mt < 8; ++mt) {
+                for (int mt = 0; mt < 8 * DV; ++mt) {
                     acc[mt][0] *= corr;
                     acc[mt][1] *= corr;
                 }
             }
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
+            for (int mt = 0; mt < 8 * DV; ++mt) {
                 // 16x16 blocks of V (tokens x dims 16*mt..): rows from lanes 0-15
                 const int r = lane & 15;
+                const uint8_t* vb = vt + (mt >> 3) * G::BOX;
                 uint32_t x0, x1, y0, y1;
-                ldmatrix_t_b8(x0, x1, vt + swz(r, mt));
-                ldmatrix_t_b8(y0, y1, vt + swz(16 + r, mt));
+                ldmatrix_t_b8(x0, x1, vb + swz(r, mt & 7));
+                ldmatrix_t_b8(y0, y1, vb + swz(16 + r, mt & 7));
                 int d[4] = {0, 0, 0, 0};
                 mma_s8u8(d, x0, x1, y0, y1, bw0, bw1);
                 // d: (dim 16mt+gid, col 2t4 = hi digit of head t4), (.., lo), rows +8
@@ -500,7 +595,7 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
             }
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&p_empty[g * kPBufs + b]);
+                mbar_arrive(&p_empty[u * kPBufs + b]);
                 mbar_arrive(&empty[s]);
             }
         }
@@ -509,9 +604,9 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
             if (lane == 0) fail_flag = 1;
         } else if (head_live) {
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-                mo[(g * GROUP + t4) * D + 16 * mt + gid] = acc[mt][0];
-                mo[(g * GROUP + t4) * D + 16 * mt + gid + 8] = acc[mt][1];
+            for (int mt = 0; mt < 8 * DV; ++mt) {
+                mo[(u * 4 + t4) * DH + 16 * mt + gid] = acc[mt][0];
+                mo[(u * 4 + t4) * DH + 16 * mt + gid + 8] = acc[mt][1];
             }
         }
     }
@@ -520,16 +615,18 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
 
     // ---- write the chunk's state (or the final output when unsplit)
     const int H = a.num_heads;
-    for (int o = threadIdx.x; o < HKV * GROUP * D; o += G::kConsumerThreads) {
-        const int d = o % D;
-        const int hl = o / D;                 // g2 * GROUP + j
-        const int g2 = hl / GROUP, j = hl % GROUP;
+    for (int o = threadIdx.x; o < U * 4 * DH; o += G::kConsumerThreads) {
+        const int d = o % DH;
+        const int hl = o / DH;                // u2 * 4 + quad slot
+        const int u2 = hl >> 2;
+        const int j = 4 * (u2 % QW) + (hl & 3);
+        if (j >= group) continue;
+        const int h = (g0 + u2 / QW) + hkv * j;
         const float M = mm[hl];
-        const float so = mo[hl * D + d];
+        const float so = mo[hl * DH + d];
         const float sl = ml[hl];
-        const int h = g2 + HKV * j;
         if (direct) {
-            const size_t oi = ((size_t)seq * H + h) * D + d;
+            const size_t oi = ((size_t)seq * H + h) * DH + d;
             if (a.mode == kOut) {
                 a.out[oi] = __fdiv_rn(so, sl);
             } else {
@@ -541,7 +638,7 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
             }
         } else {
             const size_t pidx = ((size_t)seq * a.max_chunks + chunk) * H + h;
-            a.part_o[pidx * D + d] = so;
+            a.part_o[pidx * DH + d] = so;
             if (d == 0) {
                 a.part_ml[pidx * 2] = M;
                 a.part_ml[pidx * 2 + 1] = sl;
@@ -553,10 +650,13 @@ __global__ void __launch_bounds__(Geo<HKV>::kThreads, Geo<HKV>::kCtasPerSm)
 // Merges the chunk partials of one (sequence, head).  4 warps per dim group:
 // the chunk weights 2^(m_c - M) are computed once into shared memory, then
 // each of kCombineSplit thread groups sums a quarter of the chunks for every
-// dim (independent loads, so a long chunk list is not one serial chain).
+// dim (independent loads, so a long chunk list is not one serial chain).  A
+// thread covers dim d of each of the head's DV 128-dim blocks.
 constexpr int kCombineSplit = 4;
 static_assert(D * kCombineSplit >= 256, "one thread per chunk: the plan allows 256 chunks");
+template <int DV>
 __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const DecodeArgs a) {
+    constexpr int DH = D * DV;
     const int seq = blockIdx.x, h = blockIdx.y;
     const int d = threadIdx.x % D, part = threadIdx.x / D;
     const int H = a.num_heads;
@@ -566,7 +666,7 @@ __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const Decode
     if (!load_entry(a, seq, off, cap, len)) return;  // flagged by decode_kernel
     const int nch = (len + a.chunk_tokens - 1) / a.chunk_tokens;
     const size_t base = (size_t)seq * a.max_chunks * H + h;
-    __shared__ float s_f[256], s_l[256], s_red[D * kCombineSplit];
+    __shared__ float s_f[256], s_l[256], s_red[DH * kCombineSplit];
     __shared__ float s_M;
     // chunk maxima -> M (the plan keeps nch <= 256 < the block's threads, so
     // thread c holds chunk c's (m, l) from the one load)
@@ -591,64 +691,99 @@ __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const Decode
         s_l[threadIdx.x] = f * mlc.y;
     }
     __syncthreads();
-    float so = 0.0f;
+    float so[DV];
+#pragma unroll
+    for (int dv = 0; dv < DV; ++dv) so[dv] = 0.0f;
 #pragma unroll 4
-    for (int c = part; c < nch; c += kCombineSplit)
-        so += s_f[c] * a.part_o[(base + (size_t)c * H) * D + d];
-    s_red[part * D + d] = so;
+    for (int c = part; c < nch; c += kCombineSplit) {
+        const float* po = a.part_o + (base + (size_t)c * H) * DH + d;
+#pragma unroll
+        for (int dv = 0; dv < DV; ++dv) so[dv] += s_f[c] * po[dv * D];
+    }
+#pragma unroll
+    for (int dv = 0; dv < DV; ++dv) s_red[part * DH + dv * D + d] = so[dv];
     __syncthreads();
     if (part != 0) return;
-    so = 0.0f;
-#pragma unroll
-    for (int q = 0; q < kCombineSplit; ++q) so += s_red[q * D + d];
     float sl = 0.0f;
     for (int c = 0; c < nch; ++c) sl += s_l[c];
-    const size_t oi = ((size_t)seq * H + h) * D + d;
-    if (a.mode == kOut) {
-        a.out[oi] = nch ? __fdiv_rn(so, sl) : 0.0f;
-    } else {
-        a.out[oi] = so;
-        if (d == 0) {
-            a.out_ml[((size_t)seq * H + h) * 2] = nch ? M : -INFINITY;
-            a.out_ml[((size_t)seq * H + h) * 2 + 1] = sl;
+#pragma unroll
+    for (int dv = 0; dv < DV; ++dv) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kCombineSplit; ++q) sum += s_red[q * DH + dv * D + d];
+        const size_t oi = ((size_t)seq * H + h) * DH + dv * D + d;
+        if (a.mode == kOut) {
+            a.out[oi] = nch ? __fdiv_rn(sum, sl) : 0.0f;
+        } else {
+            a.out[oi] = sum;
+            if (d == 0 && dv == 0) {
+                a.out_ml[((size_t)seq * H + h) * 2] = nch ? M : -INFINITY;
+                a.out_ml[((size_t)seq * H + h) * 2 + 1] = sl;
+            }
         }
     }
 }
 
-// Merges num_parts partial states stacked [part][seq][head] (context shards).
+// Merges num_parts partial states stacked [part][seq][head] (context shards);
+// one thread per dim of each 128-dim block of the head.
+template <int DV>
 __global__ void __launch_bounds__(D) lse_merge_kernel(const float* __restrict__ part_o,
                                                       const float* __restrict__ part_ml,
                                                       int num_parts, int num_seqs, int H,
                                                       float* __restrict__ out) {
+    constexpr int DH = D * DV;
     const int seq = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
     const size_t stride = (size_t)num_seqs * H;
     const size_t sh = (size_t)seq * H + h;
     float M = -INFINITY;
     for (int p = 0; p < num_parts; ++p) M = fmaxf(M, part_ml[(p * stride + sh) * 2]);
-    float so = 0.0f, sl = 0.0f;
+    float so[DV], sl = 0.0f;
+#pragma unroll
+    for (int dv = 0; dv < DV; ++dv) so[dv] = 0.0f;
     for (int p = 0; p < num_parts; ++p) {
         const size_t i = p * stride + sh;
         const float mp = part_ml[i * 2];
         const float f = mp == -INFINITY ? 0.0f : exp2f(mp - M);
-        so += f * part_o[i * D + d];
+#pragma unroll
+        for (int dv = 0; dv < DV; ++dv) so[dv] += f * part_o[i * DH + dv * D + d];
         sl += f * part_ml[i * 2 + 1];
     }
-    out[sh * D + d] = sl > 0.0f ? __fdiv_rn(so, sl) : 0.0f;
+#pragma unroll
+    for (int dv = 0; dv < DV; ++dv)
+        out[sh * DH + dv * D + d] = sl > 0.0f ? __fdiv_rn(so[dv], sl) : 0.0f;
 }
 
-template <int HKV, int GROUP>
+template <int HC, int QW, int SCW, int DV>
 cudaError_t launch_decode_t(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t st) {
-    using G = Geo<HKV>;
+    using G = Geo<HC, QW, SCW, DV>;
     static std::atomic<unsigned long long> attr_done{0};
-    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(decode_kernel<HKV, GROUP>),
+    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(decode_kernel<HC, QW, SCW, DV>),
                                       G::SMEM, attr_done);
     if (e != cudaSuccess) return e;
     CUtensorMap mk, mv;
-    if ((e = make_code_map(&mk, a.keys, HKV, a.total_slots, T)) != cudaSuccess) return e;
-    if ((e = make_code_map(&mv, a.values, HKV, a.total_slots, T)) != cudaSuccess) return e;
-    dim3 grid(plan.max_chunks, a.num_seqs);
-    return launch_pdl(decode_kernel<HKV, GROUP>, grid, dim3(G::kThreads), G::SMEM, st, mk, mv, a);
+    const int hkv = a.num_kv_heads;
+    // a row of the code tensor is hkv * DV 128-byte blocks
+    if ((e = make_code_map(&mk, a.keys, hkv * DV, a.total_slots, T)) != cudaSuccess) return e;
+    if ((e = make_code_map(&mv, a.values, hkv * DV, a.total_slots, T)) != cudaSuccess) return e;
+    // head blocks fastest, so that the CTAs sharing a chunk's scale rows run together
+    dim3 grid(hkv / HC, plan.max_chunks, a.num_seqs);
+    return launch_pdl(decode_kernel<HC, QW, SCW, DV>, grid, dim3(G::kThreads), G::SMEM, st, mk, mv,
+                      a);
 }
+
+// Every compiled (HC, QW, SCW, DV): for num_kv_heads 1, 2, 4, 8 (SCW), query
+// groups up to 4, 8, 16, 32 (QW = 1, 2, 4, 8) and head_dim 128 * DV, the CTA
+// covers HC KV heads: all of them for groups up to 4 at head_dim 128 (at most
+// two at 256), else as many as keep it at 4 units (8 for the largest groups).
+#define EC_DECODE_VARIANTS(X)                                                     \
+    X(1, 1, 1, 1) X(2, 1, 2, 1) X(4, 1, 4, 1) X(8, 1, 8, 1)                       \
+    X(1, 2, 1, 1) X(2, 2, 2, 1) X(2, 2, 4, 1) X(2, 2, 8, 1)                       \
+    X(1, 4, 1, 1) X(1, 4, 2, 1) X(1, 4, 4, 1) X(1, 4, 8, 1)                       \
+    X(1, 8, 1, 1) X(1, 8, 2, 1) X(1, 8, 4, 1) X(1, 8, 8, 1)                       \
+    X(1, 1, 1, 2) X(2, 1, 2, 2) X(2, 1, 4, 2) X(2, 1, 8, 2)                       \
+    X(1, 2, 1, 2) X(1, 2, 2, 2) X(1, 2, 4, 2) X(1, 2, 8, 2)                       \
+    X(1, 4, 1, 2) X(1, 4, 2, 2) X(1, 4, 4, 2) X(1, 4, 8, 2)                       \
+    X(1, 8, 1, 2) X(1, 8, 2, 2) X(1, 8, 4, 2) X(1, 8, 8, 2)
 
 }  // namespace
 
@@ -703,8 +838,31 @@ cudaError_t make_f32_row_map(CUtensorMap* m, const float* base, int hkv, uint64_
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens) {
-    const int slots = num_sms * kDecodeCtasPerSm;  // resident CTAs (exact for HKV <= 4)
+DecodeVariant decode_variant(int num_kv_heads, int group, int head_dim) {
+    DecodeVariant none{0, 0, 0, 0, 0};
+    if (group < 1 || group > 32 || (head_dim != 128 && head_dim != 256)) return none;
+    if (num_kv_heads != 1 && num_kv_heads != 2 && num_kv_heads != 4 && num_kv_heads != 8)
+        return none;
+    const int dv = head_dim / 128;
+    const int qw = group <= 4 ? 1 : group <= 8 ? 2 : group <= 16 ? 4 : 8;
+    // KV heads per CTA: every head for groups up to 4 (at most two of 256
+    // dims), two for groups up to 8 (one of 256 dims), else one
+    const int hc_cap = qw == 1 ? (dv == 1 ? 8 : 2) : qw == 2 ? (dv == 1 ? 2 : 1) : 1;
+    const int hc = num_kv_heads < hc_cap ? num_kv_heads : hc_cap;
+#define EC_VARIANT(HC_, QW_, SCW_, DV_)                                           \
+    if (hc == HC_ && qw == QW_ && num_kv_heads == SCW_ && dv == DV_)              \
+        return DecodeVariant{HC_, QW_, SCW_, DV_, Geo<HC_, QW_, SCW_, DV_>::kCtasPerSm};
+    EC_DECODE_VARIANTS(EC_VARIANT)
+#undef EC_VARIANT
+    return none;
+}
+
+DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens,
+                       int num_kv_heads, int num_heads, int head_dim) {
+    const DecodeVariant v = num_kv_heads > 0
+        ? decode_variant(num_kv_heads, num_heads / num_kv_heads, head_dim) : DecodeVariant{};
+    const int slots = num_sms * (v.hc ? v.ctas_per_sm : 2);   // resident CTAs
+    const int hblocks = v.hc ? num_kv_heads / v.hc : 1;       // CTAs per (sequence, chunk)
     DecodePlan best{T, 1};
     if (max_seq_len <= 0 || num_seqs <= 0) return best;
     const int tiles = (max_seq_len + T - 1) / T;
@@ -717,10 +875,10 @@ DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t tota
     for (int k = 1; k <= kmax; ++k) {
         const int chunk = ((tiles + k - 1) / k) * T;
         const int kk = (max_seq_len + chunk - 1) / chunk;
-        const long long ctas = (long long)num_seqs * kk;
+        const long long ctas = (long long)num_seqs * kk * hblocks;
         long long busy = ctas;
         if (ragged) {
-            const double est = (double)total_tokens / chunk + 0.5 * num_seqs;
+            const double est = ((double)total_tokens / chunk + 0.5 * num_seqs) * hblocks;
             busy = est < (double)ctas ? (long long)est + 1 : ctas;
         }
         const long long waves = (busy + slots - 1) / slots;
@@ -736,9 +894,9 @@ DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t tota
     return best;
 }
 
-size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads) {
+size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads, int head_dim) {
     if (p.max_chunks <= 1) return 0;
-    return (size_t)num_seqs * p.max_chunks * num_heads * (D + 2) * sizeof(float);
+    return (size_t)num_seqs * p.max_chunks * num_heads * (head_dim + 2) * sizeof(float);
 }
 
 cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan, void* ws,
@@ -747,22 +905,33 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
     a.max_chunks = plan.max_chunks;
     if (plan.max_chunks > 1) {
         a.part_o = static_cast<float*>(ws);
-        a.part_ml = a.part_o + (size_t)a.num_seqs * plan.max_chunks * a.num_heads * D;
+        a.part_ml = a.part_o + (size_t)a.num_seqs * plan.max_chunks * a.num_heads * a.head_dim;
     }
-    const int group = a.num_heads / num_kv_heads;
+    a.num_kv_heads = num_kv_heads;
+    const DecodeVariant v = decode_variant(num_kv_heads, a.num_heads / num_kv_heads, a.head_dim);
+    if (!v.hc || a.num_heads % num_kv_heads) return cudaErrorInvalidValue;
     cudaError_t e = cudaErrorInvalidValue;
-#define EC_DEC(H, GR) \
-    if (num_kv_heads == H && group == GR) e = launch_decode_t<H, GR>(a, plan, st);
-    EC_DEC(4, 4) EC_DEC(4, 2) EC_DEC(4, 1) EC_DEC(8, 4) EC_DEC(8, 2) EC_DEC(8, 1)
+#define EC_DEC(HC_, QW_, SCW_, DV_)                                               \
+    if (v.hc == HC_ && v.qw == QW_ && v.scw == SCW_ && v.dv == DV_)               \
+        e = launch_decode_t<HC_, QW_, SCW_, DV_>(a, plan, st);
+    EC_DECODE_VARIANTS(EC_DEC)
 #undef EC_DEC
     if (e != cudaSuccess || plan.max_chunks <= 1) return e;
-    return launch_pdl(combine_kernel, dim3(a.num_seqs, a.num_heads), dim3(D * kCombineSplit), 0, st, a);
+    const dim3 cg(a.num_seqs, a.num_heads), cb(D * kCombineSplit);
+    return v.dv == 1 ? launch_pdl(combine_kernel<1>, cg, cb, 0, st, a)
+                     : launch_pdl(combine_kernel<2>, cg, cb, 0, st, a);
 }
 
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
-                               int num_seqs, int num_heads, float* out, cudaStream_t st) {
-    lse_merge_kernel<<<dim3(num_seqs, num_heads), D, 0, st>>>(part_o, part_ml, num_parts, num_seqs,
-                                                              num_heads, out);
+                               int num_seqs, int num_heads, int head_dim, float* out,
+                               cudaStream_t st) {
+    const dim3 grid(num_seqs, num_heads);
+    if (head_dim == 128)
+        lse_merge_kernel<1><<<grid, D, 0, st>>>(part_o, part_ml, num_parts, num_seqs, num_heads, out);
+    else if (head_dim == 256)
+        lse_merge_kernel<2><<<grid, D, 0, st>>>(part_o, part_ml, num_parts, num_seqs, num_heads, out);
+    else
+        return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
 

@@ -301,7 +301,7 @@ cudaError_t launch_decode_f32(const float* keys, const float* values, int num_kv
 #undef EC_F32_CASE
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return launch_lse_combine(part_o, part_ml, chunks, 1, num_heads, out, st);
+    return launch_lse_combine(part_o, part_ml, chunks, 1, num_heads, 128, out, st);
 }
 
 }  // namespace ec

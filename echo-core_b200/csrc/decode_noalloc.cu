@@ -111,8 +111,10 @@ int ec_decode_attention_noalloc(const ec_kv_batch* b, const float* q, float* out
     if (dev < 0 || dev >= kMaxDevices) return reject(EC_ERR_UNSUPPORTED, "device ordinal >= 64");
 
     const ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, sms,
-                                                b->total_tokens_hint);
-    const size_t need = ec::decode_workspace_bytes(plan, (int)b->num_seqs, (int)num_heads);
+                                                b->total_tokens_hint, (int)hkv, (int)num_heads,
+                                                (int)b->head_dim);
+    const size_t need = ec::decode_workspace_bytes(plan, (int)b->num_seqs, (int)num_heads,
+                                                   (int)b->head_dim);
     if (need > kNoAllocScratchBytes) {
         char msg[200];
         snprintf(msg, sizeof(msg),
@@ -140,6 +142,7 @@ int ec_decode_attention_noalloc(const ec_kv_batch* b, const float* q, float* out
     a.q_mul = softmax_scale;
     a.num_seqs = (int)b->num_seqs;
     a.num_heads = (int)num_heads;
+    a.head_dim = (int)b->head_dim;
     a.row_scales = b->scale_mode == EC_SCALE_ROW;
     a.mode = ec::kOut;
     e = ec::launch_decode(a, (int)hkv, plan, scratch, reinterpret_cast<cudaStream_t>(stream));

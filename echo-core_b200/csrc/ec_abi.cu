@@ -55,11 +55,9 @@ cudaStream_t as_stream(ec_stream_t s) { return reinterpret_cast<cudaStream_t>(s)
 int ec::set_last_error(int status, const char* msg) { return fail(status, "%s", msg); }
 
 bool ec::decode_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim) {
-    if (head_dim != 128) return false;
-    if (num_kv_heads != 4 && num_kv_heads != 8) return false;
-    if (num_heads == 0 || num_heads % num_kv_heads) return false;
-    const uint32_t g = num_heads / num_kv_heads;
-    return g == 1 || g == 2 || g == 4;
+    if ((head_dim != 128 && head_dim != 256) || num_kv_heads == 0 || num_kv_heads > 8) return false;
+    if (num_heads == 0 || num_heads % num_kv_heads || num_heads / num_kv_heads > 32) return false;
+    return ec::decode_variant((int)num_kv_heads, (int)(num_heads / num_kv_heads), (int)head_dim).hc != 0;
 }
 
 using ec::decode_shape_supported;
@@ -210,8 +208,9 @@ int ec_kv_cache_create(const ec_model_config* config, int scale_mode, ec_kv_cach
     }
     if (c.use_kv_quantization && c.num_layers > 0 &&
         decode_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim)) {
-        kc->plan = ec::plan_decode(1, (int)c.max_seq_len, num_sms_current());
-        kc->ws_bytes = ec::decode_workspace_bytes(kc->plan, 1, (int)c.num_heads);
+        kc->plan = ec::plan_decode(1, (int)c.max_seq_len, num_sms_current(), 0,
+                                   (int)c.num_kv_heads, (int)c.num_heads, (int)c.head_dim);
+        kc->ws_bytes = ec::decode_workspace_bytes(kc->plan, 1, (int)c.num_heads, (int)c.head_dim);
         if (kc->ws_bytes) {
             cudaError_t e = cudaMalloc(&kc->ws, kc->ws_bytes);
             if (e != cudaSuccess) {
@@ -265,7 +264,7 @@ int ec_kv_cache_append(ec_kv_cache* cache, uint32_t layer_idx, const float* k_pr
         e = cudaMemcpyAsync(L.keys_fp32 + pos * row, k_proj, row * 4, cudaMemcpyDeviceToDevice, st);
         if (e == cudaSuccess)
             e = cudaMemcpyAsync(L.values_fp32 + pos * row, v_proj, row * 4, cudaMemcpyDeviceToDevice, st);
-    } else if (c.head_dim == 128 && aligned16(k_proj) && aligned16(v_proj) &&
+    } else if ((c.head_dim == 128 || c.head_dim == 256) && aligned16(k_proj) && aligned16(v_proj) &&
                (c.num_kv_heads == 1 || c.num_kv_heads == 2 || c.num_kv_heads == 4 || c.num_kv_heads == 8)) {
         ec::AppendArgs a{};
         a.k = k_proj;
@@ -281,6 +280,7 @@ int ec_kv_cache_append(ec_kv_cache* cache, uint32_t layer_idx, const float* k_pr
         a.total_slots = c.max_seq_len;
         a.num_seqs = 1;
         a.n_new = 1;
+        a.head_dim = (int)c.head_dim;
         e = ec::launch_append(a, (int)c.num_kv_heads, cache->scale_mode == EC_SCALE_ROW, st);
     } else if (cache->scale_mode == EC_SCALE_ROW) {
         e = ec::launch_quantize_rows(k_proj, L.keys_int8 + pos * row, L.key_scales + pos, 1, (uint32_t)row, st);
@@ -326,7 +326,7 @@ int ec_kv_cache_attention(ec_kv_cache* cache, uint32_t layer_idx, const float* q
         return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_cache_attention (fp32 cache) launch");
     }
     if (!decode_shape_supported(c.num_heads, c.num_kv_heads, c.head_dim))
-        return fail(EC_ERR_UNSUPPORTED, "kv_cache_attention: needs head_dim 128, num_kv_heads 4|8, group 1|2|4");
+        return fail(EC_ERR_UNSUPPORTED, "kv_cache_attention: needs head_dim 128|256, num_kv_heads 1|2|4|8 and num_heads a multiple of it by at most 32");
     if (!aligned16(q) || !aligned16(out)) return fail(EC_ERR_MISALIGNED, "kv_cache_attention: q/out not 16-byte aligned");
     const ec_kv_layer& L = cache->layers[layer_idx];
     ec::DecodeArgs a{};
@@ -344,6 +344,7 @@ int ec_kv_cache_attention(ec_kv_cache* cache, uint32_t layer_idx, const float* q
     a.q_mul = softmax_scale;
     a.num_seqs = 1;
     a.num_heads = (int)c.num_heads;
+    a.head_dim = (int)c.head_dim;
     a.row_scales = cache->scale_mode == EC_SCALE_ROW;
     a.mode = ec::kOut;
     cudaError_t e = ec::launch_decode(a, (int)c.num_kv_heads, cache->plan, cache->ws, as_stream(stream));
@@ -662,8 +663,8 @@ int ec::check_batch(const ec_kv_batch* b, const char* who) {
         const uint32_t p = b->page_tokens;
         if (p < 128 || (p & (p - 1)) || p > (1u << 24))
             return fail(EC_ERR_INVALID_ARGUMENT, "%s: page_tokens must be a power of two >= 128", who);
-        if (b->max_pages == 0 || b->total_slots % p)
-            return fail(EC_ERR_INVALID_ARGUMENT, "%s: paged batch needs max_pages > 0 and total_slots a multiple of page_tokens", who);
+        if (b->max_pages == 0 || b->total_slots < p || b->total_slots % p)
+            return fail(EC_ERR_INVALID_ARGUMENT, "%s: paged batch needs max_pages > 0 and total_slots a non-zero multiple of page_tokens", who);
         if ((uint64_t)b->max_pages * p > 0x7fffffffull)
             return fail(EC_ERR_INVALID_ARGUMENT, "%s: max_pages * page_tokens must fit int32", who);
     }
@@ -689,9 +690,9 @@ int ec_kv_batch_append(const ec_kv_batch* b, const float* k, const float* v,
     if (rc) return rc;
     if (tokens_per_seq == 0 || b->num_seqs == 0) return EC_OK;
     if (!k || !v) return fail(EC_ERR_INVALID_ARGUMENT, "kv_batch_append: k/v NULL");
-    if (b->head_dim != 128 || !(b->num_kv_heads == 1 || b->num_kv_heads == 2 || b->num_kv_heads == 4 ||
-                                b->num_kv_heads == 8))
-        return fail(EC_ERR_UNSUPPORTED, "kv_batch_append: needs head_dim 128 and num_kv_heads 1|2|4|8");
+    if ((b->head_dim != 128 && b->head_dim != 256) ||
+        !(b->num_kv_heads == 1 || b->num_kv_heads == 2 || b->num_kv_heads == 4 || b->num_kv_heads == 8))
+        return fail(EC_ERR_UNSUPPORTED, "kv_batch_append: needs head_dim 128|256 and num_kv_heads 1|2|4|8");
     if (!aligned16(k) || !aligned16(v)) return fail(EC_ERR_MISALIGNED, "kv_batch_append: k/v not 16-byte aligned");
     if ((uint64_t)b->num_seqs * tokens_per_seq > 0x7fffffffull)
         return fail(EC_ERR_UNSUPPORTED, "kv_batch_append: too many tokens in one call");
@@ -710,16 +711,17 @@ int ec_kv_batch_append(const ec_kv_batch* b, const float* k, const float* v,
     a.pages = ec::page_map_of(b);
     a.num_seqs = (int)b->num_seqs;
     a.n_new = (int)tokens_per_seq;
+    a.head_dim = (int)b->head_dim;
     cudaError_t e = ec::launch_append(a, (int)b->num_kv_heads, b->scale_mode == EC_SCALE_ROW,
                                       as_stream(stream));
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_batch_append launch");
 }
 
-// 1 / base^(i/d), i = 0, 2, .., 126 (echo-core-zig src/inference/engine.zig:
+// 1 / base^(i/d), i = 0, 2, .., d - 2 (echo-core-zig src/inference/engine.zig:
 // 477-478: freq = 1.0 / pow(f32, base, i / head_dim), all in fp32)
-static void rope_inv_freq(float base, float* out64) {
-    for (int i = 0; i < 128; i += 2)
-        out64[i / 2] = 1.0f / std::pow(base, static_cast<float>(i) / 128.0f);
+static void rope_inv_freq(float base, uint32_t head_dim, float* out) {
+    for (uint32_t i = 0; i < head_dim; i += 2)
+        out[i / 2] = 1.0f / std::pow(base, static_cast<float>(i) / static_cast<float>(head_dim));
 }
 
 int ec_kv_batch_append_rope(const ec_kv_batch* b, const float* k, const float* v,
@@ -730,9 +732,9 @@ int ec_kv_batch_append_rope(const ec_kv_batch* b, const float* k, const float* v
     if (!k_desc) return fail(EC_ERR_INVALID_ARGUMENT, "kv_batch_append_rope: rope descriptor NULL");
     if (tokens_per_seq == 0 || b->num_seqs == 0) return EC_OK;
     if (!k || !v) return fail(EC_ERR_INVALID_ARGUMENT, "kv_batch_append_rope: k/v NULL");
-    if (b->head_dim != 128 || !(b->num_kv_heads == 1 || b->num_kv_heads == 2 || b->num_kv_heads == 4 ||
-                                b->num_kv_heads == 8))
-        return fail(EC_ERR_UNSUPPORTED, "kv_batch_append_rope: needs head_dim 128 and num_kv_heads 1|2|4|8");
+    if ((b->head_dim != 128 && b->head_dim != 256) ||
+        !(b->num_kv_heads == 1 || b->num_kv_heads == 2 || b->num_kv_heads == 4 || b->num_kv_heads == 8))
+        return fail(EC_ERR_UNSUPPORTED, "kv_batch_append_rope: needs head_dim 128|256 and num_kv_heads 1|2|4|8");
     if (!aligned16(k) || !aligned16(v)) return fail(EC_ERR_MISALIGNED, "kv_batch_append_rope: k/v not 16-byte aligned");
     if (k_desc->norm_weight && (reinterpret_cast<uintptr_t>(k_desc->norm_weight) & 7))
         return fail(EC_ERR_MISALIGNED, "kv_batch_append_rope: norm weight not 8-byte aligned");
@@ -753,9 +755,10 @@ int ec_kv_batch_append_rope(const ec_kv_batch* b, const float* k, const float* v
     a.pages = ec::page_map_of(b);
     a.num_seqs = (int)b->num_seqs;
     a.n_new = (int)tokens_per_seq;
+    a.head_dim = (int)b->head_dim;
     a.k_norm_w = k_desc->norm_weight;
     a.rope = k_desc->rope_base > 0.0f;
-    if (a.rope) rope_inv_freq(k_desc->rope_base, a.inv_freq);
+    if (a.rope) rope_inv_freq(k_desc->rope_base, b->head_dim, a.inv_freq);
     cudaError_t e = ec::launch_append_rope(a, (int)b->num_kv_heads, b->scale_mode == EC_SCALE_ROW,
                                            as_stream(stream));
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "kv_batch_append_rope launch");
@@ -765,31 +768,42 @@ int ec_rope_rows(float* x, uint32_t rows, uint32_t num_heads, uint32_t head_dim,
                  const int32_t* positions, const ec_rope_desc* desc, ec_stream_t stream) {
     if (!x || !desc) return fail(EC_ERR_INVALID_ARGUMENT, "rope_rows: null argument");
     if (rows == 0 || num_heads == 0) return EC_OK;
-    if (head_dim != 128) return fail(EC_ERR_UNSUPPORTED, "rope_rows: needs head_dim 128");
+    if (head_dim != 128 && head_dim != 256)
+        return fail(EC_ERR_UNSUPPORTED, "rope_rows: needs head_dim 128 or 256");
     const bool rope = desc->rope_base > 0.0f;
     if (rope && !positions) return fail(EC_ERR_INVALID_ARGUMENT, "rope_rows: positions NULL");
     if (!aligned16(x)) return fail(EC_ERR_MISALIGNED, "rope_rows: x not 16-byte aligned");
     if (desc->norm_weight && (reinterpret_cast<uintptr_t>(desc->norm_weight) & 7))
         return fail(EC_ERR_MISALIGNED, "rope_rows: norm weight not 8-byte aligned");
-    float inv_freq[64] = {};
-    if (rope) rope_inv_freq(desc->rope_base, inv_freq);
-    cudaError_t e = ec::launch_rope_rows(x, rows, num_heads, positions, desc->norm_weight, rope ? 1 : 0,
-                                         inv_freq, as_stream(stream));
+    float inv_freq[ec::kMaxHeadDim / 2] = {};
+    if (rope) rope_inv_freq(desc->rope_base, head_dim, inv_freq);
+    cudaError_t e = ec::launch_rope_rows(x, rows, num_heads, head_dim, positions, desc->norm_weight,
+                                         rope ? 1 : 0, inv_freq, as_stream(stream));
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "rope_rows launch");
 }
 
 size_t ec_decode_workspace_size(uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim,
                                 uint32_t max_seq_len) {
-    (void)head_dim;
-    ec::DecodePlan p = ec::plan_decode((int)num_seqs, (int)max_seq_len, num_sms_current());
-    return ec::decode_workspace_bytes(p, (int)num_seqs, (int)num_heads);
+    // the plan depends on num_kv_heads, which this query does not take: the
+    // largest workspace over every num_kv_heads a kernel covers for num_heads
+    const int sms = num_sms_current();
+    size_t most = 0;
+    for (uint32_t hkv = 1; hkv <= 8; hkv *= 2) {
+        if (!num_heads || num_heads % hkv || !decode_shape_supported(num_heads, hkv, head_dim)) continue;
+        const ec::DecodePlan p = ec::plan_decode((int)num_seqs, (int)max_seq_len, sms, 0, (int)hkv,
+                                                 (int)num_heads, (int)head_dim);
+        const size_t b = ec::decode_workspace_bytes(p, (int)num_seqs, (int)num_heads, (int)head_dim);
+        if (b > most) most = b;
+    }
+    return most;
 }
 
 size_t ec_decode_workspace_size_batch(const ec_kv_batch* b, uint32_t num_heads) {
     if (!b) return 0;
     ec::DecodePlan p = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, num_sms_current(),
-                                       b->total_tokens_hint);
-    return ec::decode_workspace_bytes(p, (int)b->num_seqs, (int)num_heads);
+                                       b->total_tokens_hint, (int)b->num_kv_heads, (int)num_heads,
+                                       (int)b->head_dim);
+    return ec::decode_workspace_bytes(p, (int)b->num_seqs, (int)num_heads, (int)b->head_dim);
 }
 
 static int decode_common(const ec_kv_batch* b, const float* q, float* out, float* out_ml,
@@ -801,11 +815,13 @@ static int decode_common(const ec_kv_batch* b, const float* q, float* out, float
     if (!q || !out || (mode == ec::kPartial && !out_ml))
         return fail(EC_ERR_INVALID_ARGUMENT, "%s: q/out NULL", who);
     if (!decode_shape_supported(num_heads, b->num_kv_heads, b->head_dim))
-        return fail(EC_ERR_UNSUPPORTED, "%s: needs head_dim 128, num_kv_heads 4|8, num_heads/num_kv_heads 1|2|4", who);
+        return fail(EC_ERR_UNSUPPORTED, "%s: needs head_dim 128|256, num_kv_heads 1|2|4|8 and num_heads a multiple of it by at most 32", who);
     if (!aligned16(q) || !aligned16(out)) return fail(EC_ERR_MISALIGNED, "%s: q/out not 16-byte aligned", who);
     ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len, num_sms_current(),
-                                          b->total_tokens_hint);
-    const size_t need = ec::decode_workspace_bytes(plan, (int)b->num_seqs, (int)num_heads);
+                                          b->total_tokens_hint, (int)b->num_kv_heads, (int)num_heads,
+                                          (int)b->head_dim);
+    const size_t need = ec::decode_workspace_bytes(plan, (int)b->num_seqs, (int)num_heads,
+                                                   (int)b->head_dim);
     if (need > 0 && (!ws || ws_bytes < need))
         return fail(EC_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", who, need, ws_bytes);
     if (need > 0 && !aligned16(ws)) return fail(EC_ERR_MISALIGNED, "%s: workspace not 16-byte aligned", who);
@@ -826,6 +842,7 @@ static int decode_common(const ec_kv_batch* b, const float* q, float* out, float
     a.q_mul = softmax_scale;
     a.num_seqs = (int)b->num_seqs;
     a.num_heads = (int)num_heads;
+    a.head_dim = (int)b->head_dim;
     a.row_scales = b->scale_mode == EC_SCALE_ROW;
     a.mode = mode;
     cudaError_t e = ec::launch_decode(a, (int)b->num_kv_heads, plan, ws, as_stream(stream));
@@ -883,12 +900,13 @@ int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t num_parts
                    uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim, float* out,
                    ec_stream_t stream) {
     if (!part_o || !part_ml || !out) return fail(EC_ERR_INVALID_ARGUMENT, "lse_combine: null argument");
-    if (head_dim != 128) return fail(EC_ERR_UNSUPPORTED, "lse_combine: head_dim must be 128");
+    if (head_dim != 128 && head_dim != 256)
+        return fail(EC_ERR_UNSUPPORTED, "lse_combine: head_dim must be 128 or 256");
     if (num_parts == 0 || num_seqs == 0 || num_heads == 0) return EC_OK;
     if (num_seqs > 0x7fffffffu || num_heads > 65535u)
         return fail(EC_ERR_UNSUPPORTED, "lse_combine: grid too large");
     cudaError_t e = ec::launch_lse_combine(part_o, part_ml, (int)num_parts, (int)num_seqs,
-                                           (int)num_heads, out, as_stream(stream));
+                                           (int)num_heads, (int)head_dim, out, as_stream(stream));
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "lse_combine launch");
 }
 

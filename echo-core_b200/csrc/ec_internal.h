@@ -63,6 +63,8 @@ inline PageMap page_map_of(const ec_kv_batch* b) {
     return m;
 }
 
+constexpr int kMaxHeadDim = 256;   // head_dim 128 or 256 (append, decode)
+
 struct AppendArgs {
     const float* k;
     const float* v;
@@ -78,17 +80,18 @@ struct AppendArgs {
     uint64_t total_slots;
     int num_seqs;
     int n_new;
+    int head_dim;                 // 128 or 256
     PageMap pages;
     // K pre-processing of echo-core-zig (src/inference/engine.zig): per-head
     // RMS norm with an fp16 weight (:521-532), then RoPE (:466-518).  Used by
     // the rope variant of the append kernel only.
-    const uint16_t* k_norm_w;     // fp16 [128] or null: no norm
+    const uint16_t* k_norm_w;     // fp16 [head_dim] or null: no norm
     int rope;                     // 0: no rotation
-    float inv_freq[64];           // 1 / base^(2i/128), computed on the host
+    float inv_freq[kMaxHeadDim / 2];   // 1 / base^(2i/head_dim), computed on the host
 };
 
 struct DecodeArgs {
-    const int8_t* keys;
+    const int8_t* keys;       // [total_slots][num_kv_heads][head_dim]
     const int8_t* values;
     const float* key_scales;
     const float* val_scales;
@@ -98,14 +101,16 @@ struct DecodeArgs {
     int32_t host_offset, host_capacity, host_length;
     int32_t* err;
     uint64_t total_slots;
-    const float* q;       // [num_seqs][num_heads][128]
+    const float* q;       // [num_seqs][num_heads][head_dim]
     float* out;           // final output (normalised) when mode == kOut
     float* out_ml;        // (m, l) per (seq, head) when mode == kPartial
-    float* part_o;        // [num_seqs*max_chunks][num_heads][128]
+    float* part_o;        // [num_seqs*max_chunks][num_heads][head_dim]
     float* part_ml;       // [num_seqs*max_chunks][num_heads][2]
     float q_mul;          // softmax scale (applied to q first, as the reference does)
     int num_seqs;
     int num_heads;
+    int num_kv_heads;     // query head h reads KV head h % num_kv_heads
+    int head_dim;         // 128 or 256
     int max_chunks;
     int chunk_tokens;
     int row_scales;       // 1: EC_SCALE_ROW
@@ -120,10 +125,11 @@ cudaError_t launch_quantize_rows(const float* in, int8_t* out, float* scales, ui
 cudaError_t launch_append(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st);
 cudaError_t launch_append_rope(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st);
 // In-place per-head RMS norm (fp16 weight, may be null) and RoPE of rows of
-// num_heads * 128 floats, row r at position positions[r].
-cudaError_t launch_rope_rows(float* x, uint32_t rows, uint32_t num_heads, const int32_t* positions,
-                             const uint16_t* norm_w, int rope, const float* inv_freq64,
-                             cudaStream_t st);
+// num_heads * head_dim floats (head_dim 128 or 256), row r at position
+// positions[r]; inv_freq has head_dim / 2 entries.
+cudaError_t launch_rope_rows(float* x, uint32_t rows, uint32_t num_heads, uint32_t head_dim,
+                             const int32_t* positions, const uint16_t* norm_w, int rope,
+                             const float* inv_freq, cudaStream_t st);
 cudaError_t launch_fused_dequant_dot(const float* q, const int8_t* k, const float* s, float* out,
                                      uint32_t dim, uint32_t seq_len, cudaStream_t st);
 
@@ -132,10 +138,19 @@ struct DecodePlan {
     int chunk_tokens;
     int max_chunks;
 };
+// The compiled decode kernel for a shape: hc KV heads per CTA, qw quads of
+// query heads per KV head, scw = num_kv_heads, dv = head_dim / 128, and its
+// resident CTAs per SM.  hc == 0: no kernel covers the shape.
+struct DecodeVariant {
+    int hc, qw, scw, dv, ctas_per_sm;
+};
+DecodeVariant decode_variant(int num_kv_heads, int group, int head_dim);
 // total_tokens: host estimate of the batch's cached tokens (0: unknown, every
-// sequence is assumed to be max_seq_len long)
-DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens = 0);
-size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads);
+// sequence is assumed to be max_seq_len long).  The kernel variant of
+// (num_kv_heads, num_heads, head_dim) sets how many CTAs fit on the GPU at once.
+DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens,
+                       int num_kv_heads, int num_heads, int head_dim);
+size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads, int head_dim);
 // Returns cudaErrorInvalidValue for a shape outside the envelope.
 cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan, void* ws,
                           cudaStream_t st);
@@ -174,7 +189,8 @@ int check_batch(const ec_kv_batch* b, const char* who);
 // The (num_heads, num_kv_heads, head_dim) shapes the int8 decode kernel covers.
 bool decode_shape_supported(uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim);
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
-                               int num_seqs, int num_heads, float* out, cudaStream_t st);
+                               int num_seqs, int num_heads, int head_dim, float* out,
+                               cudaStream_t st);
 
 // Context-parallel exchange + merge over peer memory (cp_exchange.cu).
 constexpr int kCpMaxWorld = 8;

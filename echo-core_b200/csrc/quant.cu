@@ -95,8 +95,9 @@ struct TableView {
     }
 };
 
-// Quantizes one token's K and V rows held as xs[t][g] (lane l holds float4 l
-// of head g's 128 floats) and stores codes and scales at `slot`.
+// Quantizes one token's K and V rows held as xs[t][g * DV + dv] (lane l holds
+// float4 l of the dv-th 128-float block of head g; head_dim = 128 * DV) and
+// stores codes and scales at `slot`.
 //
 // The 2 x HKV absmaxes (2 for ROW) are reduced with a butterfly
 // reduce-scatter: after it, lane l holds the full absmax of value
@@ -110,10 +111,10 @@ struct TableView {
 // even integer 1.5 * 2^23 rounds v to an integer with ties to even, and the
 // sum's mantissa is 2^22 + RNE(v).  A subnormal scale (absmax below about
 // 1.5e-36) takes the exact path, uniformly across the warp.
-template <int HKV, bool ROW>
-__device__ __forceinline__ void quantize_store(const float4 (&xs)[2][HKV], const AppendArgs& a,
+template <int HKV, bool ROW, int DV>
+__device__ __forceinline__ void quantize_store(const float4 (&xs)[2][HKV * DV], const AppendArgs& a,
                                                int64_t slot, int lane) {
-    constexpr int D = 128;
+    constexpr int D = 128 * DV;
     constexpr int NV = ROW ? 2 : 2 * HKV;           // values to reduce: (t, g) or t
     constexpr int LB = NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : 4;   // log2(NV)
     constexpr int SH = 5 - LB;                      // lane >> SH = the value a lane ends with
@@ -123,8 +124,12 @@ __device__ __forceinline__ void quantize_store(const float4 (&xs)[2][HKV], const
     for (int t = 0; t < 2; ++t) {
 #pragma unroll
         for (int g = 0; g < HKV; ++g) {
-            const float4 x = xs[t][g];
-            const float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+            float m = 0.0f;
+#pragma unroll
+            for (int dv = 0; dv < DV; ++dv) {
+                const float4 x = xs[t][g * DV + dv];
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+            }
             if (ROW) v[t] = g == 0 ? m : fmaxf(v[t], m);
             else v[t * HKV + g] = m;
         }
@@ -161,21 +166,24 @@ __device__ __forceinline__ void quantize_store(const float4 (&xs)[2][HKV], const
         for (int g = 0; g < HKV; ++g) {
             const int src = (ROW ? t : t * HKV + g) << SH;
             const float inv = __shfl_sync(0xffffffffu, inv_own, src);
-            const float4 x = xs[t][g];
-            uint32_t word;
-            if (!((sub >> src) & 1u)) {
-                constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
-                const uint32_t b0 = __float_as_uint(__fadd_rn(__fmul_rn(x.x, inv), kRound));
-                const uint32_t b1 = __float_as_uint(__fadd_rn(__fmul_rn(x.y, inv), kRound));
-                const uint32_t b2 = __float_as_uint(__fadd_rn(__fmul_rn(x.z, inv), kRound));
-                const uint32_t b3 = __float_as_uint(__fadd_rn(__fmul_rn(x.w, inv), kRound));
-                word = __byte_perm(__byte_perm(b0, b1, 0x0040u), __byte_perm(b2, b3, 0x0040u), 0x5410u);
-            } else {
-                word = (uint32_t)(q_body(x.x, inv) & 0xff) | ((uint32_t)(q_body(x.y, inv) & 0xff) << 8) |
-                       ((uint32_t)(q_body(x.z, inv) & 0xff) << 16) |
-                       ((uint32_t)(q_body(x.w, inv) & 0xff) << 24);
+#pragma unroll
+            for (int dv = 0; dv < DV; ++dv) {
+                const float4 x = xs[t][g * DV + dv];
+                uint32_t word;
+                if (!((sub >> src) & 1u)) {
+                    constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
+                    const uint32_t b0 = __float_as_uint(__fadd_rn(__fmul_rn(x.x, inv), kRound));
+                    const uint32_t b1 = __float_as_uint(__fadd_rn(__fmul_rn(x.y, inv), kRound));
+                    const uint32_t b2 = __float_as_uint(__fadd_rn(__fmul_rn(x.z, inv), kRound));
+                    const uint32_t b3 = __float_as_uint(__fadd_rn(__fmul_rn(x.w, inv), kRound));
+                    word = __byte_perm(__byte_perm(b0, b1, 0x0040u), __byte_perm(b2, b3, 0x0040u), 0x5410u);
+                } else {
+                    word = (uint32_t)(q_body(x.x, inv) & 0xff) | ((uint32_t)(q_body(x.y, inv) & 0xff) << 8) |
+                           ((uint32_t)(q_body(x.z, inv) & 0xff) << 16) |
+                           ((uint32_t)(q_body(x.w, inv) & 0xff) << 24);
+                }
+                reinterpret_cast<uint32_t*>(dst + g * D + dv * 128)[lane] = word;
             }
-            reinterpret_cast<uint32_t*>(dst + g * D)[lane] = word;
         }
     }
 }
@@ -189,9 +197,9 @@ __device__ __forceinline__ void bump_own_length(const AppendArgs& a, int s, int3
     if (lane == 0) a.seq_len[s] = len + 1;
 }
 
-template <int HKV, bool ROW>
+template <int HKV, bool ROW, int DV>
 __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
-    constexpr int D = 128;
+    constexpr int D = 128 * DV;
     pdl_wait();  // k / v and the table may come from the previous kernel
     pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -203,13 +211,13 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
     // the lane are issued first, so that they and the table load are in
     // flight together.
     const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
-    float4 xs[2][HKV];
+    float4 xs[2][HKV * DV];
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int g = 0; g < HKV; ++g)
-            xs[t][g] = __ldcs(reinterpret_cast<const float4*>((t == 0 ? a.k : a.v) + src_row) +
-                              g * 32 + lane);
+        for (int gd = 0; gd < HKV * DV; ++gd)
+            xs[t][gd] = __ldcs(reinterpret_cast<const float4*>((t == 0 ? a.k : a.v) + src_row) +
+                               gd * 32 + lane);
     TableView tv{a.seq_offset, a.seq_capacity, a.seq_len, a.host_offset, a.host_capacity,
                  a.host_length, a.total_slots, a.pages};
     int32_t off, cap, len;
@@ -227,7 +235,7 @@ __global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
         return;
     }
 
-    quantize_store<HKV, ROW>(xs, a, slot, lane);
+    quantize_store<HKV, ROW, DV>(xs, a, slot, lane);
     bump_own_length(a, s, len, lane);
 }
 
@@ -249,14 +257,17 @@ __global__ void bump_lengths_kernel(AppendArgs a) {
 // + 1e-6); k = k * (1/rms) * w) and rotary position embedding over
 // interleaved pairs (:466-518: angle = pos * freq_i, freq_i = 1/base^(i/d);
 // (k0, k1) -> (k0 cos - k1 sin, k0 sin + k1 cos)).  Products and sums are
-// rounded one at a time (no contraction), as the Zig code computes them; the
-// sines and cosines are computed in double and rounded to fp32.
+// rounded one at a time (no contraction) and in the Zig code's order -- the
+// sum of squares runs over the head's dims in sequence (:525-526), not as a
+// tree -- so the results are bit-identical to the CPU restatement; the sines
+// and cosines are the double-precision values rounded to fp32.
 struct PairRot { float c0, s0, c1, s1; };
 
-__device__ __forceinline__ PairRot pair_rotation(int pos, int lane, const float* inv_freq) {
-    // lane holds dims 4*lane .. 4*lane+3: pairs 2*lane and 2*lane+1
-    const float a0 = __fmul_rn((float)pos, inv_freq[2 * lane]);
-    const float a1 = __fmul_rn((float)pos, inv_freq[2 * lane + 1]);
+__device__ __forceinline__ PairRot pair_rotation(int pos, int lane, const float* inv_freq,
+                                                 int dv = 0) {
+    // lane holds dims 128*dv + 4*lane .. +3: pairs 64*dv + 2*lane and +1
+    const float a0 = __fmul_rn((float)pos, inv_freq[64 * dv + 2 * lane]);
+    const float a1 = __fmul_rn((float)pos, inv_freq[64 * dv + 2 * lane + 1]);
     double s0, c0, s1, c1;
     sincos((double)a0, &s0, &c0);
     sincos((double)a1, &s1, &c1);
@@ -272,28 +283,43 @@ __device__ __forceinline__ float4 rotate(float4 x, const PairRot& r) {
     return y;
 }
 
-// per-head RMS norm of one 128-float head held as float4 per lane
-__device__ __forceinline__ float4 head_rms_norm(float4 x, const uint16_t* w, int lane) {
-    float ss = __fadd_rn(__fadd_rn(__fmul_rn(x.x, x.x), __fmul_rn(x.y, x.y)),
-                         __fadd_rn(__fmul_rn(x.z, x.z), __fmul_rn(x.w, x.w)));
+// per-head RMS norm of one head of 128 * DV floats held as DV float4 per lane
+// (lane l: dims 128*dv + 4l .. +3).  The squares are summed in dimension
+// order, one rounding per addition, as src/inference/engine.zig:525-526 sums
+// them: every lane runs the same chain over squares broadcast by shuffle.
+template <int DV>
+__device__ __forceinline__ void head_rms_norm(float4 (&x)[DV], const uint16_t* w, int lane) {
+    constexpr float kD = 128.0f * DV;
+    float ss = 0.0f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
+    for (int dv = 0; dv < DV; ++dv) {
+        const float q0 = __fmul_rn(x[dv].x, x[dv].x), q1 = __fmul_rn(x[dv].y, x[dv].y);
+        const float q2 = __fmul_rn(x[dv].z, x[dv].z), q3 = __fmul_rn(x[dv].w, x[dv].w);
+#pragma unroll 8
+        for (int l = 0; l < 32; ++l) {
+            ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, q0, l));
+            ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, q1, l));
+            ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, q2, l));
+            ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, q3, l));
+        }
+    }
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, kD), 1e-6f));
     const float inv = __fdiv_rn(1.0f, rms);
-    const ushort4 wb = reinterpret_cast<const ushort4*>(w)[lane];
-    float4 y;
-    y.x = __fmul_rn(__fmul_rn(x.x, inv), __half2float(__ushort_as_half(wb.x)));
-    y.y = __fmul_rn(__fmul_rn(x.y, inv), __half2float(__ushort_as_half(wb.y)));
-    y.z = __fmul_rn(__fmul_rn(x.z, inv), __half2float(__ushort_as_half(wb.z)));
-    y.w = __fmul_rn(__fmul_rn(x.w, inv), __half2float(__ushort_as_half(wb.w)));
-    return y;
+#pragma unroll
+    for (int dv = 0; dv < DV; ++dv) {
+        const ushort4 wb = reinterpret_cast<const ushort4*>(w)[dv * 32 + lane];
+        x[dv].x = __fmul_rn(__fmul_rn(x[dv].x, inv), __half2float(__ushort_as_half(wb.x)));
+        x[dv].y = __fmul_rn(__fmul_rn(x[dv].y, inv), __half2float(__ushort_as_half(wb.y)));
+        x[dv].z = __fmul_rn(__fmul_rn(x[dv].z, inv), __half2float(__ushort_as_half(wb.z)));
+        x[dv].w = __fmul_rn(__fmul_rn(x[dv].w, inv), __half2float(__ushort_as_half(wb.w)));
+    }
 }
 
 // append_kernel with K normed and rotated at its cache position before
 // quantization (one warp per (sequence, new token), as append_kernel)
-template <int HKV, bool ROW>
+template <int HKV, bool ROW, int DV>
 __global__ void __launch_bounds__(256) append_rope_kernel(AppendArgs a) {
-    constexpr int D = 128;
+    constexpr int D = 128 * DV;
     pdl_wait();  // k / v and the table may come from the previous kernel
     pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -319,21 +345,32 @@ __global__ void __launch_bounds__(256) append_rope_kernel(AppendArgs a) {
         return;
     }
     const size_t src_row = ((size_t)s * a.n_new + i) * (HKV * D);
-    PairRot rot{};
-    if (a.rope) rot = pair_rotation(pos, lane, a.inv_freq);
-    float4 xs[2][HKV];
+    PairRot rot[DV];
+    if (a.rope) {
+#pragma unroll
+        for (int dv = 0; dv < DV; ++dv) rot[dv] = pair_rotation(pos, lane, a.inv_freq, dv);
+    }
+    float4 xs[2][HKV * DV];
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int g = 0; g < HKV; ++g) {
-            float4 x = __ldcs(reinterpret_cast<const float4*>((t == 0 ? a.k : a.v) + src_row) + g * 32 + lane);
+            float4 x[DV];
+#pragma unroll
+            for (int dv = 0; dv < DV; ++dv)
+                x[dv] = __ldcs(reinterpret_cast<const float4*>((t == 0 ? a.k : a.v) + src_row) +
+                               (g * DV + dv) * 32 + lane);
             if (t == 0) {
-                if (a.k_norm_w) x = head_rms_norm(x, a.k_norm_w, lane);
-                if (a.rope) x = rotate(x, rot);
+                if (a.k_norm_w) head_rms_norm<DV>(x, a.k_norm_w, lane);
+                if (a.rope) {
+#pragma unroll
+                    for (int dv = 0; dv < DV; ++dv) x[dv] = rotate(x[dv], rot[dv]);
+                }
             }
-            xs[t][g] = x;
+#pragma unroll
+            for (int dv = 0; dv < DV; ++dv) xs[t][g * DV + dv] = x[dv];
         }
-    quantize_store<HKV, ROW>(xs, a, slot, lane);
+    quantize_store<HKV, ROW, DV>(xs, a, slot, lane);
     bump_own_length(a, s, len, lane);
 }
 
@@ -343,20 +380,26 @@ struct RopeRowsArgs {
     const uint16_t* norm_w;
     uint32_t rows, num_heads;
     int rope;
-    float inv_freq[64];
+    float inv_freq[kMaxHeadDim / 2];
 };
 
 // one warp per (row, head): the Q side of the same pre-processing
+template <int DV>
 __global__ void __launch_bounds__(256) rope_rows_kernel(RopeRowsArgs a) {
     const uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (w >= (uint64_t)a.rows * a.num_heads) return;
     const uint32_t r = (uint32_t)(w / a.num_heads);
-    float4* p = reinterpret_cast<float4*>(a.x + w * 128) + lane;
-    float4 x = *p;
-    if (a.norm_w) x = head_rms_norm(x, a.norm_w, lane);
-    if (a.rope) x = rotate(x, pair_rotation(a.positions[r], lane, a.inv_freq));
-    *p = x;
+    float4* p = reinterpret_cast<float4*>(a.x + w * 128 * DV) + lane;
+    float4 x[DV];
+#pragma unroll
+    for (int dv = 0; dv < DV; ++dv) x[dv] = p[32 * dv];
+    if (a.norm_w) head_rms_norm<DV>(x, a.norm_w, lane);
+#pragma unroll
+    for (int dv = 0; dv < DV; ++dv) {
+        if (a.rope) x[dv] = rotate(x[dv], pair_rotation(a.positions[r], lane, a.inv_freq, dv));
+        p[32 * dv] = x[dv];
+    }
 }
 
 // ---------------------------------------------------------------- launchers
@@ -377,29 +420,37 @@ static cudaError_t launch_append_with(AppendFn fn, const AppendArgs& a, cudaStre
     return e;
 }
 
-#define EC_PICK_APPEND(K)                                      \
-    switch (num_kv_heads) {                                    \
-        case 1: return row_mode ? K<1, true> : K<1, false>;    \
-        case 2: return row_mode ? K<2, true> : K<2, false>;    \
-        case 4: return row_mode ? K<4, true> : K<4, false>;    \
-        case 8: return row_mode ? K<8, true> : K<8, false>;    \
-        default: return nullptr;                               \
+#define EC_PICK_APPEND_DV(K, DV)                                             \
+    switch (num_kv_heads) {                                                  \
+        case 1: return row_mode ? K<1, true, DV> : K<1, false, DV>;          \
+        case 2: return row_mode ? K<2, true, DV> : K<2, false, DV>;          \
+        case 4: return row_mode ? K<4, true, DV> : K<4, false, DV>;          \
+        case 8: return row_mode ? K<8, true, DV> : K<8, false, DV>;          \
+        default: return nullptr;                                             \
     }
-static AppendFn pick_append(int num_kv_heads, bool row_mode) { EC_PICK_APPEND(append_kernel) }
-static AppendFn pick_append_rope(int num_kv_heads, bool row_mode) {
+#define EC_PICK_APPEND(K)                                                    \
+    if (head_dim == 128) { EC_PICK_APPEND_DV(K, 1) }                         \
+    if (head_dim == 256) { EC_PICK_APPEND_DV(K, 2) }                         \
+    return nullptr;
+static AppendFn pick_append(int num_kv_heads, int head_dim, bool row_mode) {
+    EC_PICK_APPEND(append_kernel)
+}
+static AppendFn pick_append_rope(int num_kv_heads, int head_dim, bool row_mode) {
     EC_PICK_APPEND(append_rope_kernel)
 }
 #undef EC_PICK_APPEND
+#undef EC_PICK_APPEND_DV
 
 cudaError_t launch_append_rope(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st) {
-    return launch_append_with(pick_append_rope(num_kv_heads, row_mode), a, st);
+    return launch_append_with(pick_append_rope(num_kv_heads, a.head_dim, row_mode), a, st);
 }
 
-cudaError_t launch_rope_rows(float* x, uint32_t rows, uint32_t num_heads, const int32_t* positions,
-                             const uint16_t* norm_w, int rope, const float* inv_freq64,
-                             cudaStream_t st) {
+cudaError_t launch_rope_rows(float* x, uint32_t rows, uint32_t num_heads, uint32_t head_dim,
+                             const int32_t* positions, const uint16_t* norm_w, int rope,
+                             const float* inv_freq, cudaStream_t st) {
     const uint64_t warps = (uint64_t)rows * num_heads;
     if (warps == 0) return cudaSuccess;
+    if (head_dim != 128 && head_dim != 256) return cudaErrorInvalidValue;
     RopeRowsArgs a{};
     a.x = x;
     a.positions = positions;
@@ -407,10 +458,13 @@ cudaError_t launch_rope_rows(float* x, uint32_t rows, uint32_t num_heads, const 
     a.rows = rows;
     a.num_heads = num_heads;
     a.rope = rope;
-    for (int i = 0; i < 64; ++i) a.inv_freq[i] = inv_freq64[i];
+    for (uint32_t i = 0; i < head_dim / 2; ++i) a.inv_freq[i] = inv_freq[i];
     const uint64_t blocks = (warps * 32 + 255) / 256;
     if (blocks > 0x7fffffffull) return cudaErrorInvalidConfiguration;
-    rope_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(a);
+    if (head_dim == 128)
+        rope_rows_kernel<1><<<(unsigned)blocks, 256, 0, st>>>(a);
+    else
+        rope_rows_kernel<2><<<(unsigned)blocks, 256, 0, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -425,7 +479,7 @@ cudaError_t launch_quantize_rows(const float* in, int8_t* out, float* scales, ui
 }
 
 cudaError_t launch_append(const AppendArgs& a, int num_kv_heads, bool row_mode, cudaStream_t st) {
-    return launch_append_with(pick_append(num_kv_heads, row_mode), a, st);
+    return launch_append_with(pick_append(num_kv_heads, a.head_dim, row_mode), a, st);
 }
 
 // ------------------------------------------------------ fused dequant dot

@@ -88,10 +88,10 @@ class RopeDesc(ctypes.Structure):
 
 
 def rope_rows(x, rows: int, num_heads: int, positions=None, rope_base: float = 10000.0,
-              norm_weight=None, stream=None) -> None:
+              norm_weight=None, stream=None, head_dim: int = 128) -> None:
     """In-place per-head RMS norm and RoPE of query rows (ec_rope_rows)."""
     d = RopeDesc(rope_base, _ptr(norm_weight) if norm_weight is not None else None)
-    check(lib().ec_rope_rows(_ptr(x), rows, num_heads, 128,
+    check(lib().ec_rope_rows(_ptr(x), rows, num_heads, head_dim,
                              _ptr(positions) if positions is not None else None,
                              ctypes.byref(d), _stream(stream)))
 

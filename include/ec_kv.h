@@ -253,11 +253,14 @@ EC_API int ec_kv_batch_append(const ec_kv_batch* batch, const float* k, const fl
 
 /* K pre-processing of echo-core-zig before the cache append
  * (src/inference/engine.zig:544-559): a per-head RMS norm with an fp16 weight
- * (:521-532; rms = sqrt(sum x^2 / 128 + 1e-6), x = x * (1/rms) * w), then
- * rotary position embedding over interleaved pairs (:466-518; angle =
- * pos * freq_i, freq_i = 1 / rope_base^(i/128); (x0, x1) -> (x0 cos - x1 sin,
- * x0 sin + x1 cos)).  rope_base <= 0 skips the rotation, a NULL norm_weight
- * (device, fp16 [128], 8-byte aligned) skips the norm. */
+ * (:521-532; rms = sqrt(sum x^2 / d + 1e-6) summed in dimension order,
+ * x = x * (1/rms) * w), then rotary position embedding over interleaved pairs
+ * (:466-518; angle = pos * freq_i, freq_i = 1 / rope_base^(i/d); (x0, x1) ->
+ * (x0 cos - x1 sin, x0 sin + x1 cos)), d = head_dim (128 or 256).  Every
+ * product and sum is rounded on its own in that order; cos and sin are the
+ * fp32 roundings of their double-precision values.  rope_base <= 0 skips the
+ * rotation, a NULL norm_weight (device, fp16 [head_dim], 8-byte aligned)
+ * skips the norm. */
 typedef struct ec_rope_desc {
     float rope_base;                /* 10000 in echo-core-zig */
     const uint16_t* norm_weight;
@@ -276,7 +279,9 @@ EC_API int ec_rope_rows(float* x, uint32_t rows, uint32_t num_heads, uint32_t he
                         const int32_t* positions, const ec_rope_desc* desc, ec_stream_t stream);
 
 /* Workspace (device bytes) ec_decode_attention needs for this batch shape on
- * the current device. */
+ * the current device: the largest over the num_kv_heads values the kernels
+ * cover for num_heads (the split plan depends on num_kv_heads, which this
+ * query does not take); ec_decode_workspace_size_batch gives the exact size. */
 EC_API size_t ec_decode_workspace_size(uint32_t num_seqs, uint32_t num_heads, uint32_t head_dim,
                                 uint32_t max_seq_len);
 /* The same for a batch descriptor, taking its total_tokens_hint into account
@@ -286,8 +291,9 @@ EC_API size_t ec_decode_workspace_size_batch(const ec_kv_batch* batch, uint32_t 
 /* Decode attention for every sequence of the batch (the loop of
  * src/inference.cpp:321-392 per sequence):
  * q [num_seqs][num_heads][head_dim] fp32, out same shape fp32, device.
- * Supported envelope: head_dim 128, num_kv_heads 4 or 8,
- * num_heads/num_kv_heads in {1, 2, 4}. */
+ * Supported envelope: head_dim 128 or 256, num_kv_heads 1, 2, 4 or 8, and
+ * num_heads any multiple of num_kv_heads up to 32 times it (query head h
+ * reads KV head h % num_kv_heads, src/inference.cpp:335). */
 EC_API int ec_decode_attention(const ec_kv_batch* batch, const float* q, float* out,
                         uint32_t num_heads, float softmax_scale, void* workspace,
                         size_t workspace_bytes, ec_stream_t stream);

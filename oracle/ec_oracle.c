@@ -257,7 +257,21 @@ void oracle_decode_attention_f32(const float* keys, const float* values, uint32_
  * :466-518).  x: [num_heads][head_dim] fp32 in place; norm_w: head_dim fp32
  * values of the fp16 weight, or NULL; rope_base <= 0: no rotation.  Every
  * product and sum is rounded on its own (volatile), as the Zig code evaluates
- * them without contraction.
+ * them without contraction, in the Zig code's order:
+ *   :525-526  rms += x[i] * x[i], i = 0 .. head_dim-1 in sequence
+ *   :527      rms = sqrt(rms / head_dim + 1e-6)
+ *   :528      inv_rms = 1 / rms
+ *   :530      x[i] = x[i] * inv_rms * w[i]        (left to right)
+ *   :477      freq = 1 / pow(base, i / head_dim)  (fp32 throughout)
+ *   :478      angle = pos * freq
+ *   :479-480  cos(angle), sin(angle)
+ *   :483-484  x0' = x0 cos - x1 sin;  x1' = x0 sin + x1 cos
+ * The Zig code's @cos/@sin/pow are fp32 library functions that this container
+ * cannot run (no Zig toolchain); this restatement takes cos and sin as the
+ * fp32 rounding of the double-precision values at the fp32 angle (the
+ * correctly rounded fp32 result but for double-rounding cases) and pow as
+ * the C library's powf.  The restatement is therefore pinned to no Zig
+ * output; the GPU kernels are bit-exact with it.
  */
 void oracle_norm_rope(float* x, uint32_t num_heads, uint32_t head_dim, uint32_t pos,
                       const float* norm_w, float rope_base) {
@@ -280,7 +294,7 @@ void oracle_norm_rope(float* x, uint32_t num_heads, uint32_t head_dim, uint32_t 
             for (uint32_t i = 0; i < head_dim; i += 2) {
                 const float freq = 1.0f / powf(rope_base, (float)i / (float)head_dim);
                 volatile float angle = (float)pos * freq;
-                const float c = cosf(angle), s = sinf(angle);
+                const float c = (float)cos((double)angle), s = (float)sin((double)angle);
                 const float x0 = p[i], x1 = p[i + 1];
                 volatile float a = x0 * c, b = x1 * s, d = x0 * s, e = x1 * c;
                 p[i] = a - b;

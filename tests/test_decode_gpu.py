@@ -21,6 +21,10 @@ def _dev(torch, a):
 
 
 def _make_seq(rng, L, hkv, mode=O.SCALE_PER_HEAD):
+    if L == 0:
+        ns = hkv if mode == O.SCALE_PER_HEAD else 1
+        z8, zs = np.zeros((0, hkv * D), np.int8), np.zeros((0, ns), np.float32)
+        return z8, z8, zs, zs
     kq, ks = O.quantize_kv(W.kv_rows(rng, L, hkv, D), hkv, D, mode)
     vq, vs = O.quantize_kv(W.kv_rows(rng, L, hkv, D), hkv, D, mode)
     return kq, vq, ks, vs
@@ -89,7 +93,11 @@ def test_config2_ragged_batch_append_then_decode(cuda):
         assert_attn_close(got[s], want, f"seq {s}")
 
 
-@pytest.mark.parametrize("H,hkv", [(16, 4), (8, 4), (4, 4), (32, 8), (16, 8), (8, 8)])
+@pytest.mark.parametrize("H,hkv", [
+    (16, 4), (8, 4), (4, 4), (32, 8), (16, 8), (8, 8),
+    # every num_kv_heads the append covers, query groups up to 32
+    (8, 1), (16, 2), (32, 4), (64, 8), (1, 1), (2, 1), (4, 2), (2, 2), (12, 4), (6, 2),
+    (24, 4), (16, 1), (48, 8), (32, 1), (40, 2), (20, 4)])
 def test_gqa_groupings(cuda, H, hkv):
     import torch
     import eckv
@@ -103,17 +111,62 @@ def test_gqa_groupings(cuda, H, hkv):
         assert_attn_close(got[s], want, f"H{H} hkv{hkv} L{L}")
 
 
-def test_row_scale_mode(cuda):
+@pytest.mark.parametrize("H,hkv", [(16, 4), (8, 1), (16, 2), (64, 8), (32, 4)])
+def test_row_scale_mode(cuda, H, hkv):
     import torch
     import eckv
-    rng = np.random.default_rng(42)
-    lens = [7, 130, 515]
-    seqs = [_make_seq(rng, L, 4, O.SCALE_ROW) for L in lens]
-    q = W.queries(rng, len(lens), 16, D)
-    got, _ = _run_batch(torch, eckv, seqs, q, 16, 4, mode=eckv.SCALE_ROW)
+    rng = np.random.default_rng(42 + H + hkv)
+    lens = [7, 130, 515, 3001]
+    seqs = [_make_seq(rng, L, hkv, O.SCALE_ROW) for L in lens]
+    q = W.queries(rng, len(lens), H, D)
+    got, _ = _run_batch(torch, eckv, seqs, q, H, hkv, mode=eckv.SCALE_ROW)
     for s, L in enumerate(lens):
-        want = O.decode_attention(*seqs[s], L, q[s], 16, 4, D, W.softmax_scale(D), O.SCALE_ROW)
-        assert_attn_close(got[s], want, f"row L{L}")
+        want = O.decode_attention(*seqs[s], L, q[s], H, hkv, D, W.softmax_scale(D), O.SCALE_ROW)
+        assert_attn_close(got[s], want, f"row H{H} hkv{hkv} L{L}")
+
+
+@pytest.mark.parametrize("H,hkv", [(8, 1), (16, 2), (32, 4)])
+def test_small_kv_head_counts_long_ragged(cuda, H, hkv):
+    """One and two KV heads (4-byte scale copies) and split head blocks over
+    long ragged sequences at unaligned slab offsets, split-K included."""
+    import torch
+    import eckv
+    rng = np.random.default_rng(H * 3 + hkv)
+    lens = [20001, 4097, 1, 9999, 0, 15000]
+    seqs = [_make_seq(rng, L, hkv) for L in lens]
+    q = W.queries(rng, len(lens), H, D)
+    got, bc = _run_batch(torch, eckv, seqs, q, H, hkv, caps=[max(L, 3) for L in lens])
+    assert bc.workspace(H)[1] > 0
+    for s, L in enumerate(lens):
+        if L == 0:
+            assert not got[s].any()
+            continue
+        want = O.decode_attention(*seqs[s], L, q[s], H, hkv, D, W.softmax_scale(D))
+        assert_attn_close(got[s], want, f"H{H} hkv{hkv} L{L}")
+
+
+@pytest.mark.parametrize("H,hkv", [(8, 1), (16, 2)])
+def test_kvcache_object_small_kv_head_counts(cuda, H, hkv):
+    """The KVCache object's attention with one and two KV heads."""
+    import torch
+    import eckv
+    rng = np.random.default_rng(H + 100 * hkv)
+    L = 777
+    k = W.kv_rows(rng, L, hkv, D)
+    v = W.kv_rows(rng, L, hkv, D)
+    q = W.queries(rng, 1, H, D)[0]
+    c = eckv.KVCache(num_heads=H, num_kv_heads=hkv, head_dim=D, num_layers=1, max_seq_len=1024)
+    kd, vd = _dev(torch, k), _dev(torch, v)
+    for t in range(L):
+        c.append(0, kd[t], vd[t])
+    out = torch.empty(H * D, dtype=torch.float32, device="cuda")
+    c.attention(0, _dev(torch, q), out, W.softmax_scale(D))
+    torch.cuda.synchronize()
+    kq, ks = O.quantize_kv(k, hkv, D)
+    vq, vs = O.quantize_kv(v, hkv, D)
+    want = O.decode_attention(kq, vq, ks, vs, L, q, H, hkv, D, W.softmax_scale(D))
+    assert_attn_close(out.cpu().numpy().reshape(H, D), want, f"kvcache H{H} hkv{hkv}")
+    c.close()
 
 
 def test_empty_and_single_token_sequences(cuda):
