@@ -34,6 +34,10 @@
 // scores.  K and V codes are exact in f16; p'
 // enters the PV product as an f16 pair hi + lo (two MMAs), about 22 bits, so
 // the only rounding of consequence is Q's bf16 cast (part of the contract).
+// p' = p * v_scale * 2^-E is carried in f16 under a CTA-wide power of two
+// 2^-E chosen from the first tile's largest v-scale and raised (with O
+// rescaled to match) whenever a later tile's v-scales would leave the f16
+// range, so any finite v-scale is in range; the output is O * 2^E / l.
 // Every wait is bounded; a timeout raises a CTA-wide abort flag so that every
 // role stops, waits for its own in-flight work and the CTA frees its tensor
 // memory before returning.  The softmax warps decide together (a barrier
@@ -78,7 +82,7 @@ enum {
     B_KV_FULL = 0, B_KV_EMPTY = 2, B_KC_FULL = 4, B_KC_FREE = 5, B_VC_FULL = 6, B_VC_FREE = 8,
     B_S_FULL = 10, B_P_FULL = 13, B_PV_BUF = 16, B_Q_FULL = 19, B_DRAIN, NBARS
 };
-constexpr int OFF_MISC = OFF_BAR + NBARS * 8;      // [0] tmem base, [1] abort flag
+constexpr int OFF_MISC = OFF_BAR + NBARS * 8;      // [0] tmem base, [1] abort flag, [2] v-scale max
 constexpr int SMEM = 1024 + OFF_MISC + 16;
 static_assert(SMEM <= 227 * 1024, "shared memory budget");
 
@@ -88,6 +92,9 @@ constexpr int TMEM_COLS = 512;
 constexpr int NSP = 3;
 constexpr int TM_O = 384;
 constexpr float kLazyRescale = 8.0f;
+// Largest v_scale * 2^-E a tile may carry: p <= 2^8 under the lazy rescale,
+// so p' stays below 2^15, inside f16 (max 65504) with its hi/lo split.
+constexpr float kVScaleMax = 128.0f;
 constexpr unsigned kFull = 0xffffffffu;
 
 // Instruction descriptors (kind::f16, fp32 accumulate, M = 128, N = 128).
@@ -101,6 +108,7 @@ struct Smem {
         return reinterpret_cast<volatile int*>(base + OFF_MISC) + 1;
     }
     __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(base + OFF_MISC); }
+    __device__ int* vmax_bits() const { return reinterpret_cast<int*>(base + OFF_MISC) + 2; }
 };
 
 // Bounded wait that also gives up as soon as another role has aborted.  The
@@ -381,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(S.bar(B_Q_FULL), 8);
         mbar_init(S.bar(B_DRAIN), 1);
         *S.abort_flag() = 0;
+        *S.vmax_bits() = 0;
         fence_mbar_init();
     }
     if (warp == kMmaWarp) {
@@ -598,6 +607,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         float sc_next = load_scale(0);
         float sc_next2 = ntiles > 1 ? load_scale(1) : 0.0f;   // two tiles ahead
+        // v-scales enter p' times 2^-vexp (CTA-wide; set from tile 0's largest
+        // v-scale, raised when a later tile's would leave the f16 range)
+        int vexp = 0;
+        float v_mul = 1.0f;
         float m_run[4];
         float2 l_run[4];                           // this thread's even / odd columns
 #pragma unroll
@@ -608,15 +621,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (; j < ntiles; ++j) {
             const int sb = j % NSP, par = j & 1;
             float* sck = scb + par * 2 * BN;
-            sck[st] = sc_next * sc_mul;
-            // p' = p * v_scale is carried in f16 with p < 2^8: v-scales of 255
-            // or more could overflow it, so they are flagged
-            if (st >= BN && sc_next >= 255.0f) flag_error(a.err, EC_DEVERR_RANGE);
+            const float raw = sc_next;
+            const bool is_v = st >= BN;
+            sck[st] = raw * (is_v ? v_mul : sc_mul);
+            // tile 0 sets the v-scale exponent; later tiles raise it only
+            // when one of their v-scales would leave p''s f16 range
+            const bool grow = is_v && (j == 0 || raw * v_mul > kVScaleMax);
             sc_next = sc_next2;
             if (j + 2 < ntiles) sc_next2 = load_scale(j + 2);
             bad |= !warp_wait_abortable(S.bar(B_S_FULL + sb), (j / NSP) & 1, abort_flag);
-            // tile j's scales are visible to all, and all agree whether to go on
-            if (bar_any(1, kSoftmaxThreads, bad)) break;
+            // tile j's scales are visible to all, and all agree whether to go
+            // on; failures and exponent changes are rare and share one barrier
+            float ofac = 1.0f;                     // O rescale for a raised exponent
+            if (bar_any(1, kSoftmaxThreads, bad || grow)) {
+                if (bar_any(1, kSoftmaxThreads, bad)) break;
+                int* vmb = S.vmax_bits();
+                if (is_v) atomicMax(vmb, __float_as_int(raw));   // v-scales are >= 0
+                named_bar(1, kSoftmaxThreads);
+                const float vmax = __int_as_float(*vmb);
+                int ex = 0;
+                if (vmax > 0.0f) frexpf(vmax, &ex);   // vmax < 2^ex
+                const int e_new = j == 0 ? min(100, max(-100, ex - 7)) : max(vexp, min(100, ex - 7));
+                if (j > 0) ofac = ldexpf(1.0f, vexp - e_new);
+                vexp = e_new;
+                v_mul = ldexpf(1.0f, -vexp);
+                if (is_v) sck[st] = raw * v_mul;
+                named_bar(1, kSoftmaxThreads);
+                if (st == 0) *vmb = 0;             // next read is past another barrier
+            }
             tc_fence_after();
             float2 ks[8], vs[8];                   // scales of this thread's column pairs
 #pragma unroll
@@ -697,8 +729,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < 4; ++k) neg_m[k] = m_run[k] == -INFINITY ? 0.0f : -m_run[k];
 
             // rescale this half of the O rows only when some row's maximum
-            // jumped (rare): O must first hold every earlier tile
-            if (j >= 1 && __any_sync(kFull, any_corr)) {
+            // jumped or the v-scale exponent rose (rare): O must first hold
+            // every earlier tile
+            if (j >= 1 && (__any_sync(kFull, any_corr) || ofac != 1.0f)) {
                 const int pj = j - 1;
                 if (warp_wait_abortable(S.bar(B_PV_BUF + pj % NSP), (pj / NSP) & 1, abort_flag)) {
                     tc_fence_after();
@@ -711,10 +744,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tmem_ld_16x256b_x2(oa, o);
 #pragma unroll
                             for (int i = 0; i < 8; i += 4) {
-                                o[i] *= corr[2 * blk];
-                                o[i + 1] *= corr[2 * blk];
-                                o[i + 2] *= corr[2 * blk + 1];
-                                o[i + 3] *= corr[2 * blk + 1];
+                                o[i] *= corr[2 * blk] * ofac;
+                                o[i + 1] *= corr[2 * blk] * ofac;
+                                o[i + 2] *= corr[2 * blk + 1] * ofac;
+                                o[i + 3] *= corr[2 * blk + 1] * ofac;
                             }
                             tmem_st_16x256b_x2(oa, o);
                         }
@@ -804,7 +837,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float l = l_sum[k] + red[((ntiles & 1) * 2 + (half ^ 1)) * BM + rw];
                     bool row_live;
                     float* op = out_row(a, rw, row_live) + c0 + 2 * qq;
-                    const float inv = (row_live && l > 0.0f) ? __fdiv_rn(1.0f, l) : 0.0f;
+                    const float inv =
+                        (row_live && l > 0.0f) ? ldexpf(__fdiv_rn(1.0f, l), vexp) : 0.0f;
                     if (row_live) {
 #pragma unroll
                         for (int n = 0; n < 8; ++n)

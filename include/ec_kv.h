@@ -71,7 +71,7 @@ enum {
     EC_DEVERR_OVERFLOW = 2,     /* append would pass a sequence's capacity   */
     EC_DEVERR_TIMEOUT = 3,      /* a bounded device wait ran out             */
     EC_DEVERR_RANGE = 4         /* a value outside a kernel's supported range
-                                   (prefill: a v-scale of 255 or more)      */
+                                   (no current kernel raises it)            */
 };
 
 EC_API int ec_abi_version(void);
@@ -349,8 +349,8 @@ EC_API void ec_cp_comm_destroy(ec_cp_comm* comm);
  * slots [0, len - n_new + i].  q [num_seqs][n_new][num_heads][128] fp32 is cast
  * to bf16 on load (bf16-cast queries); out has the same shape, fp32.  Runs on
  * the tcgen05 tensor cores; head_dim 128, any num_kv_heads dividing num_heads.
- * p' = p * v_scale is carried in f16, so v_scale must stay below 255
- * (|v| below about 32,000); a larger one flags EC_DEVERR_RANGE. */
+ * Any finite v-scale is in range: p' = p * v_scale is carried in f16 under a
+ * power of two that follows the v-scales the kernel meets. */
 EC_API int ec_prefill_attention(const ec_kv_batch* batch, const float* q, float* out,
                                 uint32_t n_new, uint32_t num_heads, float softmax_scale,
                                 ec_stream_t stream);

@@ -164,19 +164,63 @@ def test_prefill_error_against_raw_fp32_queries(cuda):
     assert er < 0.1, er
 
 
-def test_prefill_flags_v_scales_out_of_range(cuda):
-    """v-scales of 255 or more (|v| near 32,000 and above) are outside the
-    f16 range of p' = p * v_scale: the kernel flags EC_DEVERR_RANGE."""
+def _value_range_case(torch, eckv, past, n_new, vmod, seed):
+    """Prefill with V values modified by vmod(v_past, v_new) before
+    quantization; returns (got, want) for every row against the oracle's
+    decode loop over the row's causal prefix with the bf16-cast query."""
+    rng = np.random.default_rng(seed)
+    H, hkv = 16, 4
+    kp, vp = W.kv_rows(rng, past, hkv, D), W.kv_rows(rng, past, hkv, D)
+    kn, vn = W.kv_rows(rng, n_new, hkv, D), W.kv_rows(rng, n_new, hkv, D)
+    vp, vn = vmod(vp, vn)
+    bc = eckv.BatchCache([past + n_new], num_kv_heads=hkv)
+    if past:
+        kq, ks = O.quantize_kv(kp, hkv, D)
+        vq, vs = O.quantize_kv(vp, hkv, D)
+        fill_batch(bc, [(kq, vq, ks, vs)])
+    bc.append(torch.from_numpy(kn[None]).cuda(), torch.from_numpy(vn[None]).cuda(), n_new)
+    q = W.queries(rng, n_new, H, D)[None]
+    out = torch.empty((1, n_new, H, D), device="cuda")
+    bc.prefill(torch.from_numpy(q).cuda(), out, n_new, H, W.softmax_scale(D))
+    torch.cuda.synchronize()
+    assert bc.device_error() == 0
+    K = np.concatenate([kp, kn]) if past else kn
+    V = np.concatenate([vp, vn]) if past else vn
+    kq, ks = O.quantize_kv(K, hkv, D)
+    vq, vs = O.quantize_kv(V, hkv, D)
+    qb = _bf16_round(q)[0]
+    got = out.cpu().numpy()[0]
+    want = np.stack([O.decode_attention(kq, vq, ks, vs, past + i + 1, qb[i], H, hkv, D,
+                                        W.softmax_scale(D)) for i in range(n_new)])
+    return got, want
+
+
+def test_prefill_large_v_scales_in_range(cuda):
+    """v-scales far above the f16 range of p = softmax weight (|v| in the
+    hundreds of thousands, in the first tile and first met in a later tile):
+    the CTA-wide power of two on p' * v_scale follows them, O is rescaled
+    when it rises, and the rows match the oracle."""
     import torch
     import eckv
-    n_new = 64
-    bc = eckv.BatchCache([n_new], num_kv_heads=4)
-    k = torch.randn(1, n_new, 4 * D, device="cuda")
-    v = torch.randn(1, n_new, 4 * D, device="cuda")
-    v[0, 10] *= 20000.0                               # one token's v-scale near 600
-    bc.append(k, v, n_new)
-    q = torch.randn(1, n_new, 16, D, device="cuda")
-    out = torch.empty(1, n_new, 16, D, device="cuda")
-    bc.prefill(q, out, n_new, 16, W.softmax_scale(D))
-    torch.cuda.synchronize()
-    assert bc.device_error() == eckv.DEVERR_RANGE
+
+    def big(vp, vn):
+        vn = vn.copy()
+        vn[10] *= 20000.0          # tile 0 of the chunk (past 0)
+        vn[300] *= 3.0e5           # first met in tile 2: the exponent rises mid-row
+        vn[301:310] *= 1.0e3
+        return vp, vn
+    got, want = _value_range_case(torch, eckv, 0, 384, big, 61)
+    assert_attn_close(got, want, "large v")
+    got, want = _value_range_case(torch, eckv, 200, 140, lambda vp, vn: (vp * 4.0e4, vn), 62)
+    assert_attn_close(got, want, "large v in the cached part")
+
+
+def test_prefill_tiny_v_scales_keep_relative_precision(cuda):
+    """|v| around 1e-4: p' sits far below f16's normal range without the
+    power of two; with it the rows keep their relative precision."""
+    import torch
+    import eckv
+    got, want = _value_range_case(torch, eckv, 130, 200,
+                                  lambda vp, vn: (vp * 1.0e-4, vn * 1.0e-4), 63)
+    err = float(np.abs(got - want).max())
+    assert err <= 1e-3 * float(np.abs(want).max()), err
