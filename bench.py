@@ -685,18 +685,27 @@ def run_cp_arm(args, rank, world, local_rank):
     scale = W.softmax_scale(D)
     stream = torch.cuda.current_stream()
 
-    fused = world > 1 and not args.cp_nccl
-    cx = ranks.CPExchange(1, H) if fused else None
+    # N > 1: the decode kernel, then one kernel that merges this rank's split-K
+    # chunks, exchanges the state over peer memory and merges the ranks (two
+    # launches a step); --cp-unfused keeps the chunk merge as its own launch
+    # before the exchange; --cp-nccl exchanges with an NCCL all-gather.
+    # N = 1: the plain decode (decode + chunk merge).
+    peer = world > 1 and not args.cp_nccl
+    fused = peer and not args.cp_unfused
+    cx = ranks.CPExchange(1, H) if peer else None
 
     def step():
-        bc.decode_partial(qg, po_local, pml_local, H, scale, stream)
+        if world == 1:
+            bc.decode(qg, out, H, scale, stream)
+            return
         if fused:
+            cx.decode_exchange(bc, qg, out, H, scale, stream)
+            return
+        bc.decode_partial(qg, po_local, pml_local, H, scale, stream)
+        if peer:
             cx.combine(po_local, pml_local, out, stream)     # exchange + merge, one kernel
             return
-        if world > 1:
-            po, pml = ranks.gather_partials(po_local, pml_local)
-        else:
-            po, pml = po_local[None], pml_local[None]
+        po, pml = ranks.gather_partials(po_local, pml_local)
         eckv.lse_combine(po, pml, world, 1, H, D, out, stream)
 
     for _ in range(args.warmup):
@@ -744,8 +753,10 @@ def run_cp_arm(args, rank, world, local_rank):
             "ms_per_step": round(float(t[0]) / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": cfg.name, "ctx": total, "parallelism": f"context-split x{world}",
-                       "exchange": ("peer stores + merge in one kernel (ec_cp_exchange_combine)"
-                                    if fused else "NCCL all-gather + ec_lse_combine"
+                       "exchange": ("chunk merge + peer stores + rank merge in one kernel "
+                                    "(ec_cp_decode_exchange)" if fused else
+                                    "peer stores + merge in one kernel (ec_cp_exchange_combine)"
+                                    if peer else "NCCL all-gather + ec_lse_combine"
                                     if world > 1 else "none"),
                        "launch": "CUDA graph replay" if use_graph else "eager"},
             "pct_of_hbm_peak": round(100 * gbs / (peak * world), 1)}), flush=True)
@@ -771,6 +782,9 @@ def main():
                          "replaying the step as a captured CUDA graph")
     ap.add_argument("--cp-nccl", action="store_true",
                     help="config 4: exchange partials with an NCCL all-gather instead of peer stores")
+    ap.add_argument("--cp-unfused", action="store_true",
+                    help="config 4: merge each rank's split-K chunks in their own launch before "
+                         "the peer exchange")
     ap.add_argument("--kv-fp32", action="store_true",
                     help="decode over the fp32 cache mode (one sequence per rank)")
     args = ap.parse_args()

@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
     const int g0 = blockIdx.x * HC;                  // first KV head of this CTA
     const int chunk = blockIdx.y;
     const int seq = blockIdx.z;
-    const bool direct = a.max_chunks == 1;
+    const bool direct = a.max_chunks == 1 && a.mode != kChunks;
     pdl_wait();  // the append before this kernel writes the lengths and the codes
     pdl_trigger();
     int32_t off, cap, len;
@@ -647,18 +647,24 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
     }
 }
 
-// Merges the chunk partials of one (sequence, head).  4 warps per dim group:
-// the chunk weights 2^(m_c - M) are computed once into shared memory, then
-// each of kCombineSplit thread groups sums a quarter of the chunks for every
-// dim (independent loads, so a long chunk list is not one serial chain).  A
-// thread covers dim d of each of the head's DV 128-dim blocks.
+// Merges the chunk partials of one (sequence, head) in three passes over the
+// chunks, each spread over the block's threads: the maximum M of the chunk
+// maxima, the weights 2^(m_c - M) (kept in shared memory) with the weighted
+// sum of l, then O, where each of kCombineSplit thread groups sums every
+// kCombineSplit-th chunk for every dim (independent loads, so a long chunk
+// list is not one serial chain).  A thread covers dim d of each of the
+// head's DV 128-dim blocks.  Reductions run in a fixed order: the result
+// does not depend on timing.
 constexpr int kCombineSplit = 4;
-static_assert(D * kCombineSplit >= 256, "one thread per chunk: the plan allows 256 chunks");
+constexpr int kCombineThreads = D * kCombineSplit;
+constexpr int kMaxChunks = 1024;                   // split-K chunks per sequence, at most
 template <int DV>
-__global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeArgs a) {
     constexpr int DH = D * DV;
+    constexpr int kWarpsC = kCombineThreads / 32;
     const int seq = blockIdx.x, h = blockIdx.y;
-    const int d = threadIdx.x % D, part = threadIdx.x / D;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int d = tid % D, part = tid / D;
     const int H = a.num_heads;
     pdl_wait();  // the partials of decode_kernel
     pdl_trigger();
@@ -666,31 +672,46 @@ __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const Decode
     if (!load_entry(a, seq, off, cap, len)) return;  // flagged by decode_kernel
     const int nch = (len + a.chunk_tokens - 1) / a.chunk_tokens;
     const size_t base = (size_t)seq * a.max_chunks * H + h;
-    __shared__ float s_f[256], s_l[256], s_red[DH * kCombineSplit];
-    __shared__ float s_M;
-    // chunk maxima -> M (the plan keeps nch <= 256 < the block's threads, so
-    // thread c holds chunk c's (m, l) from the one load)
-    const bool has_c = threadIdx.x < nch;
-    float2 mlc = make_float2(-INFINITY, 0.0f);
-    if (has_c) mlc = *reinterpret_cast<const float2*>(a.part_ml + (base + (size_t)threadIdx.x * H) * 2);
-    float m = mlc.x;
+    __shared__ float s_f[kMaxChunks], s_red[DH * kCombineSplit];
+    __shared__ float s_M, s_L;
+    auto ml_of = [&](int c) {
+        return *reinterpret_cast<const float2*>(a.part_ml + (base + (size_t)c * H) * 2);
+    };
+    // pass 1: M = max over the chunk maxima
+    float m = -INFINITY;
+    for (int c = tid; c < nch; c += kCombineThreads) m = fmaxf(m, ml_of(c).x);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
+    if (lane == 0) s_red[wid] = m;
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         float M = -INFINITY;
-        for (int w = 0; w < D * kCombineSplit / 32; ++w) M = fmaxf(M, s_red[w]);
+        for (int w = 0; w < kWarpsC; ++w) M = fmaxf(M, s_red[w]);
         s_M = M;
     }
     __syncthreads();
     const float M = s_M;
-    if (has_c) {
+    // pass 2: chunk weights and sum_c 2^(m_c - M) * l_c
+    float lsum = 0.0f;
+    for (int c = tid; c < nch; c += kCombineThreads) {
+        const float2 mlc = ml_of(c);
         const float f = mlc.x == -INFINITY ? 0.0f : exp2f(mlc.x - M);
-        s_f[threadIdx.x] = f;
-        s_l[threadIdx.x] = f * mlc.y;
+        s_f[c] = f;
+        lsum += f * mlc.y;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    __syncthreads();                                   // s_red's maxima are read
+    if (lane == 0) s_red[wid] = lsum;
+    __syncthreads();
+    if (tid == 0) {
+        float L = 0.0f;
+        for (int w = 0; w < kWarpsC; ++w) L += s_red[w];
+        s_L = L;
     }
     __syncthreads();
+    const float sl = s_L;
+    // pass 3: O
     float so[DV];
 #pragma unroll
     for (int dv = 0; dv < DV; ++dv) so[dv] = 0.0f;
@@ -704,8 +725,6 @@ __global__ void __launch_bounds__(D * kCombineSplit) combine_kernel(const Decode
     for (int dv = 0; dv < DV; ++dv) s_red[part * DH + dv * D + d] = so[dv];
     __syncthreads();
     if (part != 0) return;
-    float sl = 0.0f;
-    for (int c = 0; c < nch; ++c) sl += s_l[c];
 #pragma unroll
     for (int dv = 0; dv < DV; ++dv) {
         float sum = 0.0f;
@@ -867,7 +886,7 @@ DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t tota
     if (max_seq_len <= 0 || num_seqs <= 0) return best;
     const int tiles = (max_seq_len + T - 1) / T;
     double best_cost = 1e300;
-    const int kmax = tiles < 256 ? tiles : 256;
+    const int kmax = tiles < kMaxChunks ? tiles : kMaxChunks;
     // with a token count below the all-full batch, the CTAs that find work
     // are about total / chunk plus half a chunk per sequence; the others exit
     // at once (about 16 tokens' worth of time each)
@@ -903,7 +922,7 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
                           cudaStream_t st) {
     a.chunk_tokens = plan.chunk_tokens;
     a.max_chunks = plan.max_chunks;
-    if (plan.max_chunks > 1) {
+    if (plan.max_chunks > 1 || a.mode == kChunks) {
         a.part_o = static_cast<float*>(ws);
         a.part_ml = a.part_o + (size_t)a.num_seqs * plan.max_chunks * a.num_heads * a.head_dim;
     }
@@ -916,8 +935,8 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
         e = launch_decode_t<HC_, QW_, SCW_, DV_>(a, plan, st);
     EC_DECODE_VARIANTS(EC_DEC)
 #undef EC_DEC
-    if (e != cudaSuccess || plan.max_chunks <= 1) return e;
-    const dim3 cg(a.num_seqs, a.num_heads), cb(D * kCombineSplit);
+    if (e != cudaSuccess || plan.max_chunks <= 1 || a.mode == kChunks) return e;
+    const dim3 cg(a.num_seqs, a.num_heads), cb(kCombineThreads);
     return v.dv == 1 ? launch_pdl(combine_kernel<1>, cg, cb, 0, st, a)
                      : launch_pdl(combine_kernel<2>, cg, cb, 0, st, a);
 }

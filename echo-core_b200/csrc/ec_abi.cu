@@ -624,6 +624,29 @@ void ec_cp_comm_destroy(ec_cp_comm* c) {
     delete c;
 }
 
+// Checks a comm for a step with the given epoch and fills the exchange
+// arguments common to both exchange entry points.
+static int cp_step_args(ec_cp_comm* c, uint32_t epoch, float* out, const char* who,
+                        ec::CpExchangeArgs& a) {
+    if (!c->opened && c->world > 1) return fail(EC_ERR_INVALID_ARGUMENT, "%s: comm not opened", who);
+    const int mode = epoch == 0 ? 2 : 1;
+    if (c->epoch_mode != 0 && c->epoch_mode != mode)
+        return fail(EC_ERR_INVALID_ARGUMENT,
+                    "%s: a comm uses caller epochs or device epochs (0), not both", who);
+    c->epoch_mode = mode;
+    a = ec::CpExchangeArgs{};
+    for (int r = 0; r < c->world; ++r) a.peer_base[r] = c->peers[r];
+    a.out = out;
+    a.err = nullptr;
+    a.world = c->world;
+    a.rank = c->rank;
+    a.num_seqs = c->num_seqs;
+    a.num_heads = c->num_heads;
+    a.epoch = epoch;
+    a.epoch_dev = mode == 2 ? c->epoch_dev : nullptr;
+    return EC_OK;
+}
+
 int ec_cp_exchange_combine(ec_cp_comm* c, const float* part_o, const float* part_ml,
                            uint32_t epoch, float* out, ec_stream_t stream) {
     if (!c || !part_o || !part_ml || !out)
@@ -649,6 +672,73 @@ int ec_cp_exchange_combine(ec_cp_comm* c, const float* part_o, const float* part
     a.epoch_dev = mode == 2 ? c->epoch_dev : nullptr;
     cudaError_t e = ec::launch_cp_exchange(a, as_stream(stream));
     return e == cudaSuccess ? EC_OK : cuda_fail(e, "cp_exchange_combine launch");
+}
+
+size_t ec_cp_decode_workspace_size(const ec_kv_batch* b, uint32_t num_heads) {
+    if (!b) return 0;
+    const ec::DecodePlan p = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len,
+                                             num_sms_current(), b->total_tokens_hint,
+                                             (int)b->num_kv_heads, (int)num_heads,
+                                             (int)b->head_dim);
+    const int chunks = p.max_chunks > 1 ? p.max_chunks : 1;
+    return (size_t)b->num_seqs * chunks * num_heads * (b->head_dim + 2) * sizeof(float);
+}
+
+int ec_cp_decode_exchange(ec_cp_comm* c, const ec_kv_batch* b, const float* q,
+                          uint32_t num_heads, float softmax_scale, void* workspace,
+                          size_t workspace_bytes, uint32_t epoch, float* out,
+                          ec_stream_t stream) {
+    const char* who = "cp_decode_exchange";
+    if (!c) return fail(EC_ERR_INVALID_ARGUMENT, "%s: comm is NULL", who);
+    int rc = ec::check_batch(b, who);
+    if (rc) return rc;
+    if (!q || !out || !workspace) return fail(EC_ERR_INVALID_ARGUMENT, "%s: q/out/workspace NULL", who);
+    if (b->num_seqs != (uint32_t)c->num_seqs || num_heads != (uint32_t)c->num_heads)
+        return fail(EC_ERR_INVALID_ARGUMENT, "%s: batch of %u sequences x %u heads, comm made for %d x %d",
+                    who, b->num_seqs, num_heads, c->num_seqs, c->num_heads);
+    if (b->head_dim != 128 || !decode_shape_supported(num_heads, b->num_kv_heads, b->head_dim))
+        return fail(EC_ERR_UNSUPPORTED, "%s: needs head_dim 128 and a decode-kernel GQA shape", who);
+    if (!aligned16(q) || !aligned16(out) || !aligned16(workspace))
+        return fail(EC_ERR_MISALIGNED, "%s: q/out/workspace not 16-byte aligned", who);
+    const ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len,
+                                                num_sms_current(), b->total_tokens_hint,
+                                                (int)b->num_kv_heads, (int)num_heads, 128);
+    const size_t need = ec_cp_decode_workspace_size(b, num_heads);
+    if (workspace_bytes < need)
+        return fail(EC_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", who, need,
+                    workspace_bytes);
+    ec::CpExchangeArgs x;
+    if ((rc = cp_step_args(c, epoch, out, who, x)) != EC_OK) return rc;
+    ec::DecodeArgs a{};
+    a.keys = b->keys;
+    a.values = b->values;
+    a.key_scales = b->key_scales;
+    a.val_scales = b->val_scales;
+    a.seq_offset = b->seq_offset;
+    a.seq_capacity = b->seq_capacity;
+    a.seq_len = b->seq_len;
+    a.err = b->error_word;
+    a.total_slots = b->total_slots;
+    a.pages = ec::page_map_of(b);
+    a.q = q;
+    a.out = out;
+    a.q_mul = softmax_scale;
+    a.num_seqs = (int)b->num_seqs;
+    a.num_heads = (int)num_heads;
+    a.head_dim = 128;
+    a.row_scales = b->scale_mode == EC_SCALE_ROW;
+    a.mode = ec::kChunks;
+    cudaStream_t st = as_stream(stream);
+    cudaError_t e = ec::launch_decode(a, (int)b->num_kv_heads, plan, workspace, st);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    x.part_o = static_cast<const float*>(workspace);
+    x.part_ml = x.part_o + (size_t)b->num_seqs * plan.max_chunks * num_heads * 128;
+    x.err = b->error_word;
+    x.seq_len = b->seq_len;
+    x.chunk_tokens = plan.chunk_tokens;
+    x.max_chunks = plan.max_chunks;
+    e = ec::launch_cp_exchange(x, st);
+    return e == cudaSuccess ? EC_OK : cuda_fail(e, who);
 }
 
 // ------------------------------------------------------------ batched cache

@@ -118,7 +118,10 @@ struct DecodeArgs {
     PageMap pages;
 };
 
-enum { kOut = 0, kPartial = 1 };
+// kOut: normalised output; kPartial: (m, l, O) per (sequence, head);
+// kChunks: every chunk's (m, l, O) left in the workspace (unsplit plans too),
+// for the exchange kernel to merge.
+enum { kOut = 0, kPartial = 1, kChunks = 2 };
 
 cudaError_t launch_quantize_rows(const float* in, int8_t* out, float* scales, uint32_t rows,
                                  uint32_t n, cudaStream_t st);
@@ -203,6 +206,12 @@ struct CpExchangeArgs {
     int world, rank, num_seqs, num_heads;
     uint32_t epoch;
     uint32_t* epoch_dev;             // non-null: [num_seqs][num_heads] epochs kept on the device
+    // max_chunks > 0: part_o / part_ml are the decode kernel's split-K chunk
+    // partials of this rank's slice ([num_seqs*max_chunks][num_heads][..]),
+    // merged in the exchange kernel; sequence s has ceil(seq_len[s] /
+    // chunk_tokens) of them
+    const int32_t* seq_len;
+    int chunk_tokens, max_chunks;
 };
 size_t cp_exchange_buffer_bytes(int world, int num_seqs, int num_heads);
 cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st);

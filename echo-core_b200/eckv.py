@@ -55,6 +55,7 @@ EXPORTS = (
     "ec_kv_cache_snapshot_size", "ec_kv_cache_snapshot", "ec_kv_cache_restore",
     "ec_kv_batch_append_rope", "ec_rope_rows",
     "ec_cp_comm_create", "ec_cp_comm_open", "ec_cp_exchange_combine", "ec_cp_comm_destroy",
+    "ec_cp_decode_workspace_size", "ec_cp_decode_exchange",
 )
 
 
@@ -145,6 +146,9 @@ def lib() -> ctypes.CDLL:
             "ec_lse_combine": ([vp, vp, u32, u32, u32, u32, vp, vp], i32),
             "ec_prefill_attention": ([ctypes.POINTER(KVBatch), vp, vp, u32, u32, f, vp], i32),
             "ec_decode_attention_noalloc": ([ctypes.POINTER(KVBatch), vp, vp, u32, f, vp], i32),
+            "ec_cp_decode_workspace_size": ([ctypes.POINTER(KVBatch), u32], ctypes.c_size_t),
+            "ec_cp_decode_exchange": ([vp, ctypes.POINTER(KVBatch), vp, u32, f, vp, ctypes.c_size_t,
+                                       ctypes.c_uint32, vp, vp], i32),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -140,6 +140,26 @@ class CPExchange:
             ctypes.c_uint32(0 if self.device_epoch else self.epoch), eckv._ptr(out),
             eckv._stream(stream)))
 
+    def decode_exchange(self, batch, q, out, num_heads: int, softmax_scale: float,
+                        stream=None) -> None:
+        """One context-parallel decode step in two launches
+        (ec_cp_decode_exchange): decode of this rank's slice held in `batch`
+        (a BatchCache of this comm's sequences) with the split-K chunk merge,
+        the exchange and the rank merge done by one kernel."""
+        import ctypes
+        import torch
+        import eckv
+        self.epoch += 1
+        d = batch.desc()
+        need = self._lib.ec_cp_decode_workspace_size(ctypes.byref(d), num_heads)
+        ws = getattr(self, "_ws", None)
+        if ws is None or ws.numel() < need:
+            ws = self._ws = torch.empty(max(need, 16), dtype=torch.uint8, device=batch.keys.device)
+        eckv.check(self._lib.ec_cp_decode_exchange(
+            self._h, ctypes.byref(d), eckv._ptr(q), num_heads, ctypes.c_float(softmax_scale),
+            eckv._ptr(ws), ws.numel(), ctypes.c_uint32(0 if self.device_epoch else self.epoch),
+            eckv._ptr(out), eckv._stream(stream)))
+
     def close(self) -> None:
         if not getattr(self, "_h", None) or not self._h.value:
             return

@@ -340,6 +340,22 @@ EC_API int ec_cp_exchange_combine(ec_cp_comm* comm, const float* part_o, const f
                                   uint32_t epoch, float* out, ec_stream_t stream);
 EC_API void ec_cp_comm_destroy(ec_cp_comm* comm);
 
+/* One context-parallel decode step in two launches per rank: the decode
+ * kernel over this rank's slice (batch: the comm's num_seqs sequences, each
+ * holding this rank's contiguous share of its tokens), leaving its split-K
+ * chunk partials in `workspace`, then the exchange kernel, which merges those
+ * chunks into this rank's (m, l, O), stores it into every rank's buffer and
+ * merges the world's states in rank order into out [num_seqs][num_heads][128]
+ * -- the output ec_decode_attention_partial + ec_cp_exchange_combine give,
+ * without their separate chunk-merge launch.  head_dim 128; num_heads must
+ * be the comm's; epoch as ec_cp_exchange_combine (0: device epochs).
+ * workspace: device, ec_cp_decode_workspace_size bytes. */
+EC_API size_t ec_cp_decode_workspace_size(const ec_kv_batch* batch, uint32_t num_heads);
+EC_API int ec_cp_decode_exchange(ec_cp_comm* comm, const ec_kv_batch* batch, const float* q,
+                                 uint32_t num_heads, float softmax_scale, void* workspace,
+                                 size_t workspace_bytes, uint32_t epoch, float* out,
+                                 ec_stream_t stream);
+
 /* Chunked-prefill attention.  The reference has no chunked prefill: it feeds
  * a prompt one token at a time (src/main.cpp:404-405), each token running the
  * decode loop of src/inference.cpp:321-392 over the cache as it stands after

@@ -87,13 +87,68 @@ def test_single_rank_device_epoch_replays_as_a_graph(cuda):
     cx.close()
 
 
+@pytest.mark.parametrize("L", [3000, 200000])
+def test_single_rank_fused_decode_exchange(cuda, L):
+    """ec_cp_decode_exchange on one rank: the decode kernel's split-K chunks
+    (one chunk at 3,000 tokens, several hundred at 200,000) merged inside the
+    exchange kernel give the oracle's output, step after step."""
+    import torch
+    import eckv
+    import ranks
+    from _util import fill_batch
+    kq, vq, ks, vs, q = _seq(L, 11)
+    bc = eckv.BatchCache([L], num_kv_heads=HKV)
+    fill_batch(bc, [(kq, vq, ks, vs)])
+    cx = ranks.CPExchange(1, H)
+    out = torch.empty((1, H, D), device="cuda")
+    want = O.decode_attention(kq, vq, ks, vs, L, q[0], H, HKV, D, W.softmax_scale(D))
+    qd = torch.from_numpy(q).cuda()
+    for step in range(3):
+        out.fill_(7.0)
+        cx.decode_exchange(bc, qd, out, H, W.softmax_scale(D))
+        torch.cuda.synchronize()
+        assert eckv.device_error() == 0 and bc.device_error() == 0
+        assert_attn_close(out.cpu().numpy()[0], want, f"fused x1 L{L} step {step}")
+    cx.close()
+
+
+def test_single_rank_fused_step_replays_as_a_graph(cuda):
+    import torch
+    import eckv
+    import ranks
+    from _util import fill_batch
+    L = 50000
+    kq, vq, ks, vs, q = _seq(L, 12)
+    bc = eckv.BatchCache([L], num_kv_heads=HKV)
+    fill_batch(bc, [(kq, vq, ks, vs)])
+    cx = ranks.CPExchange(1, H, device_epoch=True)
+    out = torch.zeros((1, H, D), device="cuda")
+    qd = torch.from_numpy(q).cuda()
+    cx.decode_exchange(bc, qd, out, H, W.softmax_scale(D))      # workspace, epoch 1
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.graph(g, stream=side):
+        cx.decode_exchange(bc, qd, out, H, W.softmax_scale(D), torch.cuda.current_stream())
+    want = O.decode_attention(kq, vq, ks, vs, L, q[0], H, HKV, D, W.softmax_scale(D))
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert eckv.device_error() == 0
+        assert_attn_close(out.cpu().numpy()[0], want, "fused x1 graph")
+    del g
+    cx.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _rank_worker(rank, world, port, L, result, same_gpu_timeout, graph=False):
+def _rank_worker(rank, world, port, L, result, same_gpu_timeout, graph=False, fused=False):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     for sub in ("oracle", "echo-core_b200", "tests"):
@@ -123,6 +178,16 @@ def _rank_worker(rank, world, port, L, result, same_gpu_timeout, graph=False):
                 code = eckv.device_error()
                 np.save(result, np.array([code, float(np.abs(out.cpu().numpy()).max())]))
             dist.barrier()
+        elif fused:
+            # decode + chunk merge + exchange in two launches per rank
+            from _util import fill_batch
+            sb = eckv.BatchCache([max(hi - lo, 1)], num_kv_heads=HKV, device=dev)
+            fill_batch(sb, [(kq[lo:hi], vq[lo:hi], ks[lo:hi], vs[lo:hi])])
+            qd = torch.from_numpy(q).to(dev)
+            for _ in range(3):
+                cx.decode_exchange(sb, qd, out, H, W.softmax_scale(D))
+            torch.cuda.synchronize()
+            assert sb.device_error() == 0
         elif graph:
             # every rank captures its step once and replays it: device epochs
             cx.combine(po, pml, out)
@@ -153,12 +218,13 @@ def _rank_worker(rank, world, port, L, result, same_gpu_timeout, graph=False):
         dist.destroy_process_group()
 
 
-def _spawn(tmp_path, same_gpu_timeout, L=20000, world=2, graph=False):
+def _spawn(tmp_path, same_gpu_timeout, L=20000, world=2, graph=False, fused=False):
     import torch.multiprocessing as mp
     out = str(tmp_path / "r.npy")
     ctx = mp.get_context("spawn")
     port = _free_port()
-    ps = [ctx.Process(target=_rank_worker, args=(r, world, port, L, out, same_gpu_timeout, graph))
+    ps = [ctx.Process(target=_rank_worker,
+                      args=(r, world, port, L, out, same_gpu_timeout, graph, fused))
           for r in range(world)]
     for p in ps:
         p.start()
@@ -207,3 +273,15 @@ def test_missing_rank_times_out_with_an_error_status(cuda, tmp_path):
     code, amax = _spawn(tmp_path, True, L=2000)
     assert code == eckv.DEVERR_TIMEOUT
     assert amax == 0.0
+
+
+def test_ranks_fused_decode_exchange(cuda, tmp_path):
+    """ec_cp_decode_exchange across ranks, one per visible GPU (2 to 8): each
+    rank decodes its contiguous slice; chunk merge, exchange and rank merge
+    run in one kernel; the merged output matches the oracle."""
+    import torch
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    code, err, ok = _spawn(tmp_path, False, L=60000, world=world, fused=True)
+    assert code == 0 and ok == 1.0, (code, err)
