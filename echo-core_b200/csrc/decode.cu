@@ -52,6 +52,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyRescale = 8.0f;
 constexpr unsigned kFull = 0xffffffffu;
 
+constexpr int kMaxChunks = 1024;                   // split-K chunks (or pieces) per sequence, at most
+constexpr int kStreamMaxSeqs = 1024;               // stream-K plans: batches up to this size
+constexpr int kStreamMinSeqs = 32;                 // ... and from this size
+
 constexpr int kResidentSmem = 228 * 1024;   // shared memory per SM
 constexpr int kCtaReservedSmem = 1024;      // reserved by the system per resident CTA
 
@@ -209,24 +213,27 @@ __device__ __forceinline__ void issue_boxes(const CUtensorMap* tk, const CUtenso
         }
 }
 
+// The ring slot of a CTA's j-th tile overall is j % kStages: a CTA that
+// streams several pieces (stream-K) keeps counting across them.  `tok` is the
+// tile's first token in its sequence, ntok its tokens (<= 32).
 template <int HC, int QW, int SCW, int DV>
-__device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMap* tk,
-                                           const CUtensorMap* tv, uint8_t* stages, uint64_t* full,
-                                           uint64_t* empty, int j, int n, int seq, int32_t off,
-                                           int t0, int g0, uint64_t pol, int lane) {
+__device__ __forceinline__ bool issue_tile_at(const DecodeArgs& a, const CUtensorMap* tk,
+                                              const CUtensorMap* tv, uint8_t* stages,
+                                              uint64_t* full, uint64_t* empty, int j, int ntok,
+                                              int seq, int32_t off, int tok, int g0, uint64_t pol,
+                                              int lane) {
     using G = Geo<HC, QW, SCW, DV>;
     const int s = j % G::kStages;
     bool ok = true;
     if (lane == 0 && j >= G::kStages) ok = mbar_wait(&empty[s], ((j / G::kStages) - 1) & 1);
     ok = __shfl_sync(kFull, ok, 0);
     if (!ok) return false;
-    const int ntok = min(T, n - j * T);
-    const int hkv = a.num_kv_heads;
+    constexpr int hkv = SCW;   // the cache's num_kv_heads: variants are chosen by it
     // a tile never crosses a page (pages are multiples of 128 tokens); a bad
     // page id is flagged and slot 0 read instead, so that the pipeline still
     // completes and nothing outside the pool is touched
     int64_t slot;
-    if (!page_slot(a.pages, seq, off, t0 + j * T, a.total_slots, slot)) {
+    if (!page_slot(a.pages, seq, off, tok, a.total_slots, slot)) {
         if (lane == 0) flag_error(a.err, EC_DEVERR_BAD_TABLE);
         slot = 0;
     }
@@ -280,6 +287,295 @@ __device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMa
 }
 
 template <int HC, int QW, int SCW, int DV>
+__device__ __forceinline__ bool issue_tile(const DecodeArgs& a, const CUtensorMap* tk,
+                                           const CUtensorMap* tv, uint8_t* stages, uint64_t* full,
+                                           uint64_t* empty, int j, int n, int seq, int32_t off,
+                                           int t0, int g0, uint64_t pol, int lane) {
+    return issue_tile_at<HC, QW, SCW, DV>(a, tk, tv, stages, full, empty, j, min(T, n - j * T),
+                                          seq, off, t0 + j * T, g0, pol, lane);
+}
+
+// ---------------------------------------------------------- warp roles
+// The QK and PV warps' work, shared by the chunked kernel (one piece of one
+// sequence per CTA) and the stream-K kernel (a CTA's pieces back to back).
+// `i` counts a CTA's tiles overall: it selects the ring stage and the p'
+// buffer and their phases, so a CTA may run any number of pieces in a row.
+
+// q of the quad's query heads (gkv + hkv * (jb + h), h < 4) of sequence seq
+// as int8 B fragments of a 24-bit per-head fixed-point scale: column n =
+// gid <-> (head jb + (gid >> 1), digit), thread t4 holds dims [32*t4, +32)
+// of every 128-dim block, k-step j covers 8 of them (block j / 4).  Returns
+// the fixed-point step of head jb + t4.
+template <int DV>
+__device__ __forceinline__ float qk_load_q(const DecodeArgs& a, int seq, int gkv, int jb,
+                                           int group, int hkv, int lane,
+                                           uint32_t (&b_hi)[4 * DV][2], uint32_t (&b_lo)[4 * DV][2]) {
+    constexpr int DH = D * DV;
+    const int gid = lane >> 2, t4 = lane & 3;
+    float sq_own;
+    {
+        const int hq = gid >> 1;
+        const bool live = jb + hq < group;
+        // a quad past the group's end (groups that are not a multiple of
+        // 4) reads query head 0 of the group and keeps no column live
+        const float* qp =
+            a.q + ((size_t)seq * a.num_heads + gkv + hkv * (live ? jb + hq : 0)) * DH + 32 * t4;
+        auto scaled = [&](float v) { return __fmul_rn(__fmul_rn(v, a.q_mul), kLog2e); };
+        // the head's absmax over all its blocks, then the digits block by
+        // block: at head_dim 128 from the values kept in registers, at 256 by
+        // loading each block again (L1 hits)
+        float amax = 0.0f;
+        float qv1[32];
+#pragma unroll
+        for (int dv = 0; dv < DV; ++dv)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float4 v = reinterpret_cast<const float4*>(qp + dv * D)[e];
+                const float x0 = scaled(v.x), x1 = scaled(v.y), x2 = scaled(v.z), x3 = scaled(v.w);
+                if (DV == 1) {
+                    qv1[4 * e + 0] = x0;
+                    qv1[4 * e + 1] = x1;
+                    qv1[4 * e + 2] = x2;
+                    qv1[4 * e + 3] = x3;
+                }
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(x0), fabsf(x1)), fmaxf(fabsf(x2), fabsf(x3))));
+            }
+        amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+        const float kQMax = 8323072.0f;  // 2^23 - 2^16 keeps d0 in [-128, 127]
+        const float inv = amax > 0.0f ? __fdiv_rn(kQMax, amax) : 0.0f;
+        sq_own = amax > 0.0f ? __fdiv_rn(amax, kQMax) : 0.0f;
+        const bool odd = gid & 1;
+#pragma unroll
+        for (int dv = 0; dv < DV; ++dv) {
+            float qv[32];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                if (DV == 1) {
+                    qv[4 * e + 0] = qv1[4 * e + 0];
+                    qv[4 * e + 1] = qv1[4 * e + 1];
+                    qv[4 * e + 2] = qv1[4 * e + 2];
+                    qv[4 * e + 3] = qv1[4 * e + 3];
+                } else {
+                    const float4 v = reinterpret_cast<const float4*>(qp + dv * D)[e];
+                    qv[4 * e + 0] = scaled(v.x);
+                    qv[4 * e + 1] = scaled(v.y);
+                    qv[4 * e + 2] = scaled(v.z);
+                    qv[4 * e + 3] = scaled(v.w);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+                    for (int x = 0; x < 4; ++x) {
+                        const int qi = __float2int_rn(qv[8 * j + 4 * half + x] * inv);
+                        const uint32_t d0 = (uint32_t)(qi >> 16) & 0xffu;
+                        const uint32_t r = (uint32_t)qi & 0xffffu;
+                        const uint32_t dl = odd ? (r & 0xffu) : (r >> 8);
+                        w0 |= (live && !odd ? d0 : 0u) << (8 * x);
+                        w1 |= (live ? dl : 0u) << (8 * x);
+                    }
+                    b_hi[4 * dv + j][half] = w0;
+                    b_lo[4 * dv + j][half] = w1;
+                }
+        }
+    }
+    return __shfl_sync(kFull, sq_own, (2 * t4) << 2);
+}
+
+// One tile of a QK warp: the quad's scores of the tile's `valid` tokens,
+// the online softmax of head jb + t4 (base 2, lazy rescale) and p' = p *
+// v_scale handed to the unit's PV warp.  False when a bounded wait ran out.
+template <int HC, int QW, int SCW, int DV>
+__device__ __forceinline__ bool qk_tile(const DecodeArgs& a, uint8_t* stages, uint64_t* full,
+                                        uint64_t* empty, uint64_t* p_full, uint64_t* p_empty,
+                                        float* pslots, int i, int valid, int u, int gl, int gkv,
+                                        bool head_live, int lane, const uint32_t (&b_hi)[4 * DV][2],
+                                        const uint32_t (&b_lo)[4 * DV][2], float sq, float& m_run,
+                                        float& l_part) {
+    using G = Geo<HC, QW, SCW, DV>;
+    constexpr int S = G::kStages;
+    const int gid = lane >> 2, t4 = lane & 3;
+    constexpr int hkv = SCW;   // the cache's num_kv_heads: variants are chosen by it
+    const float c16 = 65536.0f * sq, c8 = 256.0f * sq;
+    const int s = i % S;
+    const int b = i % kPBufs;
+    if (!warp_wait(&full[s], (i / S) & 1)) return false;
+    const uint8_t* st = stages + s * G::STAGE;
+    const uint8_t* kt = st + gl * G::HEAD_TILE;
+    const float* kst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE);
+    const float* vst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE + G::SC_TILE);
+
+    float sc[4];   // tokens gid, gid+8, 16+gid, 24+gid of head jb + t4
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+        const int ra = mt * 16 + gid, rb = ra + 8;
+        int hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int dv = 0; dv < DV; ++dv) {
+            const uint8_t* kb = kt + dv * G::BOX;
+            const uint4 a00 = *reinterpret_cast<const uint4*>(kb + swz(ra, 2 * t4));
+            const uint4 a01 = *reinterpret_cast<const uint4*>(kb + swz(ra, 2 * t4 + 1));
+            const uint4 a10 = *reinterpret_cast<const uint4*>(kb + swz(rb, 2 * t4));
+            const uint4 a11 = *reinterpret_cast<const uint4*>(kb + swz(rb, 2 * t4 + 1));
+            const uint32_t w0[8] = {a00.x, a00.y, a00.z, a00.w, a01.x, a01.y, a01.z, a01.w};
+            const uint32_t w1[8] = {a10.x, a10.y, a10.z, a10.w, a11.x, a11.y, a11.z, a11.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                mma_s8s8(hi, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1],
+                         b_hi[4 * dv + j][0], b_hi[4 * dv + j][1]);
+                mma_s8u8(lo, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1],
+                         b_lo[4 * dv + j][0], b_lo[4 * dv + j][1]);
+            }
+        }
+        // accumulator (row, col): [0] (ra, 2*t4) [1] (ra, 2*t4+1) [2]/[3] row rb
+        const float sa = fmaf((float)hi[0], c16, fmaf((float)lo[0], c8, (float)lo[1] * sq));
+        const float sb = fmaf((float)hi[2], c16, fmaf((float)lo[2], c8, (float)lo[3] * sq));
+        sc[2 * mt] = (head_live && ra < valid) ? sa * kst[ra * hkv + gkv] : -INFINITY;
+        sc[2 * mt + 1] = (head_live && rb < valid) ? sb * kst[rb * hkv + gkv] : -INFINITY;
+    }
+
+    // online softmax of head jb + t4, base 2, lazy rescale
+    float tm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 4));
+    tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 8));
+    tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 16));
+    float corr = 1.0f;
+    if (tm > m_run + kLazyRescale) {
+        corr = exp2f(m_run - tm);
+        m_run = tm;
+    }
+    l_part *= corr;
+    float p[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        p[e] = sc[e] == -INFINITY ? 0.0f : exp2f(sc[e] - m_run);
+        l_part += p[e];
+    }
+
+    if (i >= kPBufs && !warp_wait(&p_empty[u * kPBufs + b], ((i / kPBufs) - 1) & 1)) return false;
+    float* pw = pslots + b * G::PSLOT;   // p'[head][token], then corr[head]
+    if (head_live) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int tok = (e >> 1) * 16 + (e & 1) * 8 + gid;
+            pw[t4 * T + tok] = p[e] == 0.0f ? 0.0f : p[e] * vst[tok * hkv + gkv];
+        }
+        if (gid == 0) pw[4 * T + t4] = corr;
+    }
+    __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(&p_full[u * kPBufs + b]);
+        mbar_arrive(&empty[s]);
+    }
+    return true;
+}
+
+// One tile of a PV warp: O^T[dim][col] += V^T[dim][token] . P[token][col],
+// col = (head, digit), with the QK warp's rescale factor applied first.
+template <int HC, int QW, int SCW, int DV>
+__device__ __forceinline__ bool pv_tile(uint8_t* stages, uint64_t* full, uint64_t* empty,
+                                        uint64_t* p_full, uint64_t* p_empty, float* pslots, int i,
+                                        int u, int gl, int jb, int group, bool head_live, int lane,
+                                        float (&acc)[8 * DV][2]) {
+    using G = Geo<HC, QW, SCW, DV>;
+    constexpr int S = G::kStages;
+    const int gid = lane >> 2, t4 = lane & 3;
+    const int hp = gid >> 1;           // head (in the quad) whose p' digits this thread supplies
+    const bool p_live = jb + hp < group;
+    const bool lo_digit = gid & 1;
+    const int s = i % S;
+    const int b = i % kPBufs;
+    if (!warp_wait(&p_full[u * kPBufs + b], (i / kPBufs) & 1)) return false;
+    if (!warp_wait(&full[s], (i / S) & 1)) return false;
+    const uint8_t* vt = stages + s * G::STAGE + G::KV_TILE + gl * G::HEAD_TILE;
+    const float* pw = pslots + b * G::PSLOT;
+
+    // p' digits as B fragments: tokens 4*t4.. (b0) and 16 + 4*t4.. (b1)
+    float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pb = pa;
+    if (p_live) {
+        pa = *reinterpret_cast<const float4*>(pw + hp * T + 4 * t4);
+        pb = *reinterpret_cast<const float4*>(pw + hp * T + 16 + 4 * t4);
+    }
+    float pmax = fmaxf(fmaxf(fmaxf(pa.x, pa.y), fmaxf(pa.z, pa.w)),
+                       fmaxf(fmaxf(pb.x, pb.y), fmaxf(pb.z, pb.w)));
+    pmax = fmaxf(pmax, __shfl_xor_sync(kFull, pmax, 1));
+    pmax = fmaxf(pmax, __shfl_xor_sync(kFull, pmax, 2));
+    // power-of-two scale putting the head's largest p' in [2^14, 2^15);
+    // a tile whose p' all lie below 2^-100 (far under the running max,
+    // with l >= 1) contributes nothing representable and is dropped.
+    if (!(pmax >= 0x1p-100f)) {
+        pa = make_float4(0.f, 0.f, 0.f, 0.f);
+        pb = pa;
+        pmax = 0.0f;
+    }
+    const int e = pmax > 0.0f ? ((__float_as_int(pmax) >> 23) & 0xff) - 127 : 0;
+    const float up = __int_as_float((127 + 14 - e) << 23);
+    const float down = __int_as_float((127 - 14 + e) << 23);
+    uint32_t bw0 = 0, bw1 = 0;
+    {
+        const float va[4] = {pa.x, pa.y, pa.z, pa.w};
+        const float vb[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            const uint32_t qa = (uint32_t)__float2int_rn(va[x] * up);
+            const uint32_t qb = (uint32_t)__float2int_rn(vb[x] * up);
+            bw0 |= (lo_digit ? (qa & 0xffu) : (qa >> 8)) << (8 * x);
+            bw1 |= (lo_digit ? (qb & 0xffu) : (qb >> 8)) << (8 * x);
+        }
+    }
+    const float sp = __shfl_sync(kFull, down, (2 * t4) << 2);
+    float corr = 1.0f;
+    if (head_live) corr = pw[4 * T + t4];
+    if (__any_sync(kFull, corr != 1.0f)) {
+#pragma unroll
+        for (int mt = 0; mt < 8 * DV; ++mt) {
+            acc[mt][0] *= corr;
+            acc[mt][1] *= corr;
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8 * DV; ++mt) {
+        // 16x16 blocks of V (tokens x dims 16*mt..): rows from lanes 0-15
+        const int r = lane & 15;
+        const uint8_t* vb = vt + (mt >> 3) * G::BOX;
+        uint32_t x0, x1, y0, y1;
+        ldmatrix_t_b8(x0, x1, vb + swz(r, mt & 7));
+        ldmatrix_t_b8(y0, y1, vb + swz(16 + r, mt & 7));
+        int d[4] = {0, 0, 0, 0};
+        mma_s8u8(d, x0, x1, y0, y1, bw0, bw1);
+        // d: (dim 16mt+gid, col 2t4 = hi digit of head t4), (.., lo), rows +8
+        acc[mt][0] = fmaf((float)(d[0] * 256 + d[1]), sp, acc[mt][0]);
+        acc[mt][1] = fmaf((float)(d[2] * 256 + d[3]), sp, acc[mt][1]);
+    }
+    __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(&p_empty[u * kPBufs + b]);
+        mbar_arrive(&empty[s]);
+    }
+    return true;
+}
+
+// Ring and handoff barriers (thread 0).
+template <int HC, int QW, int SCW, int DV>
+__device__ __forceinline__ void init_barriers(uint64_t* full, uint64_t* empty, uint64_t* p_full,
+                                              uint64_t* p_empty) {
+    using G = Geo<HC, QW, SCW, DV>;
+    for (int s = 0; s < G::kStages; ++s) {
+        mbar_init(&full[s], 1);
+        mbar_init(&empty[s], G::kWarps);
+    }
+    for (int i = 0; i < G::kUnits * kPBufs; ++i) {
+        mbar_init(&p_full[i], 1);
+        mbar_init(&p_empty[i], 1);
+    }
+    fence_mbar_init();
+}
+
+template <int HC, int QW, int SCW, int DV>
 __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SCW, DV>::kCtasPerSm)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                   const __grid_constant__ CUtensorMap tmap_v, const DecodeArgs a) {
@@ -318,20 +614,12 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
     const int ntiles = (n + T - 1) / T;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int hkv = a.num_kv_heads;
+    constexpr int hkv = SCW;   // the cache's num_kv_heads: variants are chosen by it
     const int group = a.num_heads / hkv;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], G::kWarps);
-        }
-        for (int i = 0; i < U * kPBufs; ++i) {
-            mbar_init(&p_full[i], 1);
-            mbar_init(&p_empty[i], 1);
-        }
+        init_barriers<HC, QW, SCW, DV>(full, empty, p_full, p_empty);
         fail_flag = 0;
-        fence_mbar_init();
     }
     __syncthreads();
 
@@ -367,145 +655,16 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
 
     if (is_qk) {
         // ================================================================ QK
-        // q as B fragments: column n = gid <-> (head jb + (gid >> 1), digit),
-        // thread t4 holds dims [32*t4, 32*t4 + 32) of every 128-dim block,
-        // k-step j covers 8 of them (block j / 4).
         uint32_t b_hi[4 * DV][2], b_lo[4 * DV][2];
-        float sq_own;
-        {
-            const int hq = gid >> 1;
-            const bool live = jb + hq < group;
-            // a quad past the group's end (groups that are not a multiple of
-            // 4) reads query head 0 of the group and keeps no column live
-            const float* qp =
-                a.q + ((size_t)seq * a.num_heads + gkv + hkv * (live ? jb + hq : 0)) * DH + 32 * t4;
-            auto scaled = [&](float v) { return __fmul_rn(__fmul_rn(v, a.q_mul), kLog2e); };
-            // the head's absmax over all its blocks (first pass), then the
-            // digits block by block (second pass, the loads hit L1)
-            float amax = 0.0f;
-#pragma unroll
-            for (int dv = 0; dv < DV; ++dv)
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float4 v = reinterpret_cast<const float4*>(qp + dv * D)[e];
-                    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(scaled(v.x)), fabsf(scaled(v.y))),
-                                             fmaxf(fabsf(scaled(v.z)), fabsf(scaled(v.w)))));
-                }
-            amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
-            amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
-            const float kQMax = 8323072.0f;  // 2^23 - 2^16 keeps d0 in [-128, 127]
-            const float inv = amax > 0.0f ? __fdiv_rn(kQMax, amax) : 0.0f;
-            sq_own = amax > 0.0f ? __fdiv_rn(amax, kQMax) : 0.0f;
-            const bool odd = gid & 1;
-#pragma unroll
-            for (int dv = 0; dv < DV; ++dv) {
-                float qv[32];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float4 v = reinterpret_cast<const float4*>(qp + dv * D)[e];
-                    qv[4 * e + 0] = scaled(v.x);
-                    qv[4 * e + 1] = scaled(v.y);
-                    qv[4 * e + 2] = scaled(v.z);
-                    qv[4 * e + 3] = scaled(v.w);
-                }
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-#pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-                        for (int x = 0; x < 4; ++x) {
-                            const int qi = __float2int_rn(qv[8 * j + 4 * half + x] * inv);
-                            const uint32_t d0 = (uint32_t)(qi >> 16) & 0xffu;
-                            const uint32_t r = (uint32_t)qi & 0xffffu;
-                            const uint32_t dl = odd ? (r & 0xffu) : (r >> 8);
-                            w0 |= (live && !odd ? d0 : 0u) << (8 * x);
-                            w1 |= (live ? dl : 0u) << (8 * x);
-                        }
-                        b_hi[4 * dv + j][half] = w0;
-                        b_lo[4 * dv + j][half] = w1;
-                    }
-            }
-        }
-        const float sq = __shfl_sync(kFull, sq_own, (2 * t4) << 2);
-        const float c16 = 65536.0f * sq, c8 = 256.0f * sq;
+        const float sq = qk_load_q<DV>(a, seq, gkv, jb, group, hkv, lane, b_hi, b_lo);
         float m_run = -INFINITY;      // running max of head jb + t4 (log2 units)
         float l_part = 0.0f;          // this thread's share of that head's sum
-
         for (int i = 0; i < ntiles; ++i) {
-            const int s = i % S;
-            const int b = i % kPBufs;
-            if (!warp_wait(&full[s], (i / S) & 1)) { failed = true; break; }
-            const uint8_t* st = stages + s * G::STAGE;
-            const uint8_t* kt = st + gl * G::HEAD_TILE;
-            const float* kst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE);
-            const float* vst = reinterpret_cast<const float*>(st + 2 * G::KV_TILE + G::SC_TILE);
-            const int valid = n - i * T;
-
-            float sc[4];   // tokens gid, gid+8, 16+gid, 24+gid of head jb + t4
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                const int ra = mt * 16 + gid, rb = ra + 8;
-                int hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
-#pragma unroll
-                for (int dv = 0; dv < DV; ++dv) {
-                    const uint8_t* kb = kt + dv * G::BOX;
-                    const uint4 a00 = *reinterpret_cast<const uint4*>(kb + swz(ra, 2 * t4));
-                    const uint4 a01 = *reinterpret_cast<const uint4*>(kb + swz(ra, 2 * t4 + 1));
-                    const uint4 a10 = *reinterpret_cast<const uint4*>(kb + swz(rb, 2 * t4));
-                    const uint4 a11 = *reinterpret_cast<const uint4*>(kb + swz(rb, 2 * t4 + 1));
-                    const uint32_t w0[8] = {a00.x, a00.y, a00.z, a00.w, a01.x, a01.y, a01.z, a01.w};
-                    const uint32_t w1[8] = {a10.x, a10.y, a10.z, a10.w, a11.x, a11.y, a11.z, a11.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        mma_s8s8(hi, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1],
-                                 b_hi[4 * dv + j][0], b_hi[4 * dv + j][1]);
-                        mma_s8u8(lo, w0[2 * j], w1[2 * j], w0[2 * j + 1], w1[2 * j + 1],
-                                 b_lo[4 * dv + j][0], b_lo[4 * dv + j][1]);
-                    }
-                }
-                // accumulator (row, col): [0] (ra, 2*t4) [1] (ra, 2*t4+1) [2]/[3] row rb
-                const float sa = fmaf((float)hi[0], c16, fmaf((float)lo[0], c8, (float)lo[1] * sq));
-                const float sb = fmaf((float)hi[2], c16, fmaf((float)lo[2], c8, (float)lo[3] * sq));
-                sc[2 * mt] = (head_live && ra < valid) ? sa * kst[ra * hkv + gkv] : -INFINITY;
-                sc[2 * mt + 1] = (head_live && rb < valid) ? sb * kst[rb * hkv + gkv] : -INFINITY;
-            }
-
-            // online softmax of head jb + t4, base 2, lazy rescale
-            float tm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-            tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 4));
-            tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 8));
-            tm = fmaxf(tm, __shfl_xor_sync(kFull, tm, 16));
-            float corr = 1.0f;
-            if (tm > m_run + kLazyRescale) {
-                corr = exp2f(m_run - tm);
-                m_run = tm;
-            }
-            l_part *= corr;
-            float p[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                p[e] = sc[e] == -INFINITY ? 0.0f : exp2f(sc[e] - m_run);
-                l_part += p[e];
-            }
-
-            if (i >= kPBufs && !warp_wait(&p_empty[u * kPBufs + b], ((i / kPBufs) - 1) & 1)) {
+            if (!qk_tile<HC, QW, SCW, DV>(a, stages, full, empty, p_full, p_empty, pslots, i,
+                                          n - i * T, u, gl, gkv, head_live, lane, b_hi, b_lo, sq,
+                                          m_run, l_part)) {
                 failed = true;
                 break;
-            }
-            float* pw = pslots + b * G::PSLOT;   // p'[head][token], then corr[head]
-            if (head_live) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int tok = (e >> 1) * 16 + (e & 1) * 8 + gid;
-                    pw[t4 * T + tok] = p[e] == 0.0f ? 0.0f : p[e] * vst[tok * hkv + gkv];
-                }
-                if (gid == 0) pw[4 * T + t4] = corr;
-            }
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&p_full[u * kPBufs + b]);
-                mbar_arrive(&empty[s]);
             }
         }
         l_part += __shfl_xor_sync(kFull, l_part, 4);
@@ -520,83 +679,14 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
         }
     } else {
         // ================================================================ PV
-        // O^T[dim][col] += V^T[dim][token] . P[token][col], col = (head, digit)
         float acc[8 * DV][2];   // head jb + t4, dims 16*mt + gid (+8)
 #pragma unroll
         for (int mt = 0; mt < 8 * DV; ++mt) acc[mt][0] = acc[mt][1] = 0.0f;
-        const int hp = gid >> 1;           // head (in the quad) whose p' digits this thread supplies
-        const bool p_live = jb + hp < group;
-        const bool lo_digit = gid & 1;
-
         for (int i = 0; i < ntiles; ++i) {
-            const int s = i % S;
-            const int b = i % kPBufs;
-            if (!warp_wait(&p_full[u * kPBufs + b], (i / kPBufs) & 1)) { failed = true; break; }
-            if (!warp_wait(&full[s], (i / S) & 1)) { failed = true; break; }
-            const uint8_t* vt = stages + s * G::STAGE + G::KV_TILE + gl * G::HEAD_TILE;
-            const float* pw = pslots + b * G::PSLOT;
-
-            // p' digits as B fragments: tokens 4*t4.. (b0) and 16 + 4*t4.. (b1)
-            float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pb = pa;
-            if (p_live) {
-                pa = *reinterpret_cast<const float4*>(pw + hp * T + 4 * t4);
-                pb = *reinterpret_cast<const float4*>(pw + hp * T + 16 + 4 * t4);
-            }
-            float pmax = fmaxf(fmaxf(fmaxf(pa.x, pa.y), fmaxf(pa.z, pa.w)),
-                               fmaxf(fmaxf(pb.x, pb.y), fmaxf(pb.z, pb.w)));
-            pmax = fmaxf(pmax, __shfl_xor_sync(kFull, pmax, 1));
-            pmax = fmaxf(pmax, __shfl_xor_sync(kFull, pmax, 2));
-            // power-of-two scale putting the head's largest p' in [2^14, 2^15);
-            // a tile whose p' all lie below 2^-100 (far under the running max,
-            // with l >= 1) contributes nothing representable and is dropped.
-            if (!(pmax >= 0x1p-100f)) {
-                pa = make_float4(0.f, 0.f, 0.f, 0.f);
-                pb = pa;
-                pmax = 0.0f;
-            }
-            const int e = pmax > 0.0f ? ((__float_as_int(pmax) >> 23) & 0xff) - 127 : 0;
-            const float up = __int_as_float((127 + 14 - e) << 23);
-            const float down = __int_as_float((127 - 14 + e) << 23);
-            uint32_t bw0 = 0, bw1 = 0;
-            {
-                const float va[4] = {pa.x, pa.y, pa.z, pa.w};
-                const float vb[4] = {pb.x, pb.y, pb.z, pb.w};
-#pragma unroll
-                for (int x = 0; x < 4; ++x) {
-                    const uint32_t qa = (uint32_t)__float2int_rn(va[x] * up);
-                    const uint32_t qb = (uint32_t)__float2int_rn(vb[x] * up);
-                    bw0 |= (lo_digit ? (qa & 0xffu) : (qa >> 8)) << (8 * x);
-                    bw1 |= (lo_digit ? (qb & 0xffu) : (qb >> 8)) << (8 * x);
-                }
-            }
-            const float sp = __shfl_sync(kFull, down, (2 * t4) << 2);
-            float corr = 1.0f;
-            if (head_live) corr = pw[4 * T + t4];
-            if (__any_sync(kFull, corr != 1.0f)) {
-#pragma unroll
-                for (int mt = 0; mt < 8 * DV; ++mt) {
-                    acc[mt][0] *= corr;
-                    acc[mt][1] *= corr;
-                }
-            }
-#pragma unroll
-            for (int mt = 0; mt < 8 * DV; ++mt) {
-                // 16x16 blocks of V (tokens x dims 16*mt..): rows from lanes 0-15
-                const int r = lane & 15;
-                const uint8_t* vb = vt + (mt >> 3) * G::BOX;
-                uint32_t x0, x1, y0, y1;
-                ldmatrix_t_b8(x0, x1, vb + swz(r, mt & 7));
-                ldmatrix_t_b8(y0, y1, vb + swz(16 + r, mt & 7));
-                int d[4] = {0, 0, 0, 0};
-                mma_s8u8(d, x0, x1, y0, y1, bw0, bw1);
-                // d: (dim 16mt+gid, col 2t4 = hi digit of head t4), (.., lo), rows +8
-                acc[mt][0] = fmaf((float)(d[0] * 256 + d[1]), sp, acc[mt][0]);
-                acc[mt][1] = fmaf((float)(d[2] * 256 + d[3]), sp, acc[mt][1]);
-            }
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&p_empty[u * kPBufs + b]);
-                mbar_arrive(&empty[s]);
+            if (!pv_tile<HC, QW, SCW, DV>(stages, full, empty, p_full, p_empty, pslots, i, u, gl,
+                                          jb, group, head_live, lane, acc)) {
+                failed = true;
+                break;
             }
         }
         consumer_barrier(G::kConsumerThreads);   // every warp is done with the stage ring
@@ -647,19 +737,234 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
     }
 }
 
-// Merges the chunk partials of one (sequence, head) in three passes over the
-// chunks, each spread over the block's threads: the maximum M of the chunk
-// maxima, the weights 2^(m_c - M) (kept in shared memory) with the weighted
-// sum of l, then O, where each of kCombineSplit thread groups sums every
-// kCombineSplit-th chunk for every dim (independent loads, so a long chunk
-// list is not one serial chain).  A thread covers dim d of each of the
-// head's DV 128-dim blocks.  Reductions run in a fixed order: the result
-// does not depend on timing.
+// ------------------------------------------------------------ stream-K
+// The batch's tiles in sequence order, 0 .. TT-1, are split evenly over the
+// grid's first Ce = min(C, TT) CTAs (of every head block): CTA c takes
+// [c*TT/Ce, (c+1)*TT/Ce), at least one tile, so every CTA streams the same
+// number of tiles whatever the lengths, in one wave.  Its range meets one or more sequences; each (CTA c, sequence s)
+// intersection is a piece whose unnormalised (m, l, O) goes to workspace row
+// c + s (distinct for distinct non-empty pieces: they are ordered in both c
+// and s), and the merge kernel combines a sequence's pieces.
+
+// Tiles of sequence s (0 for an entry outside its bounds: flagged apart).
+__device__ __forceinline__ int sk_tiles(const DecodeArgs& a, int s) {
+    int32_t off, cap, len;
+    if (!load_entry(a, s, off, cap, len)) return 0;
+    return (len + T - 1) / T;
+}
+
+// The CTA whose range holds global tile t.
+__device__ __forceinline__ int sk_cta_of(long long t, long long TT, int C) {
+    return (int)(((t + 1) * C - 1) / TT);
+}
+
+// Sequences a thread covers in the stream-K table pass: thread t takes
+// sequences [t*kSkPerThread, (t+1)*kSkPerThread), so the smallest CTA (96
+// threads) covers kStreamMaxSeqs of them.
+constexpr int kSkPerThread = 11;
+static_assert(kSkPerThread * 96 >= kStreamMaxSeqs, "stream-K table pass covers the batch");
+
+// One block-wide pass over the length table (every thread calls it): the
+// batch's tile count TT; the split over Ce = min(C, TT) CTAs, each of which
+// then owns at least one tile (the merge counts on every CTA of a sequence's
+// range having written its piece); CTA c's tile range [lo, hi) (empty for
+// c >= Ce); the sequence holding tile lo and the tiles before it.  With
+// `prefix` set, the tiles before every sequence go to prefix[0 ..
+// num_seqs - 1] and TT to prefix[num_seqs], for the merge kernel.  Tile
+// indices fit int: a batch holds fewer than 2^31 slots.
+__device__ void sk_locate(const DecodeArgs& a, int c, int C, int32_t* prefix, int& lo, int& hi,
+                          int& s_at, int& p_at) {
+    __shared__ long long s_warp[32];
+    __shared__ int s_res[2];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int nw = (blockDim.x + 31) >> 5;
+    const int s_beg = tid * kSkPerThread;
+    int v[kSkPerThread];
+    long long mine = 0;
+#pragma unroll
+    for (int k = 0; k < kSkPerThread; ++k) {
+        v[k] = s_beg + k < a.num_seqs ? sk_tiles(a, s_beg + k) : 0;
+        mine += v[k];
+    }
+    if (tid == 0) {
+        s_res[0] = -1;
+        s_res[1] = 0;
+    }
+    long long x = mine;                           // inclusive scan over the block
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const long long y = __shfl_up_sync(kFull, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) s_warp[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+        long long w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long y = __shfl_up_sync(kFull, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nw) s_warp[lane] = w;
+    }
+    __syncthreads();
+    const long long TT = s_warp[nw - 1];
+    const int Ce = (int)(TT < C ? TT : C);
+    lo = c < Ce ? (int)((long long)c * TT / Ce) : 0;
+    hi = c < Ce ? (int)((long long)(c + 1) * TT / Ce) : 0;
+    int e = (int)((wid ? s_warp[wid - 1] : 0) + x - mine);   // tiles before s_beg
+#pragma unroll
+    for (int k = 0; k < kSkPerThread; ++k) {
+        if (prefix && s_beg + k < a.num_seqs) prefix[s_beg + k] = e;
+        if (lo < hi && v[k] > 0 && e <= lo && lo < e + v[k]) {
+            s_res[0] = s_beg + k;
+            s_res[1] = e;
+        }
+        e += v[k];
+    }
+    if (prefix && tid == 0) prefix[a.num_seqs] = (int32_t)TT;
+    __syncthreads();
+    s_at = s_res[0];
+    p_at = s_res[1];
+}
+
+template <int HC, int QW, int SCW, int DV>
+__global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SCW, DV>::kCtasPerSm)
+    decode_sk_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                     const __grid_constant__ CUtensorMap tmap_v, const DecodeArgs a) {
+    using G = Geo<HC, QW, SCW, DV>;
+    constexpr int DH = G::DH;
+    constexpr int S = G::kStages;
+    constexpr int U = G::kUnits;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* stages = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* pbuf = reinterpret_cast<float*>(stages + S * G::STAGE);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stages + S * G::STAGE + G::PBUF);
+    uint64_t* full = bars;
+    uint64_t* empty = full + S;
+    uint64_t* p_full = empty + S;
+    uint64_t* p_empty = p_full + U * kPBufs;
+
+    const int g0 = blockIdx.x * HC;
+    const int cta = blockIdx.y, C = a.sk_ctas;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    constexpr int hkv = SCW;   // the cache's num_kv_heads: variants are chosen by it
+    const int group = a.num_heads / hkv;
+    const int H = a.num_heads;
+    pdl_wait();  // the append before this kernel writes the lengths and the codes
+    pdl_trigger();
+    if (threadIdx.x == 0) init_barriers<HC, QW, SCW, DV>(full, empty, p_full, p_empty);
+    if (cta == 0 && blockIdx.x == 0) {
+        for (int s = threadIdx.x; s < a.num_seqs; s += blockDim.x) {
+            int32_t off, cap, len;
+            if (!load_entry(a, s, off, cap, len)) flag_error(a.err, EC_DEVERR_BAD_TABLE);
+        }
+    }
+    // the table pass (its barriers also publish the barrier inits); CTA 0 of
+    // head block 0 leaves the per-sequence tile prefix for the merge kernel
+    int32_t* prefix = (cta == 0 && blockIdx.x == 0) ? a.sk_prefix : nullptr;
+    int lo, hi, s0, p0;
+    sk_locate(a, cta, C, prefix, lo, hi, s0, p0);
+    if (lo >= hi) return;
+
+    if (warp == G::kWarps) {
+        // ============================================================ producer
+        const uint64_t pol = l2_policy_evict_first();
+        int gj = 0;
+        int p = p0;
+        for (int s = s0; s < a.num_seqs && p < hi; ++s) {
+            int32_t off, cap, len;
+            const int nt = load_entry(a, s, off, cap, len) ? (len + T - 1) / T : 0;
+            const int t_lo = max(lo, p), t_hi = min(hi, p + nt);
+            for (int t = t_lo; t < t_hi; ++t, ++gj) {
+                const int tok = (t - p) * T;
+                if (!issue_tile_at<HC, QW, SCW, DV>(a, &tmap_k, &tmap_v, stages, full, empty, gj,
+                                                    min(T, len - tok), s, off, tok, g0, pol, lane)) {
+                    if (lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
+                    return;
+                }
+            }
+            p += nt;
+        }
+        return;
+    }
+
+    const bool is_qk = warp < U;
+    const int u = is_qk ? warp : warp - U;
+    const int gl = u / QW;
+    const int gkv = g0 + gl;
+    const int jb = 4 * (u % QW);
+    const int gid = lane >> 2;
+    const int t4 = lane & 3;
+    const bool head_live = jb + t4 < group;
+    const int h_out = gkv + hkv * (jb + t4);         // the head this thread's columns belong to
+    float* pslots = pbuf + u * kPBufs * G::PSLOT;
+    int gi = 0;
+    int p = p0;
+    for (int s = s0; s < a.num_seqs && p < hi; ++s) {
+        int32_t off, cap, len;
+        const int nt = load_entry(a, s, off, cap, len) ? (len + T - 1) / T : 0;
+        const int t_lo = max(lo, p), t_hi = min(hi, p + nt);
+        const int first_tok = (t_lo - p) * T;       // the piece's first token in sequence s
+        p += nt;
+        if (t_lo >= t_hi) continue;
+        const size_t row = (size_t)(cta + s) * H;    // this piece's partial rows
+        if (is_qk) {
+            uint32_t b_hi[4 * DV][2], b_lo[4 * DV][2];
+            const float sq = qk_load_q<DV>(a, s, gkv, jb, group, hkv, lane, b_hi, b_lo);
+            float m_run = -INFINITY, l_part = 0.0f;
+            for (int t = t_lo, tok = first_tok; t < t_hi; ++t, ++gi, tok += T) {
+                if (!qk_tile<HC, QW, SCW, DV>(a, stages, full, empty, p_full, p_empty, pslots, gi,
+                                              len - tok, u, gl, gkv, head_live, lane, b_hi, b_lo,
+                                              sq, m_run, l_part)) {
+                    if (lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
+                    return;
+                }
+            }
+            l_part += __shfl_xor_sync(kFull, l_part, 4);
+            l_part += __shfl_xor_sync(kFull, l_part, 8);
+            l_part += __shfl_xor_sync(kFull, l_part, 16);
+            if (gid == 0 && head_live) {
+                a.part_ml[(row + h_out) * 2] = m_run;
+                a.part_ml[(row + h_out) * 2 + 1] = l_part;
+            }
+        } else {
+            float acc[8 * DV][2];
+#pragma unroll
+            for (int mt = 0; mt < 8 * DV; ++mt) acc[mt][0] = acc[mt][1] = 0.0f;
+            for (int t = t_lo; t < t_hi; ++t, ++gi) {
+                if (!pv_tile<HC, QW, SCW, DV>(stages, full, empty, p_full, p_empty, pslots, gi, u,
+                                              gl, jb, group, head_live, lane, acc)) {
+                    if (lane == 0) flag_error(a.err, EC_DEVERR_TIMEOUT);
+                    return;
+                }
+            }
+            if (head_live) {
+                float* po = a.part_o + (row + h_out) * DH;
+#pragma unroll
+                for (int mt = 0; mt < 8 * DV; ++mt) {
+                    po[16 * mt + gid] = acc[mt][0];
+                    po[16 * mt + gid + 8] = acc[mt][1];
+                }
+            }
+        }
+    }
+}
+
+// Merges the chunk partials of one (sequence, head): the maximum M of the
+// chunk maxima and the weights 2^(m_c - M) (kept in shared memory) with the
+// weighted sum of l -- with one chunk per thread up to 512 chunks, else in
+// two passes over the chunks -- then O, where each of kCombineSplit thread
+// groups sums every kCombineSplit-th chunk for every dim (independent loads,
+// so a long chunk list is not one serial chain).  A thread covers dim d of
+// each of the head's DV 128-dim blocks.  Reductions run in a fixed order:
+// the result does not depend on timing.
 constexpr int kCombineSplit = 4;
 constexpr int kCombineThreads = D * kCombineSplit;
-constexpr int kMaxChunks = 1024;                   // split-K chunks per sequence, at most
 template <int DV>
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kCombineThreads, 4) combine_kernel(const DecodeArgs a) {
     constexpr int DH = D * DV;
     constexpr int kWarpsC = kCombineThreads / 32;
     const int seq = blockIdx.x, h = blockIdx.y;
@@ -670,46 +975,92 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const DecodeAr
     pdl_trigger();
     int32_t off, cap, len;
     if (!load_entry(a, seq, off, cap, len)) return;  // flagged by decode_kernel
-    const int nch = (len + a.chunk_tokens - 1) / a.chunk_tokens;
-    const size_t base = (size_t)seq * a.max_chunks * H + h;
-    __shared__ float s_f[kMaxChunks], s_red[DH * kCombineSplit];
+    // the sequence's partial rows: chunks c of the chunked grid at
+    // (seq * max_chunks + c) * H + h, or the stream-K pieces of CTAs
+    // c_first .. c_last at (c + seq) * H + h
+    int nch;
+    size_t base;
+    if (a.sk_ctas) {
+        // the tile prefix the decode kernel's CTA 0 left (read only when the
+        // sequence has tiles, in which case that CTA ran the table pass)
+        const int nt = (len + T - 1) / T;
+        const long long p_s = a.sk_prefix[seq];     // written by every launch (CTA 0's table pass)
+        const long long TT = nt ? a.sk_prefix[a.num_seqs] : 1;
+        const int Ce = (int)(TT < a.sk_ctas ? TT : a.sk_ctas);
+        const int c_first = nt ? sk_cta_of(p_s, TT, Ce) : 0;
+        nch = nt ? sk_cta_of(p_s + nt - 1, TT, Ce) - c_first + 1 : 0;
+        base = (size_t)(c_first + seq) * H + h;
+    } else {
+        nch = (len + a.chunk_tokens - 1) / a.chunk_tokens;
+        base = (size_t)seq * a.max_chunks * H + h;
+    }
+    __shared__ float s_f[kMaxChunks], s_l[kCombineThreads], s_red[DH * kCombineSplit];
     __shared__ float s_M, s_L;
     auto ml_of = [&](int c) {
         return *reinterpret_cast<const float2*>(a.part_ml + (base + (size_t)c * H) * 2);
     };
-    // pass 1: M = max over the chunk maxima
-    float m = -INFINITY;
-    for (int c = tid; c < nch; c += kCombineThreads) m = fmaxf(m, ml_of(c).x);
+    if (nch <= kCombineThreads) {
+        // one chunk per thread: its (m, l) loaded once
+        const bool has_c = tid < nch;
+        const float2 mlc = has_c ? ml_of(tid) : make_float2(-INFINITY, 0.0f);
+        float m = mlc.x;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) s_red[wid] = m;
-    __syncthreads();
-    if (tid == 0) {
-        float M = -INFINITY;
-        for (int w = 0; w < kWarpsC; ++w) M = fmaxf(M, s_red[w]);
-        s_M = M;
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_red[wid] = m;
+        __syncthreads();
+        if (tid == 0) {
+            float M = -INFINITY;
+            for (int w = 0; w < kWarpsC; ++w) M = fmaxf(M, s_red[w]);
+            s_M = M;
+        }
+        __syncthreads();
+        const float f = (has_c && mlc.x != -INFINITY) ? exp2f(mlc.x - s_M) : 0.0f;
+        if (has_c) {
+            s_f[tid] = f;
+            s_l[tid] = f * mlc.y;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float L = 0.0f;
+            for (int c = 0; c < nch; ++c) L += s_l[c];
+            s_L = L;
+        }
+    } else {
+        // pass 1: M = max over the chunk maxima
+        float m = -INFINITY;
+        for (int c = tid; c < nch; c += kCombineThreads) m = fmaxf(m, ml_of(c).x);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_red[wid] = m;
+        __syncthreads();
+        if (tid == 0) {
+            float M = -INFINITY;
+            for (int w = 0; w < kWarpsC; ++w) M = fmaxf(M, s_red[w]);
+            s_M = M;
+        }
+        __syncthreads();
+        const float M = s_M;
+        // pass 2: chunk weights and sum_c 2^(m_c - M) * l_c
+        float lsum = 0.0f;
+        for (int c = tid; c < nch; c += kCombineThreads) {
+            const float2 mlc = ml_of(c);
+            const float f = mlc.x == -INFINITY ? 0.0f : exp2f(mlc.x - M);
+            s_f[c] = f;
+            lsum += f * mlc.y;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+        __syncthreads();                               // s_red's maxima are read
+        if (lane == 0) s_red[wid] = lsum;
+        __syncthreads();
+        if (tid == 0) {
+            float L = 0.0f;
+            for (int w = 0; w < kWarpsC; ++w) L += s_red[w];
+            s_L = L;
+        }
     }
     __syncthreads();
     const float M = s_M;
-    // pass 2: chunk weights and sum_c 2^(m_c - M) * l_c
-    float lsum = 0.0f;
-    for (int c = tid; c < nch; c += kCombineThreads) {
-        const float2 mlc = ml_of(c);
-        const float f = mlc.x == -INFINITY ? 0.0f : exp2f(mlc.x - M);
-        s_f[c] = f;
-        lsum += f * mlc.y;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-    __syncthreads();                                   // s_red's maxima are read
-    if (lane == 0) s_red[wid] = lsum;
-    __syncthreads();
-    if (tid == 0) {
-        float L = 0.0f;
-        for (int w = 0; w < kWarpsC; ++w) L += s_red[w];
-        s_L = L;
-    }
-    __syncthreads();
     const float sl = s_L;
     // pass 3: O
     float so[DV];
@@ -775,9 +1126,12 @@ __global__ void __launch_bounds__(D) lse_merge_kernel(const float* __restrict__ 
 template <int HC, int QW, int SCW, int DV>
 cudaError_t launch_decode_t(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t st) {
     using G = Geo<HC, QW, SCW, DV>;
-    static std::atomic<unsigned long long> attr_done{0};
-    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(decode_kernel<HC, QW, SCW, DV>),
-                                      G::SMEM, attr_done);
+    static std::atomic<unsigned long long> attr_done{0}, attr_done_sk{0};
+    const bool sk = a.sk_ctas > 0;
+    cudaError_t e = sk ? ensure_smem_limit(reinterpret_cast<const void*>(decode_sk_kernel<HC, QW, SCW, DV>),
+                                           G::SMEM, attr_done_sk)
+                       : ensure_smem_limit(reinterpret_cast<const void*>(decode_kernel<HC, QW, SCW, DV>),
+                                           G::SMEM, attr_done);
     if (e != cudaSuccess) return e;
     CUtensorMap mk, mv;
     const int hkv = a.num_kv_heads;
@@ -785,6 +1139,9 @@ cudaError_t launch_decode_t(const DecodeArgs& a, const DecodePlan& plan, cudaStr
     if ((e = make_code_map(&mk, a.keys, hkv * DV, a.total_slots, T)) != cudaSuccess) return e;
     if ((e = make_code_map(&mv, a.values, hkv * DV, a.total_slots, T)) != cudaSuccess) return e;
     // head blocks fastest, so that the CTAs sharing a chunk's scale rows run together
+    if (sk)
+        return launch_pdl(decode_sk_kernel<HC, QW, SCW, DV>, dim3(hkv / HC, a.sk_ctas),
+                          dim3(G::kThreads), G::SMEM, st, mk, mv, a);
     dim3 grid(hkv / HC, plan.max_chunks, a.num_seqs);
     return launch_pdl(decode_kernel<HC, QW, SCW, DV>, grid, dim3(G::kThreads), G::SMEM, st, mk, mv,
                       a);
@@ -877,14 +1234,32 @@ DecodeVariant decode_variant(int num_kv_heads, int group, int head_dim) {
 }
 
 DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens,
-                       int num_kv_heads, int num_heads, int head_dim) {
+                       int num_kv_heads, int num_heads, int head_dim, bool allow_stream) {
     const DecodeVariant v = num_kv_heads > 0
         ? decode_variant(num_kv_heads, num_heads / num_kv_heads, head_dim) : DecodeVariant{};
     const int slots = num_sms * (v.hc ? v.ctas_per_sm : 2);   // resident CTAs
     const int hblocks = v.hc ? num_kv_heads / v.hc : 1;       // CTAs per (sequence, chunk)
-    DecodePlan best{T, 1};
+    DecodePlan best{T, 1, 0};
     if (max_seq_len <= 0 || num_seqs <= 0) return best;
     const int tiles = (max_seq_len + T - 1) / T;
+    // Stream-K for large batches of about equal lengths: one wave, every CTA
+    // of a head block streams an equal share of the batch's tiles, so no
+    // partial last wave (config 3: 1,152 chunks were 3.9 waves) and no CTA
+    // prologue per chunk.  Measured on B200 against the chunked grid: +1%
+    // on 128 x 32k, but behind on one sequence (the table pass and the
+    // prefix read add to a 15 us step) and on ragged batches of 64, whose
+    // step is set by its fixed costs; those keep the chunked plan.
+    const bool ragged_batch = total_tokens > 0 && total_tokens * 10 < (uint64_t)num_seqs * max_seq_len * 9;
+    if (allow_stream && num_seqs >= kStreamMinSeqs && num_seqs <= kStreamMaxSeqs && !ragged_batch) {
+        // (the merge takes up to kMaxChunks pieces of a sequence, one per CTA)
+        const uint64_t tokens = total_tokens > 0 ? total_tokens : (uint64_t)num_seqs * max_seq_len;
+        const uint64_t tt = (tokens + T - 1) / T;
+        int c = slots / hblocks;
+        c = c < 1 ? 1 : c;
+        if ((uint64_t)c > tt) c = (int)(tt > 0 ? tt : 1);
+        if (c > kMaxChunks) c = kMaxChunks;
+        return DecodePlan{tiles * T, 1, c};
+    }
     double best_cost = 1e300;
     const int kmax = tiles < kMaxChunks ? tiles : kMaxChunks;
     // with a token count below the all-full batch, the CTAs that find work
@@ -914,6 +1289,9 @@ DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t tota
 }
 
 size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads, int head_dim) {
+    if (p.sk_ctas > 0)   // a row per (CTA, sequence) piece (rows c + s < C + num_seqs), then the tile prefix
+        return (size_t)(p.sk_ctas + num_seqs) * num_heads * (head_dim + 2) * sizeof(float) +
+               (((size_t)num_seqs + 1) * sizeof(int32_t) + 15) / 16 * 16;
     if (p.max_chunks <= 1) return 0;
     return (size_t)num_seqs * p.max_chunks * num_heads * (head_dim + 2) * sizeof(float);
 }
@@ -922,7 +1300,14 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
                           cudaStream_t st) {
     a.chunk_tokens = plan.chunk_tokens;
     a.max_chunks = plan.max_chunks;
-    if (plan.max_chunks > 1 || a.mode == kChunks) {
+    a.sk_ctas = a.mode == kChunks ? 0 : plan.sk_ctas;
+    if (a.mode == kChunks && plan.sk_ctas > 0) return cudaErrorInvalidValue;   // needs a chunked plan
+    if (a.sk_ctas > 0) {
+        const size_t rows = (size_t)(a.sk_ctas + a.num_seqs) * a.num_heads;
+        a.part_o = static_cast<float*>(ws);
+        a.part_ml = a.part_o + rows * a.head_dim;
+        a.sk_prefix = reinterpret_cast<int32_t*>(a.part_ml + rows * 2);
+    } else if (plan.max_chunks > 1 || a.mode == kChunks) {
         a.part_o = static_cast<float*>(ws);
         a.part_ml = a.part_o + (size_t)a.num_seqs * plan.max_chunks * a.num_heads * a.head_dim;
     }
@@ -935,7 +1320,7 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
         e = launch_decode_t<HC_, QW_, SCW_, DV_>(a, plan, st);
     EC_DECODE_VARIANTS(EC_DEC)
 #undef EC_DEC
-    if (e != cudaSuccess || plan.max_chunks <= 1 || a.mode == kChunks) return e;
+    if (e != cudaSuccess || a.mode == kChunks || (plan.max_chunks <= 1 && a.sk_ctas == 0)) return e;
     const dim3 cg(a.num_seqs, a.num_heads), cb(kCombineThreads);
     return v.dv == 1 ? launch_pdl(combine_kernel<1>, cg, cb, 0, st, a)
                      : launch_pdl(combine_kernel<2>, cg, cb, 0, st, a);

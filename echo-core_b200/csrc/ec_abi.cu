@@ -679,7 +679,7 @@ size_t ec_cp_decode_workspace_size(const ec_kv_batch* b, uint32_t num_heads) {
     const ec::DecodePlan p = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len,
                                              num_sms_current(), b->total_tokens_hint,
                                              (int)b->num_kv_heads, (int)num_heads,
-                                             (int)b->head_dim);
+                                             (int)b->head_dim, false);
     const int chunks = p.max_chunks > 1 ? p.max_chunks : 1;
     return (size_t)b->num_seqs * chunks * num_heads * (b->head_dim + 2) * sizeof(float);
 }
@@ -702,7 +702,7 @@ int ec_cp_decode_exchange(ec_cp_comm* c, const ec_kv_batch* b, const float* q,
         return fail(EC_ERR_MISALIGNED, "%s: q/out/workspace not 16-byte aligned", who);
     const ec::DecodePlan plan = ec::plan_decode((int)b->num_seqs, (int)b->max_seq_len,
                                                 num_sms_current(), b->total_tokens_hint,
-                                                (int)b->num_kv_heads, (int)num_heads, 128);
+                                                (int)b->num_kv_heads, (int)num_heads, 128, false);
     const size_t need = ec_cp_decode_workspace_size(b, num_heads);
     if (workspace_bytes < need)
         return fail(EC_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", who, need,

@@ -111,6 +111,8 @@ struct DecodeArgs {
     int num_heads;
     int num_kv_heads;     // query head h reads KV head h % num_kv_heads
     int head_dim;         // 128 or 256
+    int sk_ctas;          // > 0: stream-K grid of this many CTAs per head block (0: chunked)
+    int32_t* sk_prefix;   // stream-K: [num_seqs + 1] tiles before each sequence, then the total
     int max_chunks;
     int chunk_tokens;
     int row_scales;       // 1: EC_SCALE_ROW
@@ -137,9 +139,13 @@ cudaError_t launch_fused_dequant_dot(const float* q, const int8_t* k, const floa
                                      uint32_t dim, uint32_t seq_len, cudaStream_t st);
 
 // Split policy shared by the workspace query and the launch.
+// Chunked plan (sk_ctas == 0): max_chunks chunks of chunk_tokens tokens per
+// sequence.  Stream-K plan (sk_ctas > 0): sk_ctas CTAs per head block share
+// the batch's tiles evenly; chunk_tokens then only bounds the lengths.
 struct DecodePlan {
     int chunk_tokens;
     int max_chunks;
+    int sk_ctas;
 };
 // The compiled decode kernel for a shape: hc KV heads per CTA, qw quads of
 // query heads per KV head, scw = num_kv_heads, dv = head_dim / 128, and its
@@ -151,8 +157,10 @@ DecodeVariant decode_variant(int num_kv_heads, int group, int head_dim);
 // total_tokens: host estimate of the batch's cached tokens (0: unknown, every
 // sequence is assumed to be max_seq_len long).  The kernel variant of
 // (num_kv_heads, num_heads, head_dim) sets how many CTAs fit on the GPU at once.
+// allow_stream false: a chunked plan (the context-parallel exchange merges
+// a sequence's chunks itself).
 DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens,
-                       int num_kv_heads, int num_heads, int head_dim);
+                       int num_kv_heads, int num_heads, int head_dim, bool allow_stream = true);
 size_t decode_workspace_bytes(const DecodePlan& p, int num_seqs, int num_heads, int head_dim);
 // Returns cudaErrorInvalidValue for a shape outside the envelope.
 cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan, void* ws,

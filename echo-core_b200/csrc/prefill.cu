@@ -34,10 +34,12 @@
 // scores.  K and V codes are exact in f16; p'
 // enters the PV product as an f16 pair hi + lo (two MMAs), about 22 bits, so
 // the only rounding of consequence is Q's bf16 cast (part of the contract).
-// p' = p * v_scale * 2^-E is carried in f16 under a CTA-wide power of two
-// 2^-E chosen from the first tile's largest v-scale and raised (with O
-// rescaled to match) whenever a later tile's v-scales would leave the f16
-// range, so any finite v-scale is in range; the output is O * 2^E / l.
+// Each query row carries its own power of two 2^-E, fixed before the first
+// tile from the largest v-scale of the row's causal range, that keeps every
+// p' = p * v_scale * 2^-E below 2^15 (any finite v-scale is in range) and
+// puts the row's largest p' near the top of f16's range (its relative
+// precision).  It enters the softmax exponent, 2^(s - m - E), so both p'
+// and the row sum l carry it and the output O / l needs no correction.
 // Every wait is bounded; a timeout raises a CTA-wide abort flag so that every
 // role stops, waits for its own in-flight work and the CTA frees its tensor
 // memory before returning.  The softmax warps decide together (a barrier
@@ -82,8 +84,9 @@ enum {
     B_KV_FULL = 0, B_KV_EMPTY = 2, B_KC_FULL = 4, B_KC_FREE = 5, B_VC_FULL = 6, B_VC_FREE = 8,
     B_S_FULL = 10, B_P_FULL = 13, B_PV_BUF = 16, B_Q_FULL = 19, B_DRAIN, NBARS
 };
-constexpr int OFF_MISC = OFF_BAR + NBARS * 8;      // [0] tmem base, [1] abort flag, [2] v-scale max
-constexpr int SMEM = 1024 + OFF_MISC + 16;
+constexpr int OFF_MISC = OFF_BAR + NBARS * 8;      // [0] tmem base, [1] abort flag
+constexpr int OFF_EROW = OFF_MISC + 16;            // [BM] each query row's E (float)
+constexpr int SMEM = 1024 + OFF_EROW + BM * 4;
 static_assert(SMEM <= 227 * 1024, "shared memory budget");
 
 // Tensor memory: three S/P buffers of 128 columns (QK^T scores, overwritten in
@@ -92,9 +95,12 @@ constexpr int TMEM_COLS = 512;
 constexpr int NSP = 3;
 constexpr int TM_O = 384;
 constexpr float kLazyRescale = 8.0f;
-// Largest v_scale * 2^-E a tile may carry: p <= 2^8 under the lazy rescale,
-// so p' stays below 2^15, inside f16 (max 65504) with its hi/lo split.
-constexpr float kVScaleMax = 128.0f;
+// E puts a row's v-scales below 2^7 (p <= 2^8 under the lazy rescale, so p'
+// < 2^15, inside f16 with its hi/lo split), within [kEMin, 121]: the floor
+// (reached only by v-scales below 2^-57) keeps 2^(s - m - E) and the row sum
+// finite for any sequence length.
+constexpr int kVScaleBits = 7;
+constexpr int kEMin = -64;
 constexpr unsigned kFull = 0xffffffffu;
 
 // Instruction descriptors (kind::f16, fp32 accumulate, M = 128, N = 128).
@@ -108,7 +114,6 @@ struct Smem {
         return reinterpret_cast<volatile int*>(base + OFF_MISC) + 1;
     }
     __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(base + OFF_MISC); }
-    __device__ int* vmax_bits() const { return reinterpret_cast<int*>(base + OFF_MISC) + 2; }
 };
 
 // Bounded wait that also gives up as soon as another role has aborted.  The
@@ -389,7 +394,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(S.bar(B_Q_FULL), 8);
         mbar_init(S.bar(B_DRAIN), 1);
         *S.abort_flag() = 0;
-        *S.vmax_bits() = 0;
         fence_mbar_init();
     }
     if (warp == kMmaWarp) {
@@ -516,6 +520,70 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* scb = reinterpret_cast<float*>(S.base + OFF_SC);
         float* red = reinterpret_cast<float*>(S.base + OFF_RED);
 
+        const int sc_col = st & (BN - 1);         // this thread's tile column
+        // scale of kv slot t (< len) from src
+        auto scale_of = [&](const float* src, int t) -> float {
+            if (PAGED) {
+                int64_t slot;
+                if (!page_slot(pm, seq, off, t, a.total_slots, slot)) return 0.0f;
+                return a.row_scales ? src[slot] : src[(size_t)slot * HKV + g];
+            }
+            const int slot = off + t;
+            return a.row_scales ? src[slot] : src[(size_t)slot * HKV + g];
+        };
+        // Each row's E, before Q (work placed between Q's arrival and the
+        // first tile measured slower).  Every row sees slots [0, past + q0]
+        // (the shared part); row r also sees the r slots after it (the band).
+        // The 256 threads take the shared part's v-scales 16 x 256 at a time;
+        // thread st < 127 also takes band slot st and an exclusive max-scan
+        // over the band gives row r its band maximum.
+        {
+            const int shared_end = past + q0 + 1;           // exclusive
+            float vm = 0.0f;
+            for (int t0 = st; t0 < shared_end; t0 += 16 * kSoftmaxThreads) {
+                float v[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const int t = t0 + u * kSoftmaxThreads;
+                    v[u] = t < shared_end ? scale_of(a.val_scales, t) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 16; ++u) vm = fmaxf(vm, v[u]);
+            }
+            float bv = 0.0f;                                 // band slot st
+            if (st < BN && shared_end + st < kv_end) bv = scale_of(a.val_scales, shared_end + st);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) vm = fmaxf(vm, __shfl_xor_sync(kFull, vm, o));
+            float incl = bv;                                 // inclusive scan in the warp
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float n = __shfl_up_sync(kFull, incl, o);
+                if (lane >= o) incl = fmaxf(incl, n);
+            }
+            // (clear of the Q block's maxima at red[2 * 2 * BM - 8..]; tile
+            // 1's exchange is the next to write here)
+            float* vmaxw = red + 2 * 2 * BM - 24;
+            float* btot = red + 2 * 2 * BM - 16;
+            if (lane == 0) vmaxw[warp] = vm;
+            if (lane == 31 && warp < 4) btot[warp] = incl;
+            named_bar(1, kSoftmaxThreads);
+            if (st < BM) {
+                float m = 0.0f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) m = fmaxf(m, vmaxw[w]);
+                for (int w = 0; w < warp; ++w) m = fmaxf(m, btot[w]);   // earlier band warps
+                const float prev = __shfl_up_sync(kFull, incl, 1);
+                if (lane >= 1) m = fmaxf(m, prev);           // band slots < st
+                // m < 2^ev; an infinite v-scale takes the largest E (and the
+                // non-finite answer the reference's float loop gives)
+                int ev = 0;
+                if (m > 3.4028235e38f) ev = 128;
+                else if (m > 0.0f) frexpf(m, &ev);
+                reinterpret_cast<float*>(S.base + OFF_EROW)[st] =
+                    (float)max(kEMin, ev - kVScaleBits);
+            }
+            // tile 0's bar_any (a barrier of these threads) precedes every read
+        }
         // Q: cast to bf16 (the contract), then scaled by 2^qe, one power of two
         // for the whole CTA that brings max |q| into [2^14, 2^15), and stored
         // as f16.  Every bf16 value in range is exact in f16 after that
@@ -571,22 +639,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         // per-token scales of a tile: thread st loads k-scale * qk_mul of column
         // st (st < 128) or v-scale of column st - 128, two tiles ahead
-        const int sc_col = st & (BN - 1);
         const float* sc_src = st < BN ? a.key_scales : a.val_scales;
         const float sc_mul = st < BN ? a.qk_mul * q_inv : 1.0f;
         // (raw value: the multiply waits until the next tile, when the load has
         // landed, so the in-order warp does not stall on it here)
         auto load_scale = [&](int j) -> float {
-            if (PAGED) {
-                if (j * BN + sc_col >= len) return 0.0f;
-                int64_t slot;
-                if (!page_slot(pm, seq, off, j * BN + sc_col, a.total_slots, slot)) return 0.0f;
-                return a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g];
-            }
-            const int slot = off + j * BN + sc_col;
-            if (j * BN + sc_col >= len) return 0.0f;
-            return a.row_scales ? sc_src[slot] : sc_src[(size_t)slot * HKV + g];
+            const int t = j * BN + sc_col;
+            return t < len ? scale_of(sc_src, t) : 0.0f;
         };
+
+        const float* erow = reinterpret_cast<const float*>(S.base + OFF_EROW);
 
         // From here on a thread works in the 16-lane layout: quad g = lane / 4,
         // q = lane % 4.  It owns the rows rw[k] = 32*(warp%4) + 16*(k/2) + g +
@@ -607,10 +669,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         float sc_next = load_scale(0);
         float sc_next2 = ntiles > 1 ? load_scale(1) : 0.0f;   // two tiles ahead
-        // v-scales enter p' times 2^-vexp (CTA-wide; set from tile 0's largest
-        // v-scale, raised when a later tile's would leave the f16 range)
-        int vexp = 0;
-        float v_mul = 1.0f;
         float m_run[4];
         float2 l_run[4];                           // this thread's even / odd columns
 #pragma unroll
@@ -621,34 +679,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (; j < ntiles; ++j) {
             const int sb = j % NSP, par = j & 1;
             float* sck = scb + par * 2 * BN;
-            const float raw = sc_next;
-            const bool is_v = st >= BN;
-            sck[st] = raw * (is_v ? v_mul : sc_mul);
-            // tile 0 sets the v-scale exponent; later tiles raise it only
-            // when one of their v-scales would leave p''s f16 range
-            const bool grow = is_v && (j == 0 || raw * v_mul > kVScaleMax);
+            sck[st] = sc_next * sc_mul;
             sc_next = sc_next2;
             if (j + 2 < ntiles) sc_next2 = load_scale(j + 2);
             bad |= !warp_wait_abortable(S.bar(B_S_FULL + sb), (j / NSP) & 1, abort_flag);
-            // tile j's scales are visible to all, and all agree whether to go
-            // on; failures and exponent changes are rare and share one barrier
-            float ofac = 1.0f;                     // O rescale for a raised exponent
-            if (bar_any(1, kSoftmaxThreads, bad || grow)) {
-                if (bar_any(1, kSoftmaxThreads, bad)) break;
-                int* vmb = S.vmax_bits();
-                if (is_v) atomicMax(vmb, __float_as_int(raw));   // v-scales are >= 0
-                named_bar(1, kSoftmaxThreads);
-                const float vmax = __int_as_float(*vmb);
-                int ex = 0;
-                if (vmax > 0.0f) frexpf(vmax, &ex);   // vmax < 2^ex
-                const int e_new = j == 0 ? min(100, max(-100, ex - 7)) : max(vexp, min(100, ex - 7));
-                if (j > 0) ofac = ldexpf(1.0f, vexp - e_new);
-                vexp = e_new;
-                v_mul = ldexpf(1.0f, -vexp);
-                if (is_v) sck[st] = raw * v_mul;
-                named_bar(1, kSoftmaxThreads);
-                if (st == 0) *vmb = 0;             // next read is past another barrier
-            }
+            // tile j's scales are visible to all, and all agree whether to go on
+            if (bar_any(1, kSoftmaxThreads, bad)) break;
             tc_fence_after();
             float2 ks[8], vs[8];                   // scales of this thread's column pairs
 #pragma unroll
@@ -726,12 +762,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             float neg_m[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) neg_m[k] = m_run[k] == -INFINITY ? 0.0f : -m_run[k];
+            for (int k = 0; k < 4; ++k)                    // -m - E: p' and l carry 2^-E
+                neg_m[k] = (m_run[k] == -INFINITY ? 0.0f : -m_run[k]) -
+                           erow[(warp & 3) * 32 + 16 * (k >> 1) + gq + 8 * (k & 1)];
 
             // rescale this half of the O rows only when some row's maximum
-            // jumped or the v-scale exponent rose (rare): O must first hold
-            // every earlier tile
-            if (j >= 1 && (__any_sync(kFull, any_corr) || ofac != 1.0f)) {
+            // jumped (rare): O must first hold every earlier tile
+            if (j >= 1 && __any_sync(kFull, any_corr)) {
                 const int pj = j - 1;
                 if (warp_wait_abortable(S.bar(B_PV_BUF + pj % NSP), (pj / NSP) & 1, abort_flag)) {
                     tc_fence_after();
@@ -744,10 +781,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tmem_ld_16x256b_x2(oa, o);
 #pragma unroll
                             for (int i = 0; i < 8; i += 4) {
-                                o[i] *= corr[2 * blk] * ofac;
-                                o[i + 1] *= corr[2 * blk] * ofac;
-                                o[i + 2] *= corr[2 * blk + 1] * ofac;
-                                o[i + 3] *= corr[2 * blk + 1] * ofac;
+                                o[i] *= corr[2 * blk];
+                                o[i + 1] *= corr[2 * blk];
+                                o[i + 2] *= corr[2 * blk + 1];
+                                o[i + 3] *= corr[2 * blk + 1];
                             }
                             tmem_st_16x256b_x2(oa, o);
                         }
@@ -837,8 +874,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float l = l_sum[k] + red[((ntiles & 1) * 2 + (half ^ 1)) * BM + rw];
                     bool row_live;
                     float* op = out_row(a, rw, row_live) + c0 + 2 * qq;
-                    const float inv =
-                        (row_live && l > 0.0f) ? ldexpf(__fdiv_rn(1.0f, l), vexp) : 0.0f;
+                    const float inv = (row_live && l > 0.0f) ? __fdiv_rn(1.0f, l) : 0.0f;
                     if (row_live) {
 #pragma unroll
                         for (int n = 0; n < 8; ++n)

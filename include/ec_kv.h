@@ -366,7 +366,8 @@ EC_API int ec_cp_decode_exchange(ec_cp_comm* comm, const ec_kv_batch* batch, con
  * to bf16 on load (bf16-cast queries); out has the same shape, fp32.  Runs on
  * the tcgen05 tensor cores; head_dim 128, any num_kv_heads dividing num_heads.
  * Any finite v-scale is in range: p' = p * v_scale is carried in f16 under a
- * power of two that follows the v-scales the kernel meets. */
+ * power of two per query row, set from the largest v-scale of the row's
+ * causal range. */
 EC_API int ec_prefill_attention(const ec_kv_batch* batch, const float* q, float* out,
                                 uint32_t n_new, uint32_t num_heads, float softmax_scale,
                                 ec_stream_t stream);
