@@ -692,6 +692,10 @@ def run_cp_arm(args, rank, world, local_rank):
     # N = 1: the plain decode (decode + chunk merge).
     peer = world > 1 and not args.cp_nccl
     fused = peer and not args.cp_unfused
+    # graph replay at one GPU; with ranks the step stays eager (measured at 2
+    # GPUs: fused step 0.1061-0.1066 ms eager against 0.1099-0.1101 ms
+    # replayed with device epochs; unfused 0.1157 against 0.1191 ms)
+    use_graph = args.graph and world == 1
     cx = ranks.CPExchange(1, H) if peer else None
 
     def step():
@@ -711,11 +715,6 @@ def run_cp_arm(args, rank, world, local_rank):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    # graph replay at one GPU (the partial and the merge captured once).  With
-    # ranks, eager launches measured 3% faster than replaying a captured step
-    # with device epochs (0.1157 against 0.1191 ms at 2 GPUs): the exchange
-    # stays eager there.
-    use_graph = args.graph and world == 1
     graph = None
     if use_graph:
         graph = torch.cuda.CUDAGraph()

@@ -5,9 +5,10 @@
 // each rank computes the unnormalised partial (m, l, O) of its slice per
 // (sequence, head) (ec_decode_attention_partial).  Instead of an all-gather
 // followed by a merge launch, every CTA of this kernel owns one (sequence,
-// head): it stores its rank's partial into slot [rank] of every rank's
-// receive buffer with plain peer stores (CUDA IPC mappings, no multicast),
-// publishes a per-(sequence, head) flag with release semantics, waits with
+// head), or one split of its dims: it stores its rank's partial into slot
+// [rank] of every rank's receive buffer with plain peer stores (CUDA IPC
+// mappings, no multicast), publishes a per-(sequence, head, split) flag with
+// release semantics, waits with
 // acquire loads until every rank's flag for this step has arrived in its own
 // buffer, and merges the world's partials in rank order.  Receive buffers are
 // double-buffered by step parity: a fast rank publishing step e+1 never
@@ -38,133 +39,191 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
-constexpr int kChunkSplit = 4;                     // thread groups of the chunk merge
+constexpr int kXThreads = 256;                    // threads of the chunked form
 constexpr int kMaxChunkMerge = 1024;               // chunks per (sequence, head), at most
+constexpr int kXBatch = 8;                         // O loads in flight a thread
+constexpr int kXMlPerThread = kMaxChunkMerge / kXThreads;
 
-// This rank's partial of (s, h) merged from its split-K chunks: (o[d] for the
-// calling thread's dim, m, l), the LSE merge of the chunk merge kernel.
-// Every thread of the block takes part; threads d < D get o.
-__device__ void merge_chunks(const CpExchangeArgs& a, int s, int h, float& o, float& m_out,
-                             float& l_out) {
-    constexpr int NT = D * kChunkSplit;
+// Dims split of the chunked form: gridDim.z CTAs per (sequence, head), more
+// when the batch has few pairs (one long sequence: 16 pairs on 148 SMs).
+int exchange_splits(int pairs) { return pairs <= 64 ? 8 : pairs <= 128 ? 4 : pairs <= 256 ? 2 : 1; }
+
+// This rank's partial of (s, h) merged from its split-K chunks, for the
+// CTA's dims [z * dims, (z + 1) * dims): o (dim z * dims + t, for threads
+// t < dims), m and l (every thread), the LSE merge of the chunk merge
+// kernel.  Threads are float4 column groups x chunk lanes; each issues its
+// first kXBatch O loads together with the (m, l) loads, before the maximum
+// is known, so the merge is one dependent round trip after the table read.
+__device__ void merge_chunks(const CpExchangeArgs& a, int s, int h, int z, int dims, float& o,
+                             float& m_out, float& l_out) {
+    constexpr int kWarpsX = kXThreads / 32;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int d = tid % D, part = tid / D;
     const int H = a.num_heads;
+    const int groups = dims / 4, lanes = kXThreads / groups;
     int len = a.seq_len ? a.seq_len[s] : 0;
     len = len < 0 ? 0 : len;
     int nch = (len + a.chunk_tokens - 1) / a.chunk_tokens;
     nch = nch > a.max_chunks ? a.max_chunks : nch;   // a bad entry is flagged by the decode
     const size_t base = (size_t)s * a.max_chunks * H + h;
-    __shared__ float s_f[kMaxChunkMerge], s_red[NT];
+    __shared__ float s_f[kMaxChunkMerge];
+    __shared__ __align__(16) float s_acc[kXThreads * 4];   // [lane][dims]
+    __shared__ float s_rm[kWarpsX], s_rl[kWarpsX];
     __shared__ float s_M, s_L;
-    auto ml_of = [&](int c) {
-        return *reinterpret_cast<const float2*>(a.part_ml + (base + (size_t)c * H) * 2);
-    };
+
+    const int gi = tid % groups, cl = tid / groups;
+    const float4* po = reinterpret_cast<const float4*>(a.part_o + base * D + z * dims) + gi;
+    const size_t cstride = (size_t)H * (D / 4);        // float4s from chunk to chunk
+    float4 v[kXBatch];
+#pragma unroll
+    for (int k = 0; k < kXBatch; ++k) {
+        const int c = cl + k * lanes;
+        v[k] = c < nch ? po[(size_t)c * cstride] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    float2 ml[kXMlPerThread];
+#pragma unroll
+    for (int k = 0; k < kXMlPerThread; ++k) {
+        const int c = tid + k * kXThreads;
+        ml[k] = c < nch ? *reinterpret_cast<const float2*>(a.part_ml + (base + (size_t)c * H) * 2)
+                        : make_float2(-INFINITY, 0.0f);
+    }
     float m = -INFINITY;
-    for (int c = tid; c < nch; c += NT) m = fmaxf(m, ml_of(c).x);
+#pragma unroll
+    for (int k = 0; k < kXMlPerThread; ++k) m = fmaxf(m, ml[k].x);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (lane == 0) s_red[wid] = m;
+    if (lane == 0) s_rm[wid] = m;
     __syncthreads();
     if (tid == 0) {
         float M = -INFINITY;
-        for (int w = 0; w < NT / 32; ++w) M = fmaxf(M, s_red[w]);
+        for (int w = 0; w < kWarpsX; ++w) M = fmaxf(M, s_rm[w]);
         s_M = M;
     }
     __syncthreads();
     const float M = s_M;
     float lsum = 0.0f;
-    for (int c = tid; c < nch; c += NT) {
-        const float2 mlc = ml_of(c);
-        const float f = mlc.x == -INFINITY ? 0.0f : exp2f(mlc.x - M);
-        s_f[c] = f;
-        lsum += f * mlc.y;
+#pragma unroll
+    for (int k = 0; k < kXMlPerThread; ++k) {
+        const int c = tid + k * kXThreads;
+        const float f = ml[k].x == -INFINITY ? 0.0f : exp2f(ml[k].x - M);
+        if (c < nch) s_f[c] = f;
+        lsum += f * ml[k].y;
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
-    __syncthreads();
-    if (lane == 0) s_red[wid] = lsum;
-    __syncthreads();
+    if (lane == 0) s_rl[wid] = lsum;
+    __syncthreads();                                  // s_f and s_rl complete
     if (tid == 0) {
         float L = 0.0f;
-        for (int w = 0; w < NT / 32; ++w) L += s_red[w];
+        for (int w = 0; w < kWarpsX; ++w) L += s_rl[w];
         s_L = L;
     }
-    __syncthreads();
-    float so = 0.0f;
-#pragma unroll 4
-    for (int c = part; c < nch; c += kChunkSplit) so += s_f[c] * a.part_o[(base + (size_t)c * H) * D + d];
-    s_red[part * D + d] = so;
-    __syncthreads();
-    o = 0.0f;
-    if (part == 0) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-        for (int q = 0; q < kChunkSplit; ++q) o += s_red[q * D + d];
+    for (int k = 0; k < kXBatch; ++k) {
+        const int c = cl + k * lanes;
+        const float f = c < nch ? s_f[c] : 0.0f;
+        acc.x += f * v[k].x;
+        acc.y += f * v[k].y;
+        acc.z += f * v[k].z;
+        acc.w += f * v[k].w;
     }
+    for (int c0 = cl + kXBatch * lanes; c0 < nch; c0 += kXBatch * lanes) {
+#pragma unroll
+        for (int k = 0; k < kXBatch; ++k) {
+            const int c = c0 + k * lanes;
+            v[k] = c < nch ? po[(size_t)c * cstride] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int k = 0; k < kXBatch; ++k) {
+            const int c = c0 + k * lanes;
+            const float f = c < nch ? s_f[c] : 0.0f;
+            acc.x += f * v[k].x;
+            acc.y += f * v[k].y;
+            acc.z += f * v[k].z;
+            acc.w += f * v[k].w;
+        }
+    }
+    reinterpret_cast<float4*>(s_acc)[cl * groups + gi] = acc;
+    __syncthreads();                                  // s_acc and s_L complete
+    o = 0.0f;
+    if (tid < dims)
+        for (int q = 0; q < lanes; ++q) o += s_acc[q * dims + tid];   // lanes in order
     m_out = nch ? M : -INFINITY;
     l_out = s_L;
     __syncthreads();
 }
 
+// One CTA per (sequence, head, dims split z): gridDim.z = 1 for the plain
+// form (partials given), exchange_splits() for the chunked form.  Every
+// split has its own (m, l) slot, flag and device epoch, so the CTAs of a
+// (sequence, head) publish, wait and merge independently.
 template <bool CHUNKS>
-__global__ void __launch_bounds__(CHUNKS ? D * kChunkSplit : D) cp_exchange_kernel(CpExchangeArgs a) {
-    const int s = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+__global__ void __launch_bounds__(CHUNKS ? kXThreads : D) cp_exchange_kernel(CpExchangeArgs a) {
+    const int s = blockIdx.x, h = blockIdx.y, z = blockIdx.z, t = threadIdx.x;
     const int S = a.num_seqs, H = a.num_heads, W = a.world;
+    const int dims = D / (int)gridDim.z;
     const size_t sh = (size_t)s * H + h;
+    const size_t shz = sh * kCpSplitMax + z;
     if (CHUNKS) {
         pdl_wait();   // the decode kernel's chunk partials
         pdl_trigger();
     }
-    // device epochs: one counter per (sequence, head), advanced by the only
-    // CTA that uses it, so every call of a replayed graph runs the next epoch
+    // device epochs: one counter per (sequence, head, split), advanced by the
+    // only CTA that uses it, so every call of a replayed graph runs the next epoch
     __shared__ uint32_t s_epoch;
-    if (d == 0) {
+    if (t == 0) {
         uint32_t e = a.epoch;
         if (a.epoch_dev) {
-            e = a.epoch_dev[sh] + 1;
-            a.epoch_dev[sh] = e;
+            e = a.epoch_dev[shz] + 1;
+            a.epoch_dev[shz] = e;
         }
         s_epoch = e;
     }
     __syncthreads();
     const uint32_t epoch = s_epoch;
     const int par = epoch & 1;
-    // per rank buffer: [2 parities][W ranks][S][H] of O (D floats), ml (2), flag (1)
+    // per rank buffer: [2 parities][W ranks][S][H] of O (D floats), then
+    // [2][W][S][H][kCpSplitMax] of (m, l) and of flags
     const size_t n_sh = (size_t)S * H;
     auto o_at = [&](float* base, int p, int r) { return base + ((size_t)(p * W + r) * n_sh + sh) * D; };
     auto ml_at = [&](float* base, int p, int r) {
-        return base + (size_t)2 * W * n_sh * D + ((size_t)(p * W + r) * n_sh + sh) * 2;
+        return base + (size_t)2 * W * n_sh * D + (((size_t)(p * W + r) * n_sh + sh) * kCpSplitMax + z) * 2;
     };
     auto flag_at = [&](float* base, int p, int r) {
-        return reinterpret_cast<uint32_t*>(base + (size_t)2 * W * n_sh * (D + 2)) +
-               (size_t)(p * W + r) * n_sh + sh;
+        return reinterpret_cast<uint32_t*>(base + (size_t)2 * W * n_sh * (D + 2 * kCpSplitMax)) +
+               ((size_t)(p * W + r) * n_sh + sh) * kCpSplitMax + z;
     };
 
-    // ---- publish this rank's partial into slot [rank] of every rank's buffer
+    // ---- publish this rank's partial (this split's dims) into slot [rank]
+    // of every rank's buffer
     float o, ml;
     if (CHUNKS) {
         float m_loc, l_loc;
-        merge_chunks(a, s, h, o, m_loc, l_loc);
-        ml = d == 0 ? m_loc : l_loc;
+        merge_chunks(a, s, h, z, dims, o, m_loc, l_loc);
+        ml = t == 0 ? m_loc : l_loc;
     } else {
-        o = a.part_o[sh * D + d];
-        ml = d < 2 ? a.part_ml[sh * 2 + d] : 0.0f;
+        o = a.part_o[sh * D + t];
+        ml = t < 2 ? a.part_ml[sh * 2 + t] : 0.0f;
     }
-    if (d < D) {
+    if (t < dims) {
         for (int r = 0; r < W; ++r) {
             float* base = a.peer_base[r];
-            o_at(base, par, a.rank)[d] = o;
-            if (d < 2) ml_at(base, par, a.rank)[d] = ml;
+            o_at(base, par, a.rank)[z * dims + t] = o;
+            if (t < 2) ml_at(base, par, a.rank)[t] = ml;
         }
     }
-    __threadfence_system();
+    // the CTA's stores, then thread 0's system-scope release stores of the
+    // flags: the barrier orders the other threads' stores before the release,
+    // which is cumulative, so a rank that acquires the flag sees them all.  (A
+    // fence.sc.sys before the flags measured 7 us a step on one rank; the
+    // release alone is what the protocol needs.)
     __syncthreads();
-    if (d == 0)
+    if (t == 0)
         for (int r = 0; r < W; ++r) st_release_sys(flag_at(a.peer_base[r], par, a.rank), epoch);
 
     // ---- wait for every rank's flag of this step in the local buffer
     __shared__ int s_bad;
-    if (d == 0) {
+    if (t == 0) {
         int bad = 0;
         float* mine = a.peer_base[a.rank];
         for (int r = 0; r < W && !bad; ++r) {
@@ -181,9 +240,10 @@ __global__ void __launch_bounds__(CHUNKS ? D * kChunkSplit : D) cp_exchange_kern
     }
     __syncthreads();
     float* mine = a.peer_base[a.rank];
-    if (d >= D) return;
+    if (t >= dims) return;
+    const size_t oi = sh * D + z * dims + t;
     if (s_bad) {
-        a.out[sh * D + d] = 0.0f;
+        a.out[oi] = 0.0f;
         return;
     }
     // ---- merge in rank order (the LSE merge of ec_lse_combine)
@@ -193,25 +253,26 @@ __global__ void __launch_bounds__(CHUNKS ? D * kChunkSplit : D) cp_exchange_kern
     for (int r = 0; r < W; ++r) {
         const float* mlr = ml_at(mine, par, r);
         const float f = mlr[0] == -INFINITY ? 0.0f : exp2f(mlr[0] - M);
-        so += f * o_at(mine, par, r)[d];
+        so += f * o_at(mine, par, r)[z * dims + t];
         sl += f * mlr[1];
     }
-    a.out[sh * D + d] = sl > 0.0f ? __fdiv_rn(so, sl) : 0.0f;
+    a.out[oi] = sl > 0.0f ? __fdiv_rn(so, sl) : 0.0f;
 }
 
 }  // namespace
 
 size_t cp_exchange_buffer_bytes(int world, int num_seqs, int num_heads) {
     const size_t n = (size_t)2 * world * num_seqs * num_heads;
-    return n * (D + 2) * sizeof(float) + n * sizeof(uint32_t);
+    return n * (D + 2 * kCpSplitMax) * sizeof(float) + n * kCpSplitMax * sizeof(uint32_t);
 }
 
 cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st) {
     if (a.num_seqs <= 0 || a.num_heads <= 0) return cudaSuccess;
     if (a.max_chunks > 0) {
         if (a.max_chunks > kMaxChunkMerge || a.chunk_tokens <= 0) return cudaErrorInvalidValue;
-        return launch_pdl(cp_exchange_kernel<true>, dim3(a.num_seqs, a.num_heads),
-                          dim3(D * kChunkSplit), 0, st, a);
+        const int z = exchange_splits(a.num_seqs * a.num_heads);
+        return launch_pdl(cp_exchange_kernel<true>, dim3(a.num_seqs, a.num_heads, z),
+                          dim3(kXThreads), 0, st, a);
     }
     cp_exchange_kernel<false><<<dim3(a.num_seqs, a.num_heads), D, 0, st>>>(a);
     return cudaGetLastError();

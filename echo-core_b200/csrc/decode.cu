@@ -954,23 +954,31 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
 }
 
 // Merges the chunk partials of one (sequence, head): the maximum M of the
-// chunk maxima and the weights 2^(m_c - M) (kept in shared memory) with the
-// weighted sum of l -- with one chunk per thread up to 512 chunks, else in
-// two passes over the chunks -- then O, where each of kCombineSplit thread
-// groups sums every kCombineSplit-th chunk for every dim (independent loads,
-// so a long chunk list is not one serial chain).  A thread covers dim d of
-// each of the head's DV 128-dim blocks.  Reductions run in a fixed order:
-// the result does not depend on timing.
-constexpr int kCombineSplit = 4;
-constexpr int kCombineThreads = D * kCombineSplit;
+// chunk maxima, the weights 2^(m_c - M) (kept in shared memory), L = the
+// weighted sum of l, and O = the weighted sum of the chunks' O rows.  The
+// head's dims are split over gridDim.z CTAs (8 when the batch has few
+// (sequence, head) pairs, so that one long sequence's merge is spread over
+// many SMs instead of a few).  A CTA's threads are float4 column groups x
+// chunk lanes; each issues its first kBatch O loads together with the (m, l)
+// loads, before M is known, so that a merge of a few hundred chunks is two
+// dependent global round trips (table entry, then partials) instead of a
+// chain.  Reductions run in a fixed order: the result does not depend on
+// timing.
+constexpr int kCombineThreads = 256;
+constexpr int kCombineBatch = 8;                  // O loads in flight a thread
+constexpr int kCombineMlPerThread = kMaxChunks / kCombineThreads;
+static_assert(kMaxChunks % kCombineThreads == 0, "(m, l) loads cover every chunk");
 template <int DV>
 __global__ void __launch_bounds__(kCombineThreads, 4) combine_kernel(const DecodeArgs a) {
     constexpr int DH = D * DV;
     constexpr int kWarpsC = kCombineThreads / 32;
     const int seq = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int d = tid % D, part = tid / D;
     const int H = a.num_heads;
+    const int dims = DH / (int)gridDim.z;            // this CTA's dims: [z * dims, (z+1) * dims)
+    const int groups = dims / 4;
+    const int lanes = kCombineThreads / groups;
+    const int z = blockIdx.z;
     pdl_wait();  // the partials of decode_kernel
     pdl_trigger();
     int32_t off, cap, len;
@@ -992,107 +1000,112 @@ __global__ void __launch_bounds__(kCombineThreads, 4) combine_kernel(const Decod
         base = (size_t)(c_first + seq) * H + h;
     } else {
         nch = (len + a.chunk_tokens - 1) / a.chunk_tokens;
+        nch = nch < a.max_chunks ? nch : a.max_chunks;
         base = (size_t)seq * a.max_chunks * H + h;
     }
-    __shared__ float s_f[kMaxChunks], s_l[kCombineThreads], s_red[DH * kCombineSplit];
+    nch = nch < kMaxChunks ? nch : kMaxChunks;
+    __shared__ float s_f[kMaxChunks];
+    __shared__ __align__(16) float s_acc[kCombineThreads * 4];   // [lane][dims]
+    __shared__ float s_rm[kWarpsC], s_rl[kWarpsC];
     __shared__ float s_M, s_L;
-    auto ml_of = [&](int c) {
-        return *reinterpret_cast<const float2*>(a.part_ml + (base + (size_t)c * H) * 2);
-    };
-    if (nch <= kCombineThreads) {
-        // one chunk per thread: its (m, l) loaded once
-        const bool has_c = tid < nch;
-        const float2 mlc = has_c ? ml_of(tid) : make_float2(-INFINITY, 0.0f);
-        float m = mlc.x;
+
+    // the first batch of O loads: chunk lane cl takes chunks cl, cl + lanes, ...
+    const int gi = tid % groups, cl = tid / groups;
+    const float4* po = reinterpret_cast<const float4*>(a.part_o + base * DH + z * dims) + gi;
+    const size_t cstride = (size_t)H * (DH / 4);    // float4s from chunk to chunk
+    float4 v[kCombineBatch];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) s_red[wid] = m;
-        __syncthreads();
-        if (tid == 0) {
-            float M = -INFINITY;
-            for (int w = 0; w < kWarpsC; ++w) M = fmaxf(M, s_red[w]);
-            s_M = M;
-        }
-        __syncthreads();
-        const float f = (has_c && mlc.x != -INFINITY) ? exp2f(mlc.x - s_M) : 0.0f;
-        if (has_c) {
-            s_f[tid] = f;
-            s_l[tid] = f * mlc.y;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            float L = 0.0f;
-            for (int c = 0; c < nch; ++c) L += s_l[c];
-            s_L = L;
-        }
-    } else {
-        // pass 1: M = max over the chunk maxima
-        float m = -INFINITY;
-        for (int c = tid; c < nch; c += kCombineThreads) m = fmaxf(m, ml_of(c).x);
+    for (int k = 0; k < kCombineBatch; ++k) {
+        const int c = cl + k * lanes;
+        v[k] = c < nch ? po[(size_t)c * cstride] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    // (m, l) of chunks tid, tid + 256, ...
+    float2 ml[kCombineMlPerThread];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) s_red[wid] = m;
-        __syncthreads();
-        if (tid == 0) {
-            float M = -INFINITY;
-            for (int w = 0; w < kWarpsC; ++w) M = fmaxf(M, s_red[w]);
-            s_M = M;
-        }
-        __syncthreads();
-        const float M = s_M;
-        // pass 2: chunk weights and sum_c 2^(m_c - M) * l_c
-        float lsum = 0.0f;
-        for (int c = tid; c < nch; c += kCombineThreads) {
-            const float2 mlc = ml_of(c);
-            const float f = mlc.x == -INFINITY ? 0.0f : exp2f(mlc.x - M);
-            s_f[c] = f;
-            lsum += f * mlc.y;
-        }
+    for (int k = 0; k < kCombineMlPerThread; ++k) {
+        const int c = tid + k * kCombineThreads;
+        ml[k] = c < nch ? *reinterpret_cast<const float2*>(a.part_ml + (base + (size_t)c * H) * 2)
+                        : make_float2(-INFINITY, 0.0f);
+    }
+    float m = -INFINITY;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-        __syncthreads();                               // s_red's maxima are read
-        if (lane == 0) s_red[wid] = lsum;
-        __syncthreads();
-        if (tid == 0) {
-            float L = 0.0f;
-            for (int w = 0; w < kWarpsC; ++w) L += s_red[w];
-            s_L = L;
-        }
+    for (int k = 0; k < kCombineMlPerThread; ++k) m = fmaxf(m, ml[k].x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_rm[wid] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float M = -INFINITY;
+        for (int w = 0; w < kWarpsC; ++w) M = fmaxf(M, s_rm[w]);
+        s_M = M;
     }
     __syncthreads();
     const float M = s_M;
-    const float sl = s_L;
-    // pass 3: O
-    float so[DV];
+    float lsum = 0.0f;
 #pragma unroll
-    for (int dv = 0; dv < DV; ++dv) so[dv] = 0.0f;
-#pragma unroll 4
-    for (int c = part; c < nch; c += kCombineSplit) {
-        const float* po = a.part_o + (base + (size_t)c * H) * DH + d;
-#pragma unroll
-        for (int dv = 0; dv < DV; ++dv) so[dv] += s_f[c] * po[dv * D];
+    for (int k = 0; k < kCombineMlPerThread; ++k) {
+        const int c = tid + k * kCombineThreads;
+        const float f = ml[k].x == -INFINITY ? 0.0f : exp2f(ml[k].x - M);
+        if (c < nch) s_f[c] = f;
+        lsum += f * ml[k].y;
     }
 #pragma unroll
-    for (int dv = 0; dv < DV; ++dv) s_red[part * DH + dv * D + d] = so[dv];
-    __syncthreads();
-    if (part != 0) return;
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane == 0) s_rl[wid] = lsum;
+    __syncthreads();                                  // s_f and s_rl complete
+    if (tid == 0) {
+        float L = 0.0f;
+        for (int w = 0; w < kWarpsC; ++w) L += s_rl[w];
+        s_L = L;
+    }
+    // O: the batch in registers, then any further batches
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-    for (int dv = 0; dv < DV; ++dv) {
-        float sum = 0.0f;
+    for (int k = 0; k < kCombineBatch; ++k) {
+        const int c = cl + k * lanes;
+        const float f = c < nch ? s_f[c] : 0.0f;
+        acc.x += f * v[k].x;
+        acc.y += f * v[k].y;
+        acc.z += f * v[k].z;
+        acc.w += f * v[k].w;
+    }
+    for (int c0 = cl + kCombineBatch * lanes; c0 < nch; c0 += kCombineBatch * lanes) {
 #pragma unroll
-        for (int q = 0; q < kCombineSplit; ++q) sum += s_red[q * DH + dv * D + d];
-        const size_t oi = ((size_t)seq * H + h) * DH + dv * D + d;
-        if (a.mode == kOut) {
-            a.out[oi] = nch ? __fdiv_rn(sum, sl) : 0.0f;
-        } else {
-            a.out[oi] = sum;
-            if (d == 0 && dv == 0) {
-                a.out_ml[((size_t)seq * H + h) * 2] = nch ? M : -INFINITY;
-                a.out_ml[((size_t)seq * H + h) * 2 + 1] = sl;
-            }
+        for (int k = 0; k < kCombineBatch; ++k) {
+            const int c = c0 + k * lanes;
+            v[k] = c < nch ? po[(size_t)c * cstride] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int k = 0; k < kCombineBatch; ++k) {
+            const int c = c0 + k * lanes;
+            const float f = c < nch ? s_f[c] : 0.0f;
+            acc.x += f * v[k].x;
+            acc.y += f * v[k].y;
+            acc.z += f * v[k].z;
+            acc.w += f * v[k].w;
+        }
+    }
+    reinterpret_cast<float4*>(s_acc)[cl * groups + gi] = acc;
+    __syncthreads();                                  // s_acc and s_L complete
+    if (tid >= dims) return;
+    float sum = 0.0f;
+    for (int q = 0; q < lanes; ++q) sum += s_acc[q * dims + tid];   // lanes in order
+    const float sl = s_L;
+    const size_t oi = ((size_t)seq * H + h) * DH + z * dims + tid;
+    if (a.mode == kOut) {
+        a.out[oi] = nch ? __fdiv_rn(sum, sl) : 0.0f;
+    } else {
+        a.out[oi] = sum;
+        if (z == 0 && tid == 0) {
+            a.out_ml[((size_t)seq * H + h) * 2] = nch ? M : -INFINITY;
+            a.out_ml[((size_t)seq * H + h) * 2 + 1] = sl;
         }
     }
 }
+
+// Dims split of the merge: gridDim.z CTAs per (sequence, head), more when
+// the batch has few pairs (one long sequence: 16 pairs on 148 SMs).
+int combine_splits(int pairs) { return pairs <= 64 ? 8 : pairs <= 128 ? 4 : pairs <= 256 ? 2 : 1; }
 
 // Merges num_parts partial states stacked [part][seq][head] (context shards);
 // one thread per dim of each 128-dim block of the head.
@@ -1242,15 +1255,15 @@ DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t tota
     DecodePlan best{T, 1, 0};
     if (max_seq_len <= 0 || num_seqs <= 0) return best;
     const int tiles = (max_seq_len + T - 1) / T;
-    // Stream-K for large batches of about equal lengths: one wave, every CTA
-    // of a head block streams an equal share of the batch's tiles, so no
-    // partial last wave (config 3: 1,152 chunks were 3.9 waves) and no CTA
-    // prologue per chunk.  Measured on B200 against the chunked grid: +1%
-    // on 128 x 32k, but behind on one sequence (the table pass and the
-    // prefix read add to a 15 us step) and on ragged batches of 64, whose
-    // step is set by its fixed costs; those keep the chunked plan.
-    const bool ragged_batch = total_tokens > 0 && total_tokens * 10 < (uint64_t)num_seqs * max_seq_len * 9;
-    if (allow_stream && num_seqs >= kStreamMinSeqs && num_seqs <= kStreamMaxSeqs && !ragged_batch) {
+    // Stream-K for batches of 32 to 1024 sequences: one wave, every CTA of a
+    // head block streams an equal share of the batch's tiles, so no partial
+    // last wave (config 3: 1,152 chunks were 3.9 waves), no CTA prologue per
+    // chunk, and ragged lengths balance by construction.  Measured on B200
+    // against the chunked grid: +1% on 128 x 32k and +2.5% on 64 ragged
+    // sequences of 512-8192 tokens, but behind on one sequence (the table
+    // pass and the prefix read add to a 15 us step), which keeps the chunked
+    // plan.
+    if (allow_stream && num_seqs >= kStreamMinSeqs && num_seqs <= kStreamMaxSeqs) {
         // (the merge takes up to kMaxChunks pieces of a sequence, one per CTA)
         const uint64_t tokens = total_tokens > 0 ? total_tokens : (uint64_t)num_seqs * max_seq_len;
         const uint64_t tt = (tokens + T - 1) / T;
@@ -1321,7 +1334,8 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
     EC_DECODE_VARIANTS(EC_DEC)
 #undef EC_DEC
     if (e != cudaSuccess || a.mode == kChunks || (plan.max_chunks <= 1 && a.sk_ctas == 0)) return e;
-    const dim3 cg(a.num_seqs, a.num_heads), cb(kCombineThreads);
+    const dim3 cg(a.num_seqs, a.num_heads, combine_splits(a.num_seqs * a.num_heads)),
+        cb(kCombineThreads);
     return v.dv == 1 ? launch_pdl(combine_kernel<1>, cg, cb, 0, st, a)
                      : launch_pdl(combine_kernel<2>, cg, cb, 0, st, a);
 }

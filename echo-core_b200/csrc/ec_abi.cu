@@ -536,7 +536,7 @@ struct ec_cp_comm {
     int world, rank, num_seqs, num_heads, device;
     float* local;                        // this rank's receive buffer
     float* peers[ec::kCpMaxWorld];       // opened IPC mappings (own slot = local)
-    uint32_t* epoch_dev;                 // device epochs per (sequence, head) (calls with epoch 0)
+    uint32_t* epoch_dev;                 // device epochs per (sequence, head, split) (calls with epoch 0)
     int epoch_mode;                      // 0 none yet, 1 caller epochs, 2 device epochs
     bool opened;
 };
@@ -563,7 +563,7 @@ int ec_cp_comm_create(uint32_t world, uint32_t rank, uint32_t num_seqs, uint32_t
     const size_t bytes = ec::cp_exchange_buffer_bytes(c->world, c->num_seqs, c->num_heads);
     cudaError_t e = cudaMalloc(&c->local, bytes);
     if (e == cudaSuccess) e = cudaMemset(c->local, 0, bytes);   // flags start below epoch 1
-    const size_t ebytes = (size_t)num_seqs * num_heads * sizeof(uint32_t);
+    const size_t ebytes = (size_t)num_seqs * num_heads * ec::kCpSplitMax * sizeof(uint32_t);
     if (e == cudaSuccess) e = cudaMalloc(&c->epoch_dev, ebytes);
     if (e == cudaSuccess) e = cudaMemset(c->epoch_dev, 0, ebytes);
     cudaIpcMemHandle_t h;

@@ -205,6 +205,7 @@ cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int nu
 
 // Context-parallel exchange + merge over peer memory (cp_exchange.cu).
 constexpr int kCpMaxWorld = 8;
+constexpr int kCpSplitMax = 8;       // dims splits of a (sequence, head) in the exchange kernel
 struct CpExchangeArgs {
     float* peer_base[kCpMaxWorld];   // every rank's receive buffer, this rank's own included
     const float* part_o;             // this rank's partial O [num_seqs][num_heads][128]
@@ -213,7 +214,7 @@ struct CpExchangeArgs {
     int32_t* err;
     int world, rank, num_seqs, num_heads;
     uint32_t epoch;
-    uint32_t* epoch_dev;             // non-null: [num_seqs][num_heads] epochs kept on the device
+    uint32_t* epoch_dev;             // non-null: [num_seqs][num_heads][kCpSplitMax] device epochs
     // max_chunks > 0: part_o / part_ml are the decode kernel's split-K chunk
     // partials of this rank's slice ([num_seqs*max_chunks][num_heads][..]),
     // merged in the exchange kernel; sequence s has ceil(seq_len[s] /
