@@ -8,8 +8,9 @@
 // head), or one split of its dims: it stores its rank's partial into slot
 // [rank] of every rank's receive buffer with plain peer stores (CUDA IPC
 // mappings, no multicast), publishes a per-(sequence, head, split) flag with
-// release semantics, waits with
-// acquire loads until every rank's flag for this step has arrived in its own
+// release semantics (a system-scope fence, then relaxed stores), waits with
+// relaxed loads and then a fence until every rank's flag for this step has
+// arrived in its own
 // buffer, and merges the world's partials in rank order.  Receive buffers are
 // double-buffered by step parity: a fast rank publishing step e+1 never
 // overwrites what a slow rank is still merging for step e.  Every wait is
@@ -30,14 +31,15 @@ namespace {
 
 constexpr int D = 128;
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
     uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 constexpr int kXThreads = 256;                    // threads of the chunked form
 constexpr int kMaxChunkMerge = 1024;               // chunks per (sequence, head), at most
@@ -212,14 +214,16 @@ __global__ void __launch_bounds__(CHUNKS ? kXThreads : D) cp_exchange_kernel(CpE
             if (t < 2) ml_at(base, par, a.rank)[t] = ml;
         }
     }
-    // the CTA's stores, then thread 0's system-scope release stores of the
-    // flags: the barrier orders the other threads' stores before the release,
-    // which is cumulative, so a rank that acquires the flag sees them all.  (A
-    // fence.sc.sys before the flags measured 7 us a step on one rank; the
-    // release alone is what the protocol needs.)
+    // the CTA's stores, then thread 0's release pattern: one system-scope
+    // acq_rel fence (cumulative: the barrier orders the other threads' stores
+    // before it) and relaxed flag stores, so a rank that sees a flag and then
+    // fences sees the partial.  (A fence.sc.sys here measured 7 us a step on
+    // one rank; a release store per flag 3 us more than one fence at two.)
     __syncthreads();
-    if (t == 0)
-        for (int r = 0; r < W; ++r) st_release_sys(flag_at(a.peer_base[r], par, a.rank), epoch);
+    if (t == 0) {
+        fence_acq_rel_sys();
+        for (int r = 0; r < W; ++r) st_relaxed_sys(flag_at(a.peer_base[r], par, a.rank), epoch);
+    }
 
     // ---- wait for every rank's flag of this step in the local buffer
     __shared__ int s_bad;
@@ -228,13 +232,14 @@ __global__ void __launch_bounds__(CHUNKS ? kXThreads : D) cp_exchange_kernel(CpE
         float* mine = a.peer_base[a.rank];
         for (int r = 0; r < W && !bad; ++r) {
             const uint32_t* f = flag_at(mine, par, r);
-            if (ld_acquire_sys(f) == epoch) continue;
+            if (ld_relaxed_sys(f) == epoch) continue;
             const long long t0 = clock64();
-            while (ld_acquire_sys(f) != epoch) {
+            while (ld_relaxed_sys(f) != epoch) {
                 if (clock64() - t0 > kWaitBudgetCycles) { bad = 1; break; }
                 __nanosleep(64);
             }
         }
+        fence_acq_rel_sys();                         // acquire side of the flags seen
         if (bad) flag_error(a.err, EC_DEVERR_TIMEOUT);
         s_bad = bad;
     }
