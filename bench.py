@@ -468,7 +468,10 @@ def run_gpu_arm(args, rank, world, local_rank):
                    "l2": "inputs larger than L2 (KV working set per step >> 126 MB)"},
         "tok_s": round(nseq_total * args.steps / (ms_max * 1e-3), 1),
         "pct_of_hbm_peak": round(100 * gbs / (peak * world), 1),
-        "roofline": {"bound": "hbm", "kernel": "decode_kernel+combine_kernel",
+        # (the library's plan: stream-K for 32 to 1024 sequences a rank, else the chunked grid)
+        "roofline": {"bound": "hbm",
+                     "kernel": ("decode_sk_kernel" if 32 <= nseq <= 1024
+                                else "decode_kernel") + "+combine_kernel",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "alg_bytes_per_launch": alg_bytes,
