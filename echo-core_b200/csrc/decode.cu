@@ -964,12 +964,15 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
 // dependent global round trips (table entry, then partials) instead of a
 // chain.  Reductions run in a fixed order: the result does not depend on
 // timing.
-constexpr int kCombineThreads = 256;
+// NT threads at up to 64 registers: 256, or 128 for many (sequence, head)
+// pairs of one 128-dim block each (eight CTAs an SM, so up to 1,184 pairs run in
+// one wave); a CTA's thread count must cover its dims.
 constexpr int kCombineBatch = 8;                  // O loads in flight a thread
-constexpr int kCombineMlPerThread = kMaxChunks / kCombineThreads;
-static_assert(kMaxChunks % kCombineThreads == 0, "(m, l) loads cover every chunk");
-template <int DV>
-__global__ void __launch_bounds__(kCombineThreads, 4) combine_kernel(const DecodeArgs a) {
+template <int DV, int NT>
+__global__ void __launch_bounds__(NT, 1024 / NT) combine_kernel(const DecodeArgs a) {
+    constexpr int kCombineThreads = NT;
+    constexpr int kCombineMlPerThread = kMaxChunks / NT;
+    static_assert(kMaxChunks % NT == 0, "(m, l) loads cover every chunk");
     constexpr int DH = D * DV;
     constexpr int kWarpsC = kCombineThreads / 32;
     const int seq = blockIdx.x, h = blockIdx.y;
@@ -1334,10 +1337,11 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
     EC_DECODE_VARIANTS(EC_DEC)
 #undef EC_DEC
     if (e != cudaSuccess || a.mode == kChunks || (plan.max_chunks <= 1 && a.sk_ctas == 0)) return e;
-    const dim3 cg(a.num_seqs, a.num_heads, combine_splits(a.num_seqs * a.num_heads)),
-        cb(kCombineThreads);
-    return v.dv == 1 ? launch_pdl(combine_kernel<1>, cg, cb, 0, st, a)
-                     : launch_pdl(combine_kernel<2>, cg, cb, 0, st, a);
+    const int z = combine_splits(a.num_seqs * a.num_heads);
+    const dim3 cg(a.num_seqs, a.num_heads, z);
+    if (v.dv == 2) return launch_pdl(combine_kernel<2, 256>, cg, dim3(256), 0, st, a);
+    return z == 1 ? launch_pdl(combine_kernel<1, 128>, cg, dim3(128), 0, st, a)
+                  : launch_pdl(combine_kernel<1, 256>, cg, dim3(256), 0, st, a);
 }
 
 cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int num_parts,
