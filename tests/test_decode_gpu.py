@@ -252,6 +252,51 @@ def test_context_parallel_partials_and_lse_combine(cuda, parts):
     assert_attn_close(out.cpu().numpy()[0], want, f"cp{parts}")
 
 
+@pytest.mark.parametrize("nseq,H,hkv,dh", [
+    (2, 16, 4, 128),     # 32 (sequence, head) pairs: the merge splits each pair's dims over 8 CTAs
+    (6, 16, 4, 128),     # 96 pairs: 4 CTAs a pair
+    (12, 16, 4, 128),    # 192 pairs: 2 CTAs a pair
+    (24, 16, 4, 128),    # 384 pairs: one 128-thread CTA a pair
+    (2, 8, 2, 256),      # head_dim 256, 16 pairs: 8 CTAs a pair of 32 dims each
+    (20, 16, 4, 256),    # head_dim 256, 320 pairs: one 256-thread CTA a pair
+    (40, 16, 4, 128),    # 40 sequences: the stream-K plan, its pieces merged by 128-thread CTAs
+    (40, 16, 4, 256),    # stream-K at head_dim 256
+])
+def test_split_k_merge_layouts(cuda, nseq, H, hkv, dh):
+    """Every CTA layout of the split-K merge (dims split 8/4/2/1 ways by the
+    batch's pair count, 128 or 256 threads) over chunked plans of several
+    chunks a sequence and over stream-K pieces: normalised output and the
+    partial (m, l, O) form, against the oracle."""
+    import torch
+    import eckv
+    rng = np.random.default_rng(1000 + nseq * 10 + dh)
+    lens = [int(x) for x in rng.integers(2000, 9000, nseq)]
+    seqs = []
+    for L in lens:
+        kq, ks = O.quantize_kv(W.kv_rows(rng, L, hkv, dh), hkv, dh)
+        vq, vs = O.quantize_kv(W.kv_rows(rng, L, hkv, dh), hkv, dh)
+        seqs.append((kq, vq, ks, vs))
+    q = W.queries(rng, nseq, H, dh)
+    bc = eckv.BatchCache(lens, num_kv_heads=hkv, head_dim=dh)
+    fill_batch(bc, seqs)
+    assert bc.workspace(H)[1] > 0, "a split plan"
+    sc = W.softmax_scale(dh)
+    qd = _dev(torch, q)
+    out = torch.empty((nseq, H, dh), device="cuda")
+    bc.decode(qd, out, H, sc)
+    po = torch.empty((nseq, H, dh), device="cuda")
+    pml = torch.empty((nseq, H, 2), device="cuda")
+    bc.decode_partial(qd, po, pml, H, sc)
+    torch.cuda.synchronize()
+    assert bc.device_error() == 0
+    got = out.cpu().numpy()
+    part = po.cpu().numpy() / pml.cpu().numpy()[..., 1:2]
+    for s in range(nseq):
+        want = O.decode_attention(*seqs[s], lens[s], q[s], H, hkv, dh, sc)
+        assert_attn_close(got[s], want, f"seq {s}")
+        assert_attn_close(part[s], want, f"partial seq {s}")
+
+
 def test_bad_length_table_is_flagged_not_read(cuda):
     import torch
     import eckv
