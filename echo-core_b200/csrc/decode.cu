@@ -45,6 +45,12 @@
 namespace ec {
 namespace {
 
+// Prefetch a __grid_constant__ tensor map (kernel parameter space) into the
+// tensor-map cache ahead of the first TMA that uses it.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* m) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
 constexpr int D = 128;                             // dims per 128-byte box (one block)
 constexpr int T = 32;                              // tokens per tile
 constexpr int kPBufs = 2;                          // p' tiles in flight per head
@@ -598,6 +604,14 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
     const int chunk = blockIdx.y;
     const int seq = blockIdx.z;
     const bool direct = a.max_chunks == 1 && a.mode != kChunks;
+    // shared-memory set-up and the tensor maps' prefetch overlap the kernel
+    // before this one: neither reads memory that kernel writes
+    if (threadIdx.x == 0) {
+        init_barriers<HC, QW, SCW, DV>(full, empty, p_full, p_empty);
+        fail_flag = 0;
+        prefetch_tensormap(&tmap_k);
+        prefetch_tensormap(&tmap_v);
+    }
     pdl_wait();  // the append before this kernel writes the lengths and the codes
     pdl_trigger();
     int32_t off, cap, len;
@@ -616,12 +630,7 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
     const int lane = threadIdx.x & 31;
     constexpr int hkv = SCW;   // the cache's num_kv_heads: variants are chosen by it
     const int group = a.num_heads / hkv;
-
-    if (threadIdx.x == 0) {
-        init_barriers<HC, QW, SCW, DV>(full, empty, p_full, p_empty);
-        fail_flag = 0;
-    }
-    __syncthreads();
+    __syncthreads();   // the barrier inits
 
     if (warp == G::kWarps) {
         // ============================================================ producer
@@ -853,9 +862,13 @@ __global__ void __launch_bounds__(Geo<HC, QW, SCW, DV>::kThreads, Geo<HC, QW, SC
     constexpr int hkv = SCW;   // the cache's num_kv_heads: variants are chosen by it
     const int group = a.num_heads / hkv;
     const int H = a.num_heads;
+    if (threadIdx.x == 0) {   // before the wait: reads nothing the previous kernel writes
+        init_barriers<HC, QW, SCW, DV>(full, empty, p_full, p_empty);
+        prefetch_tensormap(&tmap_k);
+        prefetch_tensormap(&tmap_v);
+    }
     pdl_wait();  // the append before this kernel writes the lengths and the codes
     pdl_trigger();
-    if (threadIdx.x == 0) init_barriers<HC, QW, SCW, DV>(full, empty, p_full, p_empty);
     if (cta == 0 && blockIdx.x == 0) {
         for (int s = threadIdx.x; s < a.num_seqs; s += blockDim.x) {
             int32_t off, cap, len;
