@@ -46,9 +46,6 @@ constexpr int kMaxChunkMerge = 1024;               // chunks per (sequence, head
 constexpr int kXBatch = 8;                         // O loads in flight a thread
 constexpr int kXMlPerThread = kMaxChunkMerge / kXThreads;
 
-// Dims split of the chunked form: gridDim.z CTAs per (sequence, head), more
-// when the batch has few pairs (one long sequence: 16 pairs on 148 SMs).
-int exchange_splits(int pairs) { return pairs <= 64 ? 8 : pairs <= 128 ? 4 : pairs <= 256 ? 2 : 1; }
 
 // This rank's partial of (s, h) merged from its split-K chunks, for the
 // CTA's dims [z * dims, (z + 1) * dims): o (dim z * dims + t, for threads
@@ -275,7 +272,7 @@ cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st) {
     if (a.num_seqs <= 0 || a.num_heads <= 0) return cudaSuccess;
     if (a.max_chunks > 0) {
         if (a.max_chunks > kMaxChunkMerge || a.chunk_tokens <= 0) return cudaErrorInvalidValue;
-        const int z = exchange_splits(a.num_seqs * a.num_heads);
+        const int z = merge_splits(a.num_seqs * a.num_heads);
         return launch_pdl(cp_exchange_kernel<true>, dim3(a.num_seqs, a.num_heads, z),
                           dim3(kXThreads), 0, st, a);
     }

@@ -1119,9 +1119,6 @@ __global__ void __launch_bounds__(NT, 1024 / NT) combine_kernel(const DecodeArgs
     }
 }
 
-// Dims split of the merge: gridDim.z CTAs per (sequence, head), more when
-// the batch has few pairs (one long sequence: 16 pairs on 148 SMs).
-int combine_splits(int pairs) { return pairs <= 64 ? 8 : pairs <= 128 ? 4 : pairs <= 256 ? 2 : 1; }
 
 // Merges num_parts partial states stacked [part][seq][head] (context shards);
 // one thread per dim of each 128-dim block of the head.
@@ -1262,6 +1259,8 @@ DecodeVariant decode_variant(int num_kv_heads, int group, int head_dim) {
     return none;
 }
 
+int merge_splits(int pairs) { return pairs <= 64 ? 8 : pairs <= 128 ? 4 : pairs <= 256 ? 2 : 1; }
+
 DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens,
                        int num_kv_heads, int num_heads, int head_dim, bool allow_stream) {
     const DecodeVariant v = num_kv_heads > 0
@@ -1350,7 +1349,7 @@ cudaError_t launch_decode(DecodeArgs a, int num_kv_heads, const DecodePlan& plan
     EC_DECODE_VARIANTS(EC_DEC)
 #undef EC_DEC
     if (e != cudaSuccess || a.mode == kChunks || (plan.max_chunks <= 1 && a.sk_ctas == 0)) return e;
-    const int z = combine_splits(a.num_seqs * a.num_heads);
+    const int z = merge_splits(a.num_seqs * a.num_heads);
     const dim3 cg(a.num_seqs, a.num_heads, z);
     if (v.dv == 2) return launch_pdl(combine_kernel<2, 256>, cg, dim3(256), 0, st, a);
     return z == 1 ? launch_pdl(combine_kernel<1, 128>, cg, dim3(128), 0, st, a)

@@ -204,6 +204,11 @@ cudaError_t launch_lse_combine(const float* part_o, const float* part_ml, int nu
                                cudaStream_t st);
 
 // Context-parallel exchange + merge over peer memory (cp_exchange.cu).
+// CTAs per (sequence, head) of a split-K merge (the decode's merge kernel and
+// the context-parallel exchange), each taking a slice of the head's dims:
+// more when the batch has few pairs (one long sequence: 16 pairs on 148 SMs).
+int merge_splits(int pairs);
+
 constexpr int kCpMaxWorld = 8;
 constexpr int kCpSplitMax = 8;       // dims splits of a (sequence, head) in the exchange kernel
 struct CpExchangeArgs {
