@@ -6,16 +6,16 @@
 // (sequence, head) (ec_decode_attention_partial).  Instead of an all-gather
 // followed by a merge launch, every CTA of this kernel owns one (sequence,
 // head), or one split of its dims: it stores its rank's partial into slot
-// [rank] of every rank's receive buffer with plain peer stores (CUDA IPC
-// mappings, no multicast), publishes a per-(sequence, head, split) flag with
-// release semantics (a system-scope fence, then relaxed stores), waits with
-// relaxed loads and then a fence until every rank's flag for this step has
-// arrived in its own
-// buffer, and merges the world's partials in rank order.  Receive buffers are
-// double-buffered by step parity: a fast rank publishing step e+1 never
-// overwrites what a slow rank is still merging for step e.  Every wait is
-// bounded (about 1 s of clock64 cycles); a wait that runs out records
-// EC_DEVERR_TIMEOUT in the error word and the CTA writes zeros.
+// [rank] of every other rank's receive buffer with plain peer stores (CUDA
+// IPC mappings, no multicast), each value as a 64-bit word that carries the
+// step's epoch beside it, then waits, thread by thread, until the words of
+// every other rank in its own buffer show this step's epoch, and merges the
+// world's partials in rank order.  A word is its own flag, so the exchange
+// needs no fence and no separate flag store: one NVLink trip a step.  Receive
+// buffers are double-buffered by step parity: a fast rank publishing step e+1
+// never overwrites what a slow rank is still merging for step e.  Every wait
+// is bounded (about 1 s of clock64 cycles); a wait that runs out records
+// EC_DEVERR_TIMEOUT in the error word and the thread writes zero.
 //
 // The chunked form (CHUNKS) takes the decode kernel's split-K chunk partials
 // of this rank's slice straight from its workspace and merges them first, in
@@ -31,15 +31,14 @@ namespace {
 
 constexpr int D = 128;
 
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 constexpr int kXThreads = 256;                    // threads of the chunked form
 constexpr int kMaxChunkMerge = 1024;               // chunks per (sequence, head), at most
@@ -153,9 +152,9 @@ __device__ void merge_chunks(const CpExchangeArgs& a, int s, int h, int z, int d
 }
 
 // One CTA per (sequence, head, dims split z): gridDim.z = 1 for the plain
-// form (partials given), exchange_splits() for the chunked form.  Every
-// split has its own (m, l) slot, flag and device epoch, so the CTAs of a
-// (sequence, head) publish, wait and merge independently.
+// form (partials given), merge_splits() for the chunked form.  Every split
+// has its own (m, l) words and device epoch, so the CTAs of a (sequence,
+// head) publish, wait and merge independently.
 template <bool CHUNKS>
 __global__ void __launch_bounds__(CHUNKS ? kXThreads : D) cp_exchange_kernel(CpExchangeArgs a) {
     const int s = blockIdx.x, h = blockIdx.y, z = blockIdx.z, t = threadIdx.x;
@@ -181,82 +180,84 @@ __global__ void __launch_bounds__(CHUNKS ? kXThreads : D) cp_exchange_kernel(CpE
     __syncthreads();
     const uint32_t epoch = s_epoch;
     const int par = epoch & 1;
-    // per rank buffer: [2 parities][W ranks][S][H] of O (D floats), then
-    // [2][W][S][H][kCpSplitMax] of (m, l) and of flags
+    // per rank buffer of 64-bit words, each (epoch << 32 | value bits):
+    // [2 parities][W ranks][S][H] of O (D words), then [2][W][S][H][kCpSplitMax]
+    // of (m, l).  A word carries its own step, so a reader needs no flag and no
+    // fence: it waits until the word it reads shows this step's epoch (an
+    // aligned 64-bit relaxed store or load is single-copy atomic).
     const size_t n_sh = (size_t)S * H;
-    auto o_at = [&](float* base, int p, int r) { return base + ((size_t)(p * W + r) * n_sh + sh) * D; };
+    auto o_at = [&](float* base, int p, int r) {
+        return reinterpret_cast<uint64_t*>(base) + ((size_t)(p * W + r) * n_sh + sh) * D;
+    };
     auto ml_at = [&](float* base, int p, int r) {
-        return base + (size_t)2 * W * n_sh * D + (((size_t)(p * W + r) * n_sh + sh) * kCpSplitMax + z) * 2;
+        return reinterpret_cast<uint64_t*>(base) + (size_t)2 * W * n_sh * D +
+               (((size_t)(p * W + r) * n_sh + sh) * kCpSplitMax + z) * 2;
     };
-    auto flag_at = [&](float* base, int p, int r) {
-        return reinterpret_cast<uint32_t*>(base + (size_t)2 * W * n_sh * (D + 2 * kCpSplitMax)) +
-               ((size_t)(p * W + r) * n_sh + sh) * kCpSplitMax + z;
-    };
+    auto word = [&](float v) { return (uint64_t)epoch << 32 | __float_as_uint(v); };
 
     // ---- publish this rank's partial (this split's dims) into slot [rank]
-    // of every rank's buffer
-    float o, ml;
+    // of every other rank's buffer
+    float o, m_loc, l_loc;
     if (CHUNKS) {
-        float m_loc, l_loc;
         merge_chunks(a, s, h, z, dims, o, m_loc, l_loc);
-        ml = t == 0 ? m_loc : l_loc;
     } else {
         o = a.part_o[sh * D + t];
-        ml = t < 2 ? a.part_ml[sh * 2 + t] : 0.0f;
+        m_loc = a.part_ml[sh * 2];
+        l_loc = a.part_ml[sh * 2 + 1];
     }
     if (t < dims) {
         for (int r = 0; r < W; ++r) {
+            if (r == a.rank) continue;
             float* base = a.peer_base[r];
-            o_at(base, par, a.rank)[z * dims + t] = o;
-            if (t < 2) ml_at(base, par, a.rank)[t] = ml;
+            st_relaxed_sys_u64(o_at(base, par, a.rank) + z * dims + t, word(o));
+            if (t < 2) st_relaxed_sys_u64(ml_at(base, par, a.rank) + t, word(t == 0 ? m_loc : l_loc));
         }
     }
-    // the CTA's stores, then thread 0's release pattern: one system-scope
-    // acq_rel fence (cumulative: the barrier orders the other threads' stores
-    // before it) and relaxed flag stores, so a rank that sees a flag and then
-    // fences sees the partial.  (A fence.sc.sys here measured 7 us a step on
-    // one rank; a release store per flag 3 us more than one fence at two.)
-    __syncthreads();
-    if (t == 0) {
-        fence_acq_rel_sys();
-        for (int r = 0; r < W; ++r) st_relaxed_sys(flag_at(a.peer_base[r], par, a.rank), epoch);
-    }
+    if (t >= dims) return;
 
-    // ---- wait for every rank's flag of this step in the local buffer
-    __shared__ int s_bad;
-    if (t == 0) {
-        int bad = 0;
-        float* mine = a.peer_base[a.rank];
-        for (int r = 0; r < W && !bad; ++r) {
-            const uint32_t* f = flag_at(mine, par, r);
-            if (ld_relaxed_sys(f) == epoch) continue;
+    // ---- every other rank's words of this step, from the local buffer
+    float* mine = a.peer_base[a.rank];
+    bool bad = false;
+    auto wait_word = [&](const uint64_t* w, float& v) {
+        uint64_t x = ld_relaxed_sys_u64(w);
+        if ((uint32_t)(x >> 32) != epoch) {
             const long long t0 = clock64();
-            while (ld_relaxed_sys(f) != epoch) {
-                if (clock64() - t0 > kWaitBudgetCycles) { bad = 1; break; }
-                __nanosleep(64);
+            while ((uint32_t)((x = ld_relaxed_sys_u64(w)) >> 32) != epoch) {
+                if (clock64() - t0 > kWaitBudgetCycles) {
+                    bad = true;
+                    return;
+                }
+                __nanosleep(32);
             }
         }
-        fence_acq_rel_sys();                         // acquire side of the flags seen
-        if (bad) flag_error(a.err, EC_DEVERR_TIMEOUT);
-        s_bad = bad;
+        v = __uint_as_float((uint32_t)x);
+    };
+    float rm[kCpMaxWorld], rl[kCpMaxWorld], ro[kCpMaxWorld];
+    for (int r = 0; r < W && !bad; ++r) {
+        if (r == a.rank) {
+            rm[r] = m_loc;
+            rl[r] = l_loc;
+            ro[r] = o;
+            continue;
+        }
+        wait_word(ml_at(mine, par, r), rm[r]);
+        if (!bad) wait_word(ml_at(mine, par, r) + 1, rl[r]);
+        if (!bad) wait_word(o_at(mine, par, r) + z * dims + t, ro[r]);
     }
-    __syncthreads();
-    float* mine = a.peer_base[a.rank];
-    if (t >= dims) return;
     const size_t oi = sh * D + z * dims + t;
-    if (s_bad) {
+    if (bad) {
+        flag_error(a.err, EC_DEVERR_TIMEOUT);
         a.out[oi] = 0.0f;
         return;
     }
     // ---- merge in rank order (the LSE merge of ec_lse_combine)
     float M = -INFINITY;
-    for (int r = 0; r < W; ++r) M = fmaxf(M, ml_at(mine, par, r)[0]);
+    for (int r = 0; r < W; ++r) M = fmaxf(M, rm[r]);
     float so = 0.0f, sl = 0.0f;
     for (int r = 0; r < W; ++r) {
-        const float* mlr = ml_at(mine, par, r);
-        const float f = mlr[0] == -INFINITY ? 0.0f : exp2f(mlr[0] - M);
-        so += f * o_at(mine, par, r)[z * dims + t];
-        sl += f * mlr[1];
+        const float f = rm[r] == -INFINITY ? 0.0f : exp2f(rm[r] - M);
+        so += f * ro[r];
+        sl += f * rl[r];
     }
     a.out[oi] = sl > 0.0f ? __fdiv_rn(so, sl) : 0.0f;
 }
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(CHUNKS ? kXThreads : D) cp_exchange_kernel(CpE
 
 size_t cp_exchange_buffer_bytes(int world, int num_seqs, int num_heads) {
     const size_t n = (size_t)2 * world * num_seqs * num_heads;
-    return n * (D + 2 * kCpSplitMax) * sizeof(float) + n * kCpSplitMax * sizeof(uint32_t);
+    return n * (D + 2 * kCpSplitMax) * sizeof(uint64_t);
 }
 
 cudaError_t launch_cp_exchange(const CpExchangeArgs& a, cudaStream_t st) {
