@@ -330,7 +330,8 @@ EC_API int ec_lse_combine(const float* part_o, const float* part_ml, uint32_t nu
  * a CUDA graph and replayed; a comm uses caller epochs or device epochs, not
  * both
  * (EC_ERR_INVALID_ARGUMENT on a switch).
- * world <= 8; num_seqs * num_heads <= 2368 (one CTA each, all resident). */
+ * world <= 8; num_seqs * num_heads <= 2368.  A CTA waits only for the words
+ * of the same CTA (sequence, head, dims split) on the other ranks. */
 #define EC_CP_HANDLE_BYTES 64
 typedef struct ec_cp_comm ec_cp_comm;
 EC_API int ec_cp_comm_create(uint32_t world, uint32_t rank, uint32_t num_seqs,
