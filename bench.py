@@ -700,6 +700,11 @@ def run_cp_arm(args, rank, world, local_rank):
     # replayed with device epochs; unfused 0.1157 against 0.1191 ms)
     use_graph = args.graph and world == 1
     cx = ranks.CPExchange(1, H) if peer else None
+    # this library's kernels a step: decode (+ its split-K merge when the plan
+    # splits), or decode + exchange (fused), or decode (+ merge) + exchange /
+    # + ec_lse_combine (the NCCL all-gather between is NCCL's)
+    split = 1 if bc.workspace(H)[1] > 0 else 0
+    own_launches = 1 + split if world == 1 else 2 if fused else 2 + split
 
     def step():
         if world == 1:
@@ -761,6 +766,7 @@ def run_cp_arm(args, rank, world, local_rank):
                                     if peer else "NCCL all-gather + ec_lse_combine"
                                     if world > 1 else "none"),
                        "launch": "CUDA graph replay" if use_graph else "eager"},
+            "gpu_launches": own_launches * args.steps,
             "pct_of_hbm_peak": round(100 * gbs / (peak * world), 1)}), flush=True)
     if cx is not None:
         cx.close()
