@@ -36,6 +36,7 @@
 // denominator always share the same reference maximum).
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 
 #include <cuda.h>
 
@@ -1261,8 +1262,47 @@ DecodeVariant decode_variant(int num_kv_heads, int group, int head_dim) {
 
 int merge_splits(int pairs) { return pairs <= 64 ? 8 : pairs <= 128 ? 4 : pairs <= 256 ? 2 : 1; }
 
+static DecodePlan plan_decode_uncached(int num_seqs, int max_seq_len, int num_sms,
+                                       uint64_t total_tokens, int num_kv_heads, int num_heads,
+                                       int head_dim, bool allow_stream);
+
+// The plan is a pure function of its arguments, and a serving loop asks for
+// the same one every step (the workspace query, then the launch): the last
+// few are kept, since the chunked plan's cost model scans up to 1024 chunk
+// counts (about 10 us of host time for one long sequence).
 DecodePlan plan_decode(int num_seqs, int max_seq_len, int num_sms, uint64_t total_tokens,
                        int num_kv_heads, int num_heads, int head_dim, bool allow_stream) {
+    struct Entry {
+        int num_seqs, max_seq_len, num_sms, num_kv_heads, num_heads, head_dim;
+        uint64_t total_tokens;
+        bool allow_stream, used;
+        DecodePlan plan;
+    };
+    constexpr int kEntries = 16;
+    static std::mutex mu;
+    static Entry memo[kEntries] = {};
+    static int next = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const Entry& e : memo)
+            if (e.used && e.num_seqs == num_seqs && e.max_seq_len == max_seq_len &&
+                e.num_sms == num_sms && e.total_tokens == total_tokens &&
+                e.num_kv_heads == num_kv_heads && e.num_heads == num_heads &&
+                e.head_dim == head_dim && e.allow_stream == allow_stream)
+                return e.plan;
+    }
+    const DecodePlan p = plan_decode_uncached(num_seqs, max_seq_len, num_sms, total_tokens,
+                                              num_kv_heads, num_heads, head_dim, allow_stream);
+    std::lock_guard<std::mutex> lock(mu);
+    memo[next] = Entry{num_seqs, max_seq_len, num_sms, num_kv_heads, num_heads, head_dim,
+                       total_tokens, allow_stream, true, p};
+    next = (next + 1) % kEntries;
+    return p;
+}
+
+static DecodePlan plan_decode_uncached(int num_seqs, int max_seq_len, int num_sms,
+                                       uint64_t total_tokens, int num_kv_heads, int num_heads,
+                                       int head_dim, bool allow_stream) {
     const DecodeVariant v = num_kv_heads > 0
         ? decode_variant(num_kv_heads, num_heads / num_kv_heads, head_dim) : DecodeVariant{};
     const int slots = num_sms * (v.hc ? v.ctas_per_sm : 2);   // resident CTAs
